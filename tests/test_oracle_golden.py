@@ -1,0 +1,152 @@
+"""Pin the CPU oracle against golden vectors from the reference's own kernels.
+
+The fixtures under ``tests/golden`` were produced by
+``tests/golden/make_golden.py`` (reference Triton kernels under the Triton
+CPU interpreter).  Integer/byte outputs must match bit-exactly; floating
+point outputs within the stated tolerances.
+"""
+
+import numpy as np
+import pytest
+
+from golden_io import load
+from oracle import cache as C
+from oracle import metadata as M
+from oracle import output as O
+from oracle.fp8 import bf16_round, e4m3_to_f32
+
+D, R = 512, 64
+
+
+def test_kv_insert_bytes_match_reference():
+    g = load("kv_insert_gather")
+    page = int(g["page"])
+    cache = np.zeros_like(g["cache"])
+    C.insert_rows(cache, g["slots"], g["k"], page, D, R)
+    assert np.array_equal(cache, g["cache"])
+
+
+def test_dequant_gather_matches_reference():
+    g = load("kv_insert_gather")
+    page = int(g["page"])
+    out = np.zeros_like(g["gathered"])
+    C.dequantize_and_gather(g["cache"], g["seq_lens"], g["gather_lens"], g["block_table"], page, 5,
+                            out, D, R)
+    assert np.array_equal(bf16_round(out), g["gathered"])
+
+
+def test_save_partial_states_matches_reference():
+    g = load("compressor")
+    state = g["state_before"].copy()
+    C.save_partial_states(state, g["kv"], g["score"], g["ape"], g["positions"], g["state_slot"], 8, 128)
+    flat = state.reshape(-1, 2 * D)
+    slots = g["state_slot"]
+    ok = slots >= 0
+    assert np.array_equal(flat[slots[ok]], g["state_rows_written"][ok])
+
+
+def test_compressor_matches_reference():
+    """Compressed rows: RoPE bf16 within 1 ulp, NoPE scale bytes equal and
+    fp8 codes within one step (fp32 softmax/rsqrt ordering may differ)."""
+    g = load("compressor")
+    state = g["state_before"].copy()
+    C.save_partial_states(state, g["kv"], g["score"], g["ape"], g["positions"], g["state_slot"], 8, 128)
+    cache = np.zeros_like(g["kv_cache"])
+    C.compress_norm_rope_store(state, g["token_to_req"], g["positions"], g["state_slot"],
+                               g["state_block_table"], 8, g["norm_weight"], 1e-6, g["cos_sin"],
+                               cache, g["comp_slot"], 2, D, R, 128)
+    slots = g["comp_slot"][g["comp_slot"] >= 0]
+    assert len(slots) == 3
+    ours = C.read_rows(cache, slots, 2, D, R)
+    ref = C.read_rows(g["kv_cache"], slots, 2, D, R)
+    np.testing.assert_allclose(ours, ref, rtol=2 ** -3, atol=1e-6)
+    rel = np.linalg.norm(ours - ref) / np.linalg.norm(ref)
+    assert rel < 2e-3
+    # scale bytes
+    for s in slots:
+        page, off = divmod(int(s), 2)
+        sb = 2 * 576 + off * 8
+        assert np.array_equal(cache[page, sb:sb + 8], g["kv_cache"][page, sb:sb + 8])
+
+
+def test_metadata_builders_bit_exact():
+    g = load("metadata")
+    qsl, seq_lens = g["query_start_loc"], g["seq_lens"]
+    T = int(qsl[-1])
+    nd, ndt = int(g["num_decodes"]), int(g["num_decode_tokens"])
+    t2r = M.token_to_req_indices(qsl)
+    assert np.array_equal(t2r, g["token_to_req"])
+    cs = M.compressed_slot_mapping(T, qsl, seq_lens, g["comp_block_table"], 2, 128)
+    assert np.array_equal(cs, g["comp_slot"][:T])
+
+    idx = np.full((T, 128), 777, np.int32)
+    lens = np.full(T, 99, np.int32)
+    M.swa_indices_and_lens(ndt, 128, qsl, seq_lens, t2r, g["slot_mapping"] >= 0,
+                           g["swa_block_table"], 64, idx, lens)
+    assert np.array_equal(lens, g["swa_lens"])
+    assert np.array_equal(idx, g["swa_indices"])
+
+    maxc = int(g["max_compressed"])
+    gd = np.full((T, maxc), 555, np.int32)
+    dl = np.full(T, 555, np.int32)
+    pl = np.full((T, maxc), 555, np.int32)
+    M.c128a_topk_metadata(g["positions"], 128, ndt, t2r, g["comp_block_table"][:nd], 2,
+                          g["slot_mapping"], gd, dl, pl, maxc)
+    assert np.array_equal(gd[:ndt], g["c128a_global"][:ndt])
+    assert np.array_equal(dl[:ndt], g["c128a_lens"][:ndt])
+    assert np.array_equal(pl[: T - ndt], g["c128a_prefill"][: T - ndt])
+
+    gl = M.prefill_gather_lens(seq_lens, qsl, 2, nd, 128)
+    assert np.array_equal(gl, g["gather_lens"])
+    comb, clens = M.combine_topk_swa_indices(g["c128a_prefill"][: T - ndt], qsl[nd:], seq_lens[nd:],
+                                             gl, 128, 128, maxc, int(g["M"]), int(g["N"]))
+    assert np.array_equal(comb, g["combined"])
+    assert np.array_equal(clens, g["combined_lens"])
+
+
+def test_qk_rmsnorm_matches_reference():
+    g = load("qk_rmsnorm")
+    q = bf16_round(O.rms_norm(g["qr"], g["q_weight"], 1e-6))
+    k = bf16_round(O.rms_norm(g["kv"], g["kv_weight"], 1e-6))
+    # one bf16 ulp (rsqrt rounding)
+    np.testing.assert_allclose(q, g["q_out"], rtol=2 ** -7, atol=0)
+    np.testing.assert_allclose(k, g["kv_out"], rtol=2 ** -7, atol=0)
+    assert (q == g["q_out"]).mean() > 0.98
+
+
+def _dequant_groups(fp8, exp_bytes):
+    return e4m3_to_f32(fp8) * np.ldexp(1.0, exp_bytes.astype(np.int32) - 127)
+
+
+def test_inv_rope_fp8_quant_matches_reference():
+    g = load("inv_rope_fp8_quant")
+    G = int(g["n_groups"])
+    q, exp = O.inv_rope_fp8_quant(g["o"], g["positions"], g["cos_sin"], G, R)
+    T, H = g["o"].shape[:2]
+    hpg = H // G
+    # reference scale: [G, aligned_T, packs] int32, byte c of pack k = chunk 4k + c
+    ref_bytes = g["scale"].view(np.uint8).reshape(G, -1, g["scale"].shape[-1] * 4)[:, :T]
+    ours_bytes = (exp + 127).astype(np.uint8).reshape(T, G, hpg * (D // 128)).transpose(1, 0, 2)
+    assert np.array_equal(ours_bytes, ref_bytes[..., : hpg * (D // 128)])
+    assert (q == g["fp8"]).mean() > 0.999
+    assert np.abs(e4m3_to_f32(q).astype(np.float64) - e4m3_to_f32(g["fp8"])).max() <= 32
+
+
+def test_vha_inv_rope_fp8_quant_matches_plugin_kernel():
+    g = load("vha_inv_rope_fp8_quant")
+    G = int(g["n_groups"])
+    q, exp = O.vha_inv_rope_fp8_quant(g["o"], g["mix"], g["positions"], g["cos_sin"], G, R)
+    T, H = g["o"].shape[:2]
+    hpg = H // G
+    packed = O.pack_scale_exponents(exp)  # [T, H]
+    ref = g["scale"][:, :, :T].transpose(2, 0, 1).reshape(T, H)
+    assert (packed == ref).mean() > 0.99
+    assert (q == g["fp8"]).mean() > 0.995
+
+
+@pytest.mark.parametrize("name", ["sigmoid_mul_quant_5x1024", "sigmoid_mul_quant_13x2048"])
+def test_sigmoid_mul_quant_matches_plugin_kernel(name):
+    g = load(name)
+    q, s = O.sigmoid_mul_quant_fp8(g["x"], g["gate"])
+    assert np.array_equal(s, g["scale"])
+    assert np.array_equal(q, g["fp8"])
