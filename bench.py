@@ -1,0 +1,436 @@
+"""HCA decode benchmark (BASELINE config 2 per GPU, through the 37-layer HCA stack).
+
+A step is one decode step of the HCA layer path for 64 requests x 3 query
+tokens (ECHO/MTP with 2 drafts) at contexts U[4096, 131072], fp8 KV, 64
+heads x 128: per-step metadata build, then for each of 37 HCA layers (each
+with its own caches and inputs, so L2 cannot serve repeats) the Q head-norm +
+RoPE with the fp8 SWA insert, compressor state save + block compression,
+sparse attention over [window || compressed] rows, and VHA + inverse RoPE +
+FP8 quant.  The input GEMMs and wo_a / wo_b are outside the path.  The step is
+captured in one CUDA graph.
+
+Multi-GPU (torchrun): requests shard data-parallel, 64 per GPU, no
+collective (weak scaling); timing is the max over ranks of the device time.
+
+``--impl reference`` times the reference's CPU restatement of the same path
+(the oracle port) on the host cores; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vllm-ernie_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+LAYERS = 37
+BATCH = 64
+Q_PER_SEQ = 3
+CTX_LO, CTX_HI = 4096, 131072
+MAX_COMPRESSED = 1024  # ceil(131072 / 128) rounded to 128
+METRIC = "HCA attn tokens/s & HBM roofline % (decode, 128K ctx, fp8 KV) at 1/2/4/8 B200"
+UNIT = "tokens/s"
+ROW_BYTES_ALGO = 64 + 2 * 64 + 64 // 64  # N + 2R + N/64 at D=128
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def contexts(rank: int) -> np.ndarray:
+    rng = np.random.default_rng(1234 + rank)
+    return rng.integers(CTX_LO, CTX_HI - Q_PER_SEQ, size=BATCH, endpoint=True)
+
+
+def algorithmic_bytes(ctx: np.ndarray, heads: int, head_dim: int) -> int:
+    """Unique KV rows read + Q read + O write of one attention launch."""
+    last = ctx + Q_PER_SEQ - 1
+    rows = (last + 1) // 128 + np.minimum(last + 1, 128 + Q_PER_SEQ - 1)
+    t = len(ctx) * Q_PER_SEQ
+    return int(rows.sum()) * ROW_BYTES_ALGO + 2 * t * heads * head_dim * 2
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the oracle port of the same path
+# ---------------------------------------------------------------------------
+
+
+def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
+    """Oracle (CPU restatement of the reference path) on a bounded sample of
+    the config-2 workload: whole requests (3 query tokens each) through one
+    layer's Q prep, SWA insert, compressor, sparse attention and VHA/inverse
+    RoPE; tokens/s scaled to the 37-layer step."""
+    from oracle import attention as A
+    from oracle import cache as C
+    from oracle import metadata as M
+    from oracle import output as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(7)
+    ctx = contexts(0)
+    heads, d, r = 64, 128, 64
+    cos_sin = C.rope_cos_sin_cache(CTX_HI + 8, r, 160000.0)
+    done_tokens, t_total, reqs = 0, 0.0, 0
+    for b in range(len(ctx)):
+        L = int(ctx[b])
+        end = L + Q_PER_SEQ
+        ncomp = end // 128 + 1
+        sw_lo = max(L - 127, 0)
+        # this request's caches: contiguous pages
+        swa_pages = (end + 63) // 64
+        swa = np.zeros((swa_pages, C.page_bytes(64, d, r)), np.uint8)
+        live = np.arange(sw_lo, end)
+        C.insert_rows(swa, live, rng.standard_normal((len(live), d)).astype(np.float32), 64, d, r)
+        comp = np.zeros(((ncomp + 1) // 2 + 1, C.page_bytes(2, d, r)), np.uint8)
+        C.insert_rows(comp, np.arange(ncomp), rng.standard_normal((ncomp, d)).astype(np.float32), 2, d, r)
+        state = rng.standard_normal(((end + 7) // 8, 8, 2 * d)).astype(np.float32)
+        q = rng.standard_normal((Q_PER_SEQ, heads, d)).astype(np.float32)
+        kv = rng.standard_normal((Q_PER_SEQ, d)).astype(np.float32)
+        ks = rng.standard_normal((Q_PER_SEQ, 2 * d)).astype(np.float32)
+        pos = np.arange(L, end)
+        qsl = np.array([0, Q_PER_SEQ], np.int32)
+        sl = np.array([end], np.int32)
+        swa_bt = np.arange(swa_pages, dtype=np.int32)[None]
+        comp_bt = np.arange(comp.shape[0], dtype=np.int32)[None]
+        st_bt = np.arange(state.shape[0], dtype=np.int32)[None]
+        t0 = time.perf_counter()
+        qp = O.q_prep(q, pos, cos_sin, r, 1e-6)
+        swa_slot = M.slot_mapping(qsl, sl, swa_bt, 64)
+        C.insert_rows(swa, swa_slot, O.kv_rope(kv, pos, cos_sin, r), 64, d, r)
+        st_slot = M.slot_mapping(qsl, sl, st_bt, 8)
+        C.save_partial_states(state, ks[:, :d], ks[:, d:], np.zeros((128, d), np.float32), pos, st_slot, 8, 128)
+        t2r = np.zeros(Q_PER_SEQ, np.int32)
+        c_slot = M.compressed_slot_mapping(Q_PER_SEQ, qsl, sl, comp_bt, 2, 128)
+        C.compress_norm_rope_store(state, t2r, pos, st_slot, st_bt, 8, np.ones(d, np.float32), 1e-6, cos_sin,
+                                   comp, c_slot, 2, d, r)
+        idx = np.zeros((Q_PER_SEQ, 128), np.int32)
+        lens = np.zeros(Q_PER_SEQ, np.int32)
+        M.swa_indices_and_lens(Q_PER_SEQ, 128, qsl, sl, t2r, swa_slot >= 0, swa_bt, 64, idx, lens)
+        gd = np.zeros((Q_PER_SEQ, MAX_COMPRESSED), np.int32)
+        dl = np.zeros(Q_PER_SEQ, np.int32)
+        M.c128a_topk_metadata(pos, 128, Q_PER_SEQ, t2r, comp_bt, 2, swa_slot, gd, dl,
+                              np.zeros((1, MAX_COMPRESSED), np.int32), MAX_COMPRESSED)
+        o = A.sparse_decode(qp, swa, 64, idx, lens, comp, 2, gd, dl, d ** -0.5, np.zeros(heads, np.float32), d, r)
+        mix = np.eye(heads, dtype=np.float32)
+        O.inv_rope_fp8_quant(np.einsum("hg,tgd->thd", mix, o), pos, cos_sin, 8, r)
+        t_total += time.perf_counter() - t0
+        done_tokens += Q_PER_SEQ
+        reqs += 1
+        if t_total > seconds_budget:
+            break
+    per_layer_tok_s = done_tokens / t_total
+    return {"value": per_layer_tok_s / LAYERS, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{reqs} of {len(ctx)} config-2 requests x {Q_PER_SEQ} tokens through one HCA layer "
+                      f"({t_total:.1f} s), scaled to the {LAYERS}-layer step"}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    sys.path.insert(0, ROOT)
+    for _ in range(args.warmup):
+        pass
+    vals = []
+    budget = max(3.0, 20.0 / max(args.steps, 1))
+    for _ in range(max(args.steps, 1)):
+        vals.append(cpu_sample_tokens_per_s(budget))
+    v = statistics.median([x["value"] for x in vals])
+    cb = dict(vals[0])
+    cb["value"] = v
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": Q_PER_SEQ * BATCH / v * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x 37 HCA layers",
+                       "parallelism": f"dp{ws}", "l2": "inputs larger than L2"},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = setup_dist()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200.decode import build_decode_metadata, decode_layer, random_layer_weights
+    from vllm_ernie_b200.synthetic import (HCADims, alloc_layer_caches, make_decode_batch,
+                                           rope_cos_sin_cache)
+
+    dev = torch.device("cuda", local)
+    dims = HCADims(heads=64, head_dim=128, rope_dim=64, n_groups=8)
+    ctx = contexts(rank)
+    batch = make_decode_batch(ctx.tolist(), Q_PER_SEQ, dims, dev, seed=rank, max_model_len=CTX_HI)
+    T = batch.num_tokens
+    caches = [alloc_layer_caches(batch, seed=10_000 * rank + l) for l in range(LAYERS)]
+    weights = [random_layer_weights(dims, dev, seed=l) for l in range(LAYERS)]
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    q_raw = torch.randn((LAYERS, T, dims.heads, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    kv = torch.randn((LAYERS, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    kv_score = torch.randn((LAYERS, T, 2 * dims.head_dim), generator=g, device=dev)
+    cos_sin = rope_cos_sin_cache(CTX_HI + 8, dims.rope_dim, dims.rope_theta, dev)
+    bufs: dict = {}
+    splits = args.splits or None
+    md = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs)
+    q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
+    o_buf = torch.empty_like(q_buf)
+    outs = [None] * LAYERS
+
+    def step():
+        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=md.num_splits, buffers=bufs)
+        for l in range(LAYERS):
+            outs[l] = decode_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin,
+                                   q_buf=q_buf, o_buf=o_buf)
+
+    # metadata: token->req, 2 slot maps, compressed slot map (fill + map),
+    # window indices, C128A indices; per layer: insert, state save, compress,
+    # attention (+ split-K combine), VHA/inverse-RoPE/FP8
+    launches_per_step = 7 + LAYERS * (5 + (1 if md.num_splits > 1 else 0))
+    step()  # warm (allocations, workspace)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    barrier(ws)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(ws)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms, ws)
+    value = ws * T / (ms * 1e-3)
+
+    # --- dominant kernel: sparse attention, one launch per layer in a graph ---
+    attn_graph = torch.cuda.CUDAGraph()
+    qs = [torch.empty_like(q_buf) for _ in range(LAYERS)]
+    for l in range(LAYERS):
+        ops.fused_qnorm_rope_kv_insert(q_raw[l], kv[l], caches[l].swa, md.swa_slot, batch.positions, cos_sin,
+                                       dims.heads, dims.eps, dims.swa_page, dims.rope_dim, out=qs[l])
+
+    def attn_all():
+        for l in range(LAYERS):
+            ops.sparse_decode(qs[l], caches[l].swa, dims.swa_page, md.swa_indices, md.swa_lens, caches[l].comp,
+                              dims.comp_page, md.comp_indices, md.comp_lens, dims.head_dim ** -0.5,
+                              weights[l].attn_sink, out=o_buf, group_starts=md.group_starts,
+                              max_group_tokens=md.max_group_tokens, num_splits=md.num_splits)
+
+    attn_all()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        attn_all()
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(attn_graph):
+        attn_all()
+    for _ in range(3):
+        attn_graph.replay()
+    torch.cuda.synchronize()
+    reps = max(args.steps, 5)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        attn_graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    attn_us = e0.elapsed_time(e1) * 1e3 / (reps * LAYERS)
+    algo = algorithmic_bytes(ctx, dims.heads, dims.head_dim)
+    hbm, src = peaks()
+    achieved = algo / (attn_us * 1e-6) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "decode_attention_traffic.json")
+    if os.path.exists(prof):
+        try:
+            with open(prof) as f:
+                traffic = json.load(f).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    # --- e2e: public API with host buffers (pinned), copies inside timing ---
+    h_q = torch.empty(q_raw.shape, dtype=q_raw.dtype, pin_memory=True)
+    h_kv = torch.empty(kv.shape, dtype=kv.dtype, pin_memory=True)
+    h_ks = torch.empty(kv_score.shape, dtype=kv_score.dtype, pin_memory=True)
+    h_q.copy_(q_raw)
+    h_kv.copy_(kv)
+    h_ks.copy_(kv_score)
+    h_out = [torch.empty(o[0].shape, dtype=torch.uint8, pin_memory=True) for o in outs]
+    h_scale = [torch.empty(o[1].shape, dtype=torch.int32, pin_memory=True) for o in outs]
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(e2e_steps):
+        q_raw.copy_(h_q, non_blocking=True)
+        kv.copy_(h_kv, non_blocking=True)
+        kv_score.copy_(h_ks, non_blocking=True)
+        graph.replay()
+        for l in range(LAYERS):
+            h_out[l].copy_(outs[l][0].view(torch.uint8), non_blocking=True)
+            h_scale[l].copy_(outs[l][1], non_blocking=True)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps, ws)
+    h2d = h_q.numel() * 2 + h_kv.numel() * 2 + h_ks.numel() * 4
+    d2h = sum(o[0].numel() + o[1].numel() * 4 for o in outs)
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, ROOT)
+        cpu = cpu_sample_tokens_per_s(15.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x 37 HCA layers",
+                       "parallelism": f"dp{ws}", "layers": LAYERS, "tokens_per_step_per_gpu": T,
+                       "num_splits": md.num_splits, "l2": "inputs larger than L2 (37 layers' caches)",
+                       "per_layer_us": ms * 1e3 / LAYERS},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
+                         "kernel": "hca_attention_kernel (decode)", "launch_us": attn_us,
+                         "algorithmic_bytes": algo},
+            "cpu_baseline": cpu,
+            "e2e": {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph, attn_graph
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -108,6 +108,44 @@ def sparse_prefill_workspace(
     return out
 
 
+def sparse_prefill_paged(
+    q: np.ndarray,
+    positions: np.ndarray,
+    token_to_req: np.ndarray,
+    swa_cache: np.ndarray,
+    swa_page: int,
+    swa_bt: np.ndarray,
+    comp_cache: np.ndarray | None,
+    comp_page: int,
+    comp_bt: np.ndarray | None,
+    window: int,
+    ratio: int,
+    scale: float,
+    sink: np.ndarray | None,
+    head_dim: int,
+    rope_dim: int,
+) -> np.ndarray:
+    """Prefill semantics of ``_forward_prefill``
+    (``V/models/deepseek_v4/nvidia/flashmla.py:304-424``) evaluated straight on
+    the paged caches: token at position ``p`` of request ``r`` attends
+    compressed entries ``0 .. (p + 1) // ratio - 1`` and window positions
+    ``max(p - W + 1, 0) .. p`` (``cache_utils.py:567-594``)."""
+    t_n, h, d = q.shape
+    out = np.zeros((t_n, h, d), dtype=np.float32)
+    for t in range(t_n):
+        p, r = int(positions[t]), int(token_to_req[t])
+        wpos = np.arange(max(p - window + 1, 0), p + 1)
+        wsl = swa_bt[r, wpos // swa_page].astype(np.int64) * swa_page + wpos % swa_page
+        rows = [read_rows(swa_cache, wsl, swa_page, head_dim, rope_dim)]
+        nc = (p + 1) // ratio if comp_cache is not None else 0
+        if nc:
+            ci = np.arange(nc)
+            csl = comp_bt[r, ci // comp_page].astype(np.int64) * comp_page + ci % comp_page
+            rows.append(read_rows(comp_cache, csl, comp_page, head_dim, rope_dim))
+        out[t] = sparse_attention_token(q[t], np.concatenate(rows), scale, sink)
+    return out
+
+
 def hca_rows_for_position(p: int, window: int = 128, ratio: int = 128) -> tuple[int, int]:
     """``(compressed_entries, window_rows)`` a query at position ``p`` attends."""
     return (p + 1) // ratio, min(p + 1, window)

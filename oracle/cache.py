@@ -87,14 +87,16 @@ def read_rows(
     (``V/models/deepseek_v4/common/ops/cache_utils.py:197-320``).
     """
     nope, data, sbytes = row_geometry(head_dim, rope_dim)
-    slots = np.asarray(slots).reshape(-1)
-    out = np.zeros((slots.shape[0], head_dim), dtype=np.float32)
-    for i, slot in enumerate(slots.tolist()):
-        base, d0, s0, *_ = _row_views(cache, slot, page_size, head_dim, rope_dim)
-        vals = e4m3_to_f32(base[d0 : d0 + nope]).reshape(-1, QUANT_BLOCK)
-        exps = base[s0 : s0 + nope // QUANT_BLOCK].astype(np.int32) - 127
-        out[i, :nope] = (vals * np.ldexp(np.float32(1.0), exps)[:, None]).reshape(-1)
-        out[i, nope:] = bf16_from_bytes(base[d0 + nope : d0 + data])
+    slots = np.asarray(slots, dtype=np.int64).reshape(-1)
+    page, off = np.divmod(slots, page_size)
+    d_idx = off[:, None] * data + np.arange(data)[None, :]
+    s_idx = page_size * data + off[:, None] * sbytes + np.arange(nope // QUANT_BLOCK)[None, :]
+    raw = cache[page[:, None], d_idx]  # [n, data]
+    exps = cache[page[:, None], s_idx].astype(np.int32) - 127  # [n, nope/64]
+    out = np.empty((slots.shape[0], head_dim), dtype=np.float32)
+    vals = e4m3_to_f32(raw[:, :nope]).reshape(-1, nope // QUANT_BLOCK, QUANT_BLOCK)
+    out[:, :nope] = (vals * np.ldexp(np.float32(1.0), exps)[..., None]).reshape(-1, nope)
+    out[:, nope:] = bf16_from_bytes(raw[:, nope:])
     return out
 
 

@@ -1,0 +1,207 @@
+"""GPU parity of the sparse HCA attention (decode and prefill) and of the
+whole decode hot path, against the CPU oracle.
+
+Tolerance (from the task's parity bar for floating point): the bf16 output
+vs the oracle's fp64 evaluation on the same cached rows must have
+``max |err| <= 2e-2`` and relative L2 ``<= 5e-3``.  Index tables are
+checked bit-exactly against the oracle's builders first.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as A
+from oracle import cache as C
+from oracle import metadata as M
+from oracle import output as O
+from oracle.fp8 import bf16_round
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+MAX_ABS, MAX_REL_L2 = 2e-2, 5e-3
+
+
+def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_REL_L2):
+    err = np.abs(got.astype(np.float64) - ref)
+    rel = np.linalg.norm(got.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert err.max() <= max_abs, (err.max(), rel)
+    assert rel <= max_rel, (err.max(), rel)
+
+
+def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True):
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200.decode import build_decode_metadata
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
+
+    dims = HCADims(heads=heads)
+    maxc = 1024
+    b = make_decode_batch(ctx, q_per_seq, dims, DEV, seed=seed, max_model_len=maxc * 128)
+    caches = alloc_layer_caches(b, seed=seed + 1)
+    md = build_decode_metadata(b, maxc, num_splits=splits)
+    # index tables vs the oracle builders (bit-exact)
+    qsl, sl = b.query_start_loc.cpu().numpy(), b.seq_lens.cpu().numpy()
+    t2r = M.token_to_req_indices(qsl)
+    swa_slot = M.slot_mapping(qsl, sl, b.swa_bt.cpu().numpy(), 64)
+    assert np.array_equal(md.swa_slot.cpu().numpy(), swa_slot)
+    n = b.num_tokens
+    idx = np.full((n, 128), -7, np.int32)
+    lens = np.zeros(n, np.int32)
+    M.swa_indices_and_lens(n, 128, qsl, sl, t2r, swa_slot >= 0, b.swa_bt.cpu().numpy(), 64, idx, lens)
+    assert np.array_equal(md.swa_lens.cpu().numpy(), lens)
+    assert np.array_equal(md.swa_indices.cpu().numpy(), idx)
+    gd = np.zeros((n, maxc), np.int32)
+    dl = np.zeros(n, np.int32)
+    M.c128a_topk_metadata(b.positions.cpu().numpy(), 128, n, t2r, b.comp_bt.cpu().numpy(), 2, swa_slot, gd,
+                          dl, np.zeros((1, maxc), np.int32), maxc)
+    assert np.array_equal(md.comp_lens.cpu().numpy(), dl)
+    assert np.array_equal(md.comp_indices.cpu().numpy(), gd)
+
+    g = torch.Generator(device=DEV).manual_seed(seed + 2)
+    q = torch.randn((n, heads, 128), generator=g, device=DEV).to(torch.bfloat16)
+    if sink_mode == "random":
+        sink = torch.randn(heads, generator=g, device=DEV)
+    elif sink_mode == "neginf":
+        sink = torch.full((heads,), -float("inf"), device=DEV)
+    else:
+        sink = None
+    out = ops.sparse_decode(q, caches.swa, 64, md.swa_indices, md.swa_lens,
+                            caches.comp if comp else None, 2, md.comp_indices if comp else None,
+                            md.comp_lens if comp else None, 128 ** -0.5, sink,
+                            group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,
+                            num_splits=md.num_splits)
+    ref = A.sparse_decode(q.float().cpu().numpy(), caches.swa.cpu().numpy(), 64, idx, lens,
+                          caches.comp.cpu().numpy() if comp else None, 2, gd if comp else None,
+                          dl if comp else None, 128 ** -0.5,
+                          sink.cpu().numpy() if sink is not None else None, 128, 64)
+    check_close(out.float().cpu().numpy(), ref)
+    return out
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("q_per_seq", [1, 3])
+def test_decode_mixed_contexts(q_per_seq, splits):
+    # short (< window), boundary-crossing, and long contexts
+    ctx = [0, 5, 126, 127, 128, 254, 1000, 9000, 40000, 130000]
+    _decode_case(ctx, q_per_seq, 64, splits, seed=11 + q_per_seq + splits)
+
+
+def test_decode_config2_shape_sample():
+    """Config-2 geometry (64 heads x 128, 3 queries/seq) on a sample of 8
+    requests with contexts drawn from U[4096, 131072]."""
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(4096, 131072, size=8).tolist()
+    _decode_case(ctx, 3, 64, 4, seed=3)
+
+
+@pytest.mark.parametrize("sink_mode", ["neginf", "none"])
+def test_decode_sink_variants(sink_mode):
+    _decode_case([300, 77, 5000], 3, 64, 2, seed=5, sink_mode=sink_mode)
+
+
+def test_decode_16_heads_window_only():
+    _decode_case([3, 200, 2000], 3, 16, 1, seed=9, comp=False)
+
+
+def test_decode_grid_has_idle_splits():
+    # many splits relative to rows: empty splits must still combine correctly
+    _decode_case([10, 150], 3, 64, 8, seed=13)
+
+
+def test_prefill_matches_oracle():
+    from vllm_ernie_b200 import ops
+
+    heads = 64
+    # prefill chunks: (prior context, chunk length)
+    reqs = [(0, 300), (1000, 131), (128 * 7, 64)]
+    q_lens = np.array([c for _, c in reqs])
+    qsl = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    seq = np.array([p + c for p, c in reqs], np.int32)
+    # pages: make every needed position mapped (window of the first token .. end)
+    swa_bt = np.zeros((3, (seq.max() + 63) // 64 + 2), np.int32)
+    comp_bt = np.zeros((3, seq.max() // 256 + 2), np.int32)
+    k = 0
+    for r, (p, c) in enumerate(reqs):
+        lo, hi = max(p - 127, 0) // 64, (p + c + 63) // 64
+        swa_bt[r, lo:hi] = np.arange(k, k + hi - lo)
+        k += hi - lo
+    n_swa = k
+    k = 0
+    for r, (p, c) in enumerate(reqs):
+        hi = (p + c) // 128 // 2 + 1
+        comp_bt[r, :hi] = np.arange(k, k + hi)
+        k += hi
+    n_comp = k
+    from vllm_ernie_b200.cache_layout import page_bytes
+
+    gen = torch.Generator(device=DEV).manual_seed(22)
+    swa = torch.zeros((n_swa, page_bytes(64, 128, 64)), dtype=torch.uint8, device=DEV)
+    comp = torch.zeros((n_comp, page_bytes(2, 128, 64)), dtype=torch.uint8, device=DEV)
+    for cache, page, npg in ((swa, 64, n_swa), (comp, 2, n_comp)):
+        rows = torch.randn((npg * page, 128), generator=gen, device=DEV).to(torch.bfloat16)
+        ops.quantize_and_insert_k_cache(rows, cache, torch.arange(npg * page, device=DEV), page)
+    n = int(qsl[-1])
+    q = torch.randn((n, heads, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    sink = torch.randn(heads, generator=gen, device=DEV)
+    out = ops.sparse_prefill(q, torch.from_numpy(qsl).to(DEV), torch.from_numpy(seq).to(DEV), swa, 64,
+                             torch.from_numpy(swa_bt).to(DEV), comp, 2, torch.from_numpy(comp_bt).to(DEV),
+                             128, 128, 128 ** -0.5, sink)
+    t2r = M.token_to_req_indices(qsl)
+    pos = np.concatenate([np.arange(p, p + c) for p, c in reqs])
+    ref = A.sparse_prefill_paged(q.float().cpu().numpy(), pos, t2r, swa.cpu().numpy(), 64, swa_bt,
+                                 comp.cpu().numpy(), 2, comp_bt, 128, 128, 128 ** -0.5,
+                                 sink.cpu().numpy(), 128, 64)
+    check_close(out.float().cpu().numpy(), ref)
+
+
+def test_decode_layer_hot_path_matches_oracle():
+    """q prep + SWA insert, compressor, attention and VHA/inverse-RoPE/FP8 of
+    one layer vs the oracle composition of the same steps."""
+    from vllm_ernie_b200.decode import build_decode_metadata, decode_layer, random_layer_weights
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dims = HCADims(heads=64)
+    maxc = 256
+    # contexts chosen so some query tokens complete a 128-block this step
+    ctx = [125, 254, 1020, 5000, 30000]
+    b = make_decode_batch(ctx, 3, dims, DEV, seed=31, max_model_len=maxc * 128)
+    caches = alloc_layer_caches(b, seed=32)
+    w = random_layer_weights(dims, DEV, seed=33)
+    md = build_decode_metadata(b, maxc, num_splits=2)
+    n = b.num_tokens
+    g = torch.Generator(device=DEV).manual_seed(34)
+    q_raw = torch.randn((n, 64, 128), generator=g, device=DEV).to(torch.bfloat16)
+    kv = torch.randn((n, 128), generator=g, device=DEV).to(torch.bfloat16)
+    kv_score = torch.randn((n, 256), generator=g, device=DEV)
+    cos_sin = rope_cos_sin_cache(maxc * 128 + 8, 64, dims.rope_theta, DEV)
+    swa0, comp0, state0 = (caches.swa.cpu().numpy(), caches.comp.cpu().numpy(), caches.state.cpu().numpy())
+    y = decode_layer(b, md, caches, w, q_raw, kv, kv_score, cos_sin, quantize=False)
+    torch.cuda.synchronize()
+
+    # oracle composition
+    pos = b.positions.cpu().numpy()
+    cs = cos_sin.cpu().numpy()
+    qsl, sl = b.query_start_loc.cpu().numpy(), b.seq_lens.cpu().numpy()
+    t2r = M.token_to_req_indices(qsl)
+    swa_bt, comp_bt, st_bt = b.swa_bt.cpu().numpy(), b.comp_bt.cpu().numpy(), b.state_bt.cpu().numpy()
+    qp = O.q_prep(q_raw.float().cpu().numpy(), pos, cs, 64, 1e-6)
+    swa_slot = M.slot_mapping(qsl, sl, swa_bt, 64)
+    C.insert_rows(swa0, swa_slot, O.kv_rope(kv.float().cpu().numpy(), pos, cs, 64), 64, 128, 64)
+    st_slot = M.slot_mapping(qsl, sl, st_bt, 8)
+    ks = kv_score.cpu().numpy()
+    C.save_partial_states(state0, ks[:, :128], ks[:, 128:], w.ape.cpu().numpy(), pos, st_slot, 8, 128)
+    c_slot = M.compressed_slot_mapping(n, qsl, sl, comp_bt, 2, 128)
+    assert (c_slot >= 0).sum() >= 2
+    C.compress_norm_rope_store(state0, t2r, pos, st_slot, st_bt, 8, w.comp_norm.cpu().numpy(), 1e-6, cs,
+                               comp0, c_slot, 2, 128, 64)
+    idx = np.zeros((n, 128), np.int32)
+    lens = np.zeros(n, np.int32)
+    M.swa_indices_and_lens(n, 128, qsl, sl, t2r, swa_slot >= 0, swa_bt, 64, idx, lens)
+    gd = np.zeros((n, maxc), np.int32)
+    dl = np.zeros(n, np.int32)
+    M.c128a_topk_metadata(pos, 128, n, t2r, comp_bt, 2, swa_slot, gd, dl, np.zeros((1, maxc), np.int32), maxc)
+    o = A.sparse_decode(qp, swa0, 64, idx, lens, comp0, 2, gd, dl, 128 ** -0.5, w.attn_sink.cpu().numpy(), 128, 64)
+    mix = w.vha_mix.float().cpu().numpy()
+    y_ref = O.inv_rope_fp8_quant(np.einsum("hg,tgd->thd", mix, bf16_round(o)), pos, cs, 8, 64, quant=False)
+    check_close(y.float().cpu().numpy(), y_ref)

@@ -1,0 +1,447 @@
+// KV-cache side of the HCA path: QK RMSNorm, query head-norm + RoPE with the
+// fused fp8 SWA-cache insert, plain quantised insert, dequant gather, the
+// compressor state save and the per-128-token block compressor.
+//
+// All of these are HBM-bound, byte-moving kernels: one warp (or one CTA)
+// per row, 16-byte vector accesses where the row layout allows, no tensor
+// cores.  Row geometry is templated on the head dim (128 or 512).
+#include "hca_common.cuh"
+
+namespace hca {
+namespace {
+
+// ----------------------------------------------------------------------------
+// QK RMSNorm: grid (T, 2), y = x * rsqrt(mean(x^2) + eps) * w, fp32 math.
+// ----------------------------------------------------------------------------
+__global__ void qk_rmsnorm_kernel(__nv_bfloat16* q_out, int64_t q_out_stride,
+                                  const __nv_bfloat16* q_in, int64_t q_in_stride,
+                                  const __nv_bfloat16* q_w, int q_size, __nv_bfloat16* kv_out,
+                                  int64_t kv_out_stride, const __nv_bfloat16* kv_in,
+                                  int64_t kv_in_stride, const __nv_bfloat16* kv_w, int kv_size,
+                                  float eps) {
+  __shared__ float red[32];
+  const int64_t t = blockIdx.x;
+  const bool is_q = blockIdx.y == 0;
+  const int n = is_q ? q_size : kv_size;
+  const __nv_bfloat16* x = is_q ? q_in + t * q_in_stride : kv_in + t * kv_in_stride;
+  const __nv_bfloat16* w = is_q ? q_w : kv_w;
+  __nv_bfloat16* y = is_q ? q_out + t * q_out_stride : kv_out + t * kv_out_stride;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __bfloat162float(x[i]);
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float rrms = rsqrtf(ss / static_cast<float>(n) + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    y[i] = __float2bfloat16_rn(__bfloat162float(x[i]) * rrms * __bfloat162float(w[i]));
+}
+
+// ----------------------------------------------------------------------------
+// One cached row held by one warp: lane l owns elements [l*E, (l+1)*E).
+// ----------------------------------------------------------------------------
+template <int D>
+struct WarpRow {
+  static constexpr int E = D / 32;  // elements per lane
+  static_assert(E % 2 == 0 && E >= 2, "head_dim must be a multiple of 64");
+  float v[E];
+
+  __device__ __forceinline__ void load_bf16(const __nv_bfloat16* row, int lane) {
+    const uint16_t* p = reinterpret_cast<const uint16_t*>(row) + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = bf16_bits_to_float(p[i]);
+  }
+
+  // GPT-J rotation of the pairs that fall in the last R dims.
+  __device__ __forceinline__ void rope(const float* cs, int rope_dim, int lane, bool inverse) {
+    const int nope = D - rope_dim;
+    const int half = rope_dim / 2;
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+      const int d = lane * E + i;
+      if (d >= nope) {
+        const int pr = (d - nope) >> 1;
+        const float c = cs[pr];
+        const float s = inverse ? -cs[half + pr] : cs[half + pr];
+        rope_pair(v[i], v[i + 1], c, s);
+      }
+    }
+  }
+
+  // Quantise the NoPE part (from `v`, already bf16 valued) and store the row:
+  // fp8 NoPE bytes, RoPE as bf16 of `rope_src`, UE8M0 scale bytes + pad 0.
+  __device__ __forceinline__ void store_cache_row(RowPtr dst, int rope_dim, int lane, bool divide,
+                                                  const float* rope_src) {
+    const int nope = D - rope_dim;
+    const int d0 = lane * E;
+    constexpr int kLanesPerBlock = kQuantBlock / E;  // lanes sharing one scale
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < kLanesPerBlock; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (d0 < nope) {
+      const int e = ue8m0_exponent(amax, 1e-4f, divide);
+      const float inv = exp2i(-e);
+      uint8_t q[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) q[i] = to_e4m3(v[i] * inv);
+#pragma unroll
+      for (int i = 0; i < E; ++i) dst.data[d0 + i] = q[i];
+      if ((d0 % kQuantBlock) == 0) dst.scale[d0 / kQuantBlock] = encode_ue8m0(e);
+    } else {
+      uint16_t* r = reinterpret_cast<uint16_t*>(dst.data + nope) + (d0 - nope);
+#pragma unroll
+      for (int i = 0; i < E; ++i) r[i] = float_to_bf16_bits(rope_src[i]);
+    }
+    if (lane == 0) dst.scale[nope / kQuantBlock] = 0;
+  }
+};
+
+// grid (T, ceil((padded_heads + 1) / 4)), 128 threads: warp w of block y
+// handles head y*4 + w; head index == padded_heads is the KV row.
+template <int D>
+__global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st, int64_t qo_sh,
+                                            int padded_heads, const __nv_bfloat16* q,
+                                            int64_t q_st, int64_t q_sh, int num_heads,
+                                            const __nv_bfloat16* kv, int64_t kv_stride,
+                                            uint8_t* cache, int page_size, int64_t page_stride,
+                                            const int64_t* slot_mapping,
+                                            const int64_t* positions, const float* cos_sin,
+                                            int64_t cs_stride, int rope_dim, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x;
+  const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
+  if (h > padded_heads) return;
+  WarpRow<D> row;
+  const float* cs = cos_sin + positions[t] * cs_stride;
+  if (h < num_heads) {
+    row.load_bf16(q + t * q_st + h * q_sh, lane);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < WarpRow<D>::E; ++i) ss += row.v[i] * row.v[i];
+    ss = warp_sum(ss);
+    const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int i = 0; i < WarpRow<D>::E; ++i) row.v[i] *= rrms;
+    row.rope(cs, rope_dim, lane, false);
+    uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * WarpRow<D>::E;
+#pragma unroll
+    for (int i = 0; i < WarpRow<D>::E; ++i) o[i] = float_to_bf16_bits(row.v[i]);
+  } else if (h < padded_heads) {
+    uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * WarpRow<D>::E;
+#pragma unroll
+    for (int i = 0; i < WarpRow<D>::E; ++i) o[i] = 0;
+  } else {
+    const int64_t slot = slot_mapping[t];
+    if (slot < 0) return;
+    row.load_bf16(kv + t * kv_stride, lane);
+    float roped[WarpRow<D>::E];
+    WarpRow<D> r2 = row;
+    r2.rope(cs, rope_dim, lane, false);
+#pragma unroll
+    for (int i = 0; i < WarpRow<D>::E; ++i) roped[i] = r2.v[i];
+    const RowGeom g = row_geom(D, rope_dim);
+    row.store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, roped);
+  }
+}
+
+// Quantise already-rotated rows and insert (one warp per token).
+template <int D>
+__global__ void quantize_insert_kernel(uint8_t* cache, int page_size, int64_t page_stride,
+                                       const __nv_bfloat16* k, int64_t k_stride,
+                                       const int64_t* slot_mapping, int num_tokens, int rope_dim) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= num_tokens) return;
+  const int64_t slot = slot_mapping[t];
+  if (slot < 0) return;
+  WarpRow<D> row;
+  row.load_bf16(k + t * k_stride, lane);
+  const RowGeom g = row_geom(D, rope_dim);
+  row.store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, row.v);
+}
+
+// Dequantise one cached row into bf16 (one warp per row).
+template <int D>
+__device__ __forceinline__ void dequant_row_to_bf16(const uint8_t* cache, int64_t slot,
+                                                    int page_size, int64_t page_stride,
+                                                    int rope_dim, __nv_bfloat16* out, int lane) {
+  constexpr int E = D / 32;
+  const RowGeom g = row_geom(D, rope_dim);
+  const RowPtr p = row_ptr(const_cast<uint8_t*>(cache), slot, page_size, page_stride, g);
+  const int d0 = lane * E;
+  uint16_t* o = reinterpret_cast<uint16_t*>(out) + d0;
+  if (d0 < g.nope) {
+    const float sc = exp2i(static_cast<int>(p.scale[d0 / kQuantBlock]) - 127);
+#pragma unroll
+    for (int i = 0; i < E; ++i) o[i] = float_to_bf16_bits(e4m3_to_float(p.data[d0 + i]) * sc);
+  } else {
+    const uint16_t* r = reinterpret_cast<const uint16_t*>(p.data + g.nope) + (d0 - g.nope);
+#pragma unroll
+    for (int i = 0; i < E; ++i) o[i] = r[i];
+  }
+}
+
+// grid (num_reqs, 32), 4 warps per block; warps stride over gather rows.
+template <int D>
+__global__ void dequant_gather_kernel(__nv_bfloat16* out, int64_t out_sr, int64_t out_st,
+                                      const uint8_t* cache, int page_size, int64_t page_stride,
+                                      const int32_t* seq_lens, const int32_t* gather_lens,
+                                      const int32_t* bt, int64_t bt_stride, int offset,
+                                      int rope_dim) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int worker = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nworkers = gridDim.y * (blockDim.x >> 5);
+  const int sl = seq_lens[b];
+  const int gl = gather_lens ? gather_lens[b] : sl;
+  const int start = sl - gl;
+  for (int i = worker; i < gl; i += nworkers) {
+    const int pos = start + i;
+    const int64_t slot =
+        static_cast<int64_t>(bt[b * bt_stride + pos / page_size]) * page_size + pos % page_size;
+    dequant_row_to_bf16<D>(cache, slot, page_size, page_stride, rope_dim,
+                           out + b * out_sr + static_cast<int64_t>(offset + i) * out_st, lane);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Compressor state save: state[slot] = [kv, score + ape[pos % ratio]].
+// ----------------------------------------------------------------------------
+__global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t s_tok,
+                                           const float* kv, int64_t kv_stride,
+                                           const float* score, int64_t score_stride,
+                                           const float* ape, int64_t ape_stride,
+                                           const int64_t* positions, const int64_t* slot_mapping,
+                                           int block_size, int head_size, int state_width,
+                                           int ratio) {
+  const int64_t t = blockIdx.x;
+  const int64_t slot = slot_mapping[t];
+  if (slot < 0) return;
+  const int64_t blk = slot / block_size;
+  float* base = state + blk * s_blk + (slot - blk * block_size) * s_tok;
+  const float* a = ape + (positions[t] % ratio) * ape_stride;
+  const float* k = kv + t * kv_stride;
+  const float* s = score + t * score_stride;
+  for (int i = threadIdx.x; i < head_size; i += blockDim.x) {
+    base[i] = k[i];
+    base[state_width + i] = s[i] + a[i];
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Block compressor: one CTA of D threads per boundary token; thread c owns
+// channel c.  Softmax over the `ratio` tokens per channel, weighted sum,
+// RMSNorm, NoPE quant from the bf16 rounding, RoPE of the fp32 normed value
+// at the block start position, store into the compressed cache.
+// ----------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(D) compress_kernel(
+    const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
+    const int64_t* positions, const int64_t* state_slot, const int32_t* bt, int64_t bt_stride,
+    int block_size, const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride,
+    uint8_t* kv_cache, const int64_t* kv_slot, int kv_page_size, int64_t kv_page_stride,
+    int rope_dim, int ratio) {
+  __shared__ float red[32];
+  __shared__ int64_t row_off[512];
+  const int64_t t = blockIdx.x;
+  if (state_slot[t] < 0) return;
+  const int64_t p = positions[t];
+  if ((p + 1) % ratio != 0) return;
+  const int req = t2r[t];
+  const int c = threadIdx.x;
+  // Row offsets of the `ratio` states (all positions are >= 0 at a boundary).
+  for (int i = c; i < ratio; i += D) {
+    const int64_t pos = p - ratio + 1 + i;
+    const int64_t blk = bt[req * bt_stride + pos / block_size];
+    row_off[i] = blk * s_blk + (pos % block_size) * s_tok;
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int i = 0; i < ratio; ++i) m = fmaxf(m, state[row_off[i] + state_width + c]);
+  float den = 0.0f, acc = 0.0f;
+  for (int i = 0; i < ratio; ++i) {
+    const float w = expf(state[row_off[i] + state_width + c] - m);
+    den += w;
+    acc += w * state[row_off[i] + c];
+  }
+  const float comp = acc / den;
+  const float ss = block_sum(comp * comp, red);
+  const float normed = comp * rsqrtf(ss / static_cast<float>(D) + eps) * norm_w[c];
+  const int64_t slot = kv_slot[t];
+  if (slot < 0) return;  // uniform across the CTA
+  const RowGeom g = row_geom(D, rope_dim);
+  const RowPtr dst = row_ptr(kv_cache, slot, kv_page_size, kv_page_stride, g);
+  const int nope = g.nope;
+  // NoPE: UE8M0 quant of the bf16 rounding; 64-channel blocks = 2 warps.
+  const float qv = bf16_round(normed);
+  float amax = warp_max(c < nope ? fabsf(qv) : 0.0f);
+  __syncthreads();
+  if ((c & 31) == 0) red[c >> 5] = amax;
+  __syncthreads();
+  amax = fmaxf(red[(c >> 6) * 2], red[(c >> 6) * 2 + 1]);
+  // RoPE partner (adjacent channel) in fp32.
+  const float partner = __shfl_xor_sync(0xffffffffu, normed, 1);
+  if (c < nope) {
+    const int e = ue8m0_exponent(amax, 1e-4f, false);
+    dst.data[c] = to_e4m3(qv * exp2i(-e));
+    if ((c % kQuantBlock) == 0) dst.scale[c / kQuantBlock] = encode_ue8m0(e);
+  } else {
+    const int64_t cpos = (p / ratio) * ratio;
+    const float* cs = cos_sin + cpos * cs_stride;
+    const int pr = (c - nope) >> 1;
+    const float co = cs[pr], si = cs[rope_dim / 2 + pr];
+    const bool even = ((c - nope) & 1) == 0;
+    const float r = even ? normed * co - partner * si : normed * co + partner * si;
+    reinterpret_cast<uint16_t*>(dst.data + nope)[c - nope] = float_to_bf16_bits(r);
+  }
+  if (c == 0) dst.scale[nope / kQuantBlock] = 0;
+}
+
+}  // namespace
+}  // namespace hca
+
+using namespace hca;
+
+// Instantiated row widths: the BASELINE head dim 128 and the model's 512.
+static bool geom_ok(int head_dim, int rope_dim) {
+  return (head_dim == 128 || head_dim == 512) && valid_geom(head_dim, rope_dim);
+}
+
+extern "C" int hca_qk_rmsnorm(void* q_out, int64_t q_out_stride, const void* q_in,
+                              int64_t q_in_stride, const void* q_weight, int32_t q_size,
+                              void* kv_out, int64_t kv_out_stride, const void* kv_in,
+                              int64_t kv_in_stride, const void* kv_weight, int32_t kv_size,
+                              int32_t num_tokens, float eps, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && q_size > 0 && kv_size > 0);
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(q_out && q_in && q_weight && kv_out && kv_in && kv_weight);
+  qk_rmsnorm_kernel<<<dim3(num_tokens, 2), 256, 0, as_stream(stream)>>>(
+      static_cast<__nv_bfloat16*>(q_out), q_out_stride, static_cast<const __nv_bfloat16*>(q_in),
+      q_in_stride, static_cast<const __nv_bfloat16*>(q_weight), q_size,
+      static_cast<__nv_bfloat16*>(kv_out), kv_out_stride,
+      static_cast<const __nv_bfloat16*>(kv_in), kv_in_stride,
+      static_cast<const __nv_bfloat16*>(kv_weight), kv_size, eps);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
+                                        int64_t q_out_stride_head, int32_t padded_heads,
+                                        const void* q, int64_t q_stride_tok,
+                                        int64_t q_stride_head, int32_t num_heads, const void* kv,
+                                        int64_t kv_stride, uint8_t* swa_cache, int32_t page_size,
+                                        int64_t page_stride_bytes, const int64_t* slot_mapping,
+                                        const int64_t* positions, const float* cos_sin,
+                                        int64_t cos_sin_stride, int32_t num_tokens,
+                                        int32_t head_dim, int32_t rope_dim, float eps,
+                                        void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && num_heads > 0 && padded_heads >= num_heads && page_size > 0);
+  if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(q_out && q && kv && swa_cache && slot_mapping && positions && cos_sin);
+  dim3 grid(num_tokens, (padded_heads + 1 + 3) / 4);
+  auto* qo = static_cast<__nv_bfloat16*>(q_out);
+  auto* qi = static_cast<const __nv_bfloat16*>(q);
+  auto* ki = static_cast<const __nv_bfloat16*>(kv);
+  if (head_dim == 128)
+    qnorm_rope_kv_insert_kernel<128><<<grid, 128, 0, as_stream(stream)>>>(
+        qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi, q_stride_tok, q_stride_head,
+        num_heads, ki, kv_stride, swa_cache, page_size, page_stride_bytes, slot_mapping,
+        positions, cos_sin, cos_sin_stride, rope_dim, eps);
+  else
+    qnorm_rope_kv_insert_kernel<512><<<grid, 128, 0, as_stream(stream)>>>(
+        qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi, q_stride_tok, q_stride_head,
+        num_heads, ki, kv_stride, swa_cache, page_size, page_stride_bytes, slot_mapping,
+        positions, cos_sin, cos_sin_stride, rope_dim, eps);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_quantize_insert_k(uint8_t* cache, int32_t page_size, int64_t page_stride_bytes,
+                                     const void* k, int64_t k_stride,
+                                     const int64_t* slot_mapping, int32_t num_tokens,
+                                     int32_t head_dim, int32_t rope_dim, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && page_size > 0);
+  if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(cache && k && slot_mapping);
+  const int grid = cdiv(num_tokens, 4);
+  auto* kp = static_cast<const __nv_bfloat16*>(k);
+  if (head_dim == 128)
+    quantize_insert_kernel<128><<<grid, 128, 0, as_stream(stream)>>>(
+        cache, page_size, page_stride_bytes, kp, k_stride, slot_mapping, num_tokens, rope_dim);
+  else
+    quantize_insert_kernel<512><<<grid, 128, 0, as_stream(stream)>>>(
+        cache, page_size, page_stride_bytes, kp, k_stride, slot_mapping, num_tokens, rope_dim);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_dequantize_gather_k(void* out, int64_t out_stride_req, int64_t out_stride_tok,
+                                       const uint8_t* cache, int32_t page_size,
+                                       int64_t page_stride_bytes, const int32_t* seq_lens,
+                                       const int32_t* gather_lens, const int32_t* block_table,
+                                       int64_t bt_stride, int32_t num_reqs, int32_t offset,
+                                       int32_t head_dim, int32_t rope_dim, void* stream) {
+  HCA_CHECK_ARG(num_reqs >= 0 && page_size > 0 && offset >= 0);
+  if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_reqs == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && cache && seq_lens && block_table);
+  dim3 grid(num_reqs, 32);
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  if (head_dim == 128)
+    dequant_gather_kernel<128><<<grid, 128, 0, as_stream(stream)>>>(
+        o, out_stride_req, out_stride_tok, cache, page_size, page_stride_bytes, seq_lens,
+        gather_lens, block_table, bt_stride, offset, rope_dim);
+  else
+    dequant_gather_kernel<512><<<grid, 128, 0, as_stream(stream)>>>(
+        o, out_stride_req, out_stride_tok, cache, page_size, page_stride_bytes, seq_lens,
+        gather_lens, block_table, bt_stride, offset, rope_dim);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_save_partial_states(float* state, int64_t state_stride_block,
+                                       int64_t state_stride_tok, const float* kv,
+                                       int64_t kv_stride, const float* score,
+                                       int64_t score_stride, const float* ape, int64_t ape_stride,
+                                       const int64_t* positions, const int64_t* slot_mapping,
+                                       int32_t num_tokens, int32_t block_size,
+                                       int32_t head_size, int32_t state_width,
+                                       int32_t compress_ratio, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && block_size > 0 && head_size > 0 &&
+                state_width >= head_size && compress_ratio > 0);
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(state && kv && score && ape && positions && slot_mapping);
+  save_partial_states_kernel<<<num_tokens, 128, 0, as_stream(stream)>>>(
+      state, state_stride_block, state_stride_tok, kv, kv_stride, score, score_stride, ape,
+      ape_stride, positions, slot_mapping, block_size, head_size, state_width, compress_ratio);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_compress_norm_rope_store(
+    const float* state, int64_t state_stride_block, int64_t state_stride_tok, int32_t state_width,
+    const int32_t* token_to_req, const int64_t* positions, const int64_t* state_slot_mapping,
+    const int32_t* block_table, int64_t bt_stride, int32_t block_size, const float* norm_weight,
+    float eps, const float* cos_sin, int64_t cos_sin_stride, uint8_t* kv_cache,
+    const int64_t* kv_slot_mapping, int32_t kv_page_size, int64_t kv_page_stride_bytes,
+    int32_t num_tokens, int32_t head_dim, int32_t rope_dim, int32_t compress_ratio,
+    void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && block_size > 0 && kv_page_size > 0 &&
+                state_width >= head_dim && compress_ratio > 0 && compress_ratio <= 512);
+  if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(state && token_to_req && positions && state_slot_mapping && block_table &&
+                norm_weight && cos_sin && kv_cache && kv_slot_mapping);
+  if (head_dim == 128)
+    compress_kernel<128><<<num_tokens, 128, 0, as_stream(stream)>>>(
+        state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
+        state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
+        cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,
+        compress_ratio);
+  else
+    compress_kernel<512><<<num_tokens, 512, 0, as_stream(stream)>>>(
+        state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
+        state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
+        cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,
+        compress_ratio);
+  return HCA_LAUNCH_STATUS();
+}

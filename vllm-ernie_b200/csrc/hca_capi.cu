@@ -1,0 +1,15 @@
+// Status strings and version of the libhca_b200 C ABI.
+#include "hca_common.cuh"
+
+extern "C" const char* hca_status_string(int status) {
+  switch (status) {
+    case HCA_OK: return "ok";
+    case HCA_E_INVALID: return "invalid argument (pointer, size, stride or alignment)";
+    case HCA_E_UNSUPPORTED: return "shape not instantiated in this build";
+    case HCA_E_CUDA: return "CUDA launch error";
+    case HCA_E_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int hca_version(void) { return 100; }

@@ -1,0 +1,168 @@
+// Shared device helpers of libhca_b200: status plumbing, bf16 / e4m3 /
+// UE8M0 conversions, GPT-J RoPE and the cached-row geometry.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "hca_b200.h"
+
+#define HCA_CHECK_ARG(cond)            \
+  do {                                 \
+    if (!(cond)) return HCA_E_INVALID; \
+  } while (0)
+
+#define HCA_LAUNCH_STATUS() (cudaGetLastError() == cudaSuccess ? HCA_OK : HCA_E_CUDA)
+
+namespace hca {
+
+constexpr float kFp8Max = 448.0f;
+constexpr int kQuantBlock = 64;  // NoPE quantisation block of the cached rows
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+
+// Geometry of one cached row: N fp8 bytes + R bf16, then N/64 + 1 scale bytes.
+struct RowGeom {
+  int nope, data_bytes, scale_bytes;
+};
+
+__host__ __device__ inline RowGeom row_geom(int head_dim, int rope_dim) {
+  RowGeom g;
+  g.nope = head_dim - rope_dim;
+  g.data_bytes = g.nope + 2 * rope_dim;
+  g.scale_bytes = g.nope / kQuantBlock + 1;
+  return g;
+}
+
+inline bool valid_geom(int head_dim, int rope_dim) {
+  return head_dim > rope_dim && rope_dim > 0 && rope_dim % 16 == 0 &&
+         (head_dim - rope_dim) % kQuantBlock == 0;
+}
+
+// Address of the data row and of the scale bytes of `slot` in a paged cache.
+struct RowPtr {
+  uint8_t* data;
+  uint8_t* scale;
+};
+
+__device__ __forceinline__ RowPtr row_ptr(uint8_t* cache, int64_t slot, int page_size,
+                                          int64_t page_stride, RowGeom g) {
+  const int64_t page = slot / page_size;
+  const int off = static_cast<int>(slot - page * page_size);
+  uint8_t* base = cache + page * page_stride;
+  RowPtr p;
+  p.data = base + static_cast<int64_t>(off) * g.data_bytes;
+  p.scale = base + static_cast<int64_t>(page_size) * g.data_bytes +
+            static_cast<int64_t>(off) * g.scale_bytes;
+  return p;
+}
+
+// ceil(log2(x)) of a positive finite float, exactly (from its bits).
+__device__ __forceinline__ int ceil_log2(float x) {
+  const uint32_t b = __float_as_uint(x);
+  const int e = static_cast<int>((b >> 23) & 0xff);
+  const uint32_t m = b & 0x7fffff;
+  if (e == 0) {  // subnormal: x = m * 2^-149
+    return (32 - __clz(static_cast<int>(m - 1))) - 149;
+  }
+  return (e - 127) + (m != 0 ? 1 : 0);
+}
+
+// UE8M0 exponent of a block with abs-max `amax`.  `divide` selects
+// amax / 448 (KV insert) vs amax * (1/448) (every other quantiser).
+__device__ __forceinline__ int ue8m0_exponent(float amax, float floor_v, bool divide) {
+  const float a = fmaxf(amax, floor_v);
+  const float raw = divide ? __fdiv_rn(a, kFp8Max) : __fmul_rn(a, 1.0f / kFp8Max);
+  return ceil_log2(raw);
+}
+
+__device__ __forceinline__ uint8_t encode_ue8m0(int e) {
+  int v = e + 127;
+  v = v < 0 ? 0 : (v > 255 ? 255 : v);
+  return static_cast<uint8_t>(v);
+}
+
+// 2^e as float for e in the normal range.
+__device__ __forceinline__ float exp2i(int e) {
+  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+// clamp(x, +-448) then round-to-nearest-even to e4m3.
+__device__ __forceinline__ uint8_t to_e4m3(float x) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t v) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Two e4m3 bytes (little endian in `v`) to float2.
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t v) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v), __NV_E4M3);
+  return __half22float2(__half2(h));
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float x) {
+  __nv_bfloat16 h = __float2bfloat16_rn(x);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024; `red` holds >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : -INFINITY;
+  t = warp_max(t);
+  return t;
+}
+
+// GPT-J rotation of one (even, odd) pair: forward uses +sin, inverse -sin.
+__device__ __forceinline__ void rope_pair(float& e, float& o, float c, float s) {
+  const float ne = e * c - o * s;
+  const float no = o * c + e * s;
+  e = ne;
+  o = no;
+}
+
+}  // namespace hca

@@ -1,0 +1,253 @@
+// Output side of the HCA path: VHA head post-mix fused with inverse RoPE and
+// the 1x128 UE8M0 FP8 quant that feeds the grouped wo_a einsum, the plain
+// inverse-RoPE quant, the bf16 (unquantised) variant, and the sigmoid gate
+// fused into wo_b's input quant.
+//
+// These kernels read the attention output once (T * H * D bf16) and write
+// it once as e4m3 -- HBM-bound.  The head mix is a [H x H] x [H x D] product
+// per token (H = 64: 0.5 MFLOP/token), done on CUDA cores from L1.
+#include "hca_common.cuh"
+
+namespace hca {
+namespace {
+
+// One CTA per token (padded to aligned_T rows), 8 warps; warp w handles
+// heads w, w + 8, ...; lane l owns dims [l*E, (l+1)*E).
+//   mode 0: VHA + inverse RoPE + FP8, per-head int32 scale (plugin layout)
+//   mode 1: inverse RoPE + FP8, packed int32 scale (vLLM layout), no mix
+//   mode 2: VHA + inverse RoPE, bf16 output
+template <int D, int MODE>
+__global__ void __launch_bounds__(256) vha_out_kernel(
+    uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_t ob_st, int64_t ob_sh,
+    const __nv_bfloat16* o, int64_t o_st, int64_t o_sh, const __nv_bfloat16* mix,
+    const int64_t* positions, const float* cos_sin, int64_t cs_stride, int num_tokens,
+    int aligned_t, int num_heads, int n_groups, int rope_dim) {
+  constexpr int E = D / 32;
+  constexpr int kChunks = D / 128;  // quant chunks per head
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = blockIdx.x;
+  const int hpg = num_heads / n_groups;
+  if (t >= num_tokens) {
+    // TMA-aligned padding rows of the scale buffer are zero.
+    if (MODE == 0) {
+      for (int h = threadIdx.x; h < num_heads; h += blockDim.x) {
+        const int g = h / hpg, hh = h % hpg;
+        scale[(static_cast<int64_t>(g) * hpg + hh) * aligned_t + t] = 0;
+      }
+    } else if (MODE == 1) {
+      const int packs = (hpg * kChunks + 3) / 4;
+      for (int i = threadIdx.x; i < n_groups * packs; i += blockDim.x)
+        scale[static_cast<int64_t>(i) * aligned_t + t] = 0;
+    }
+    return;
+  }
+  const float* cs = cos_sin + positions[t] * cs_stride;
+  const int nope = D - rope_dim;
+  const __nv_bfloat16* ot = o + t * o_st;
+  for (int h = warp; h < num_heads; h += 8) {
+    float y[E];
+    if (MODE == 1 || mix == nullptr) {
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(ot + h * o_sh) + lane * E;
+#pragma unroll
+      for (int i = 0; i < E; ++i) y[i] = bf16_bits_to_float(src[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) y[i] = 0.0f;
+      const __nv_bfloat16* mrow = mix + static_cast<int64_t>(h) * num_heads;
+      for (int gh = 0; gh < num_heads; ++gh) {
+        const float m = __bfloat162float(mrow[gh]);
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(ot + gh * o_sh) + lane * E;
+#pragma unroll
+        for (int i = 0; i < E; ++i) y[i] = fmaf(m, bf16_bits_to_float(src[i]), y[i]);
+      }
+    }
+    // inverse GPT-J RoPE of the last R dims (pairs never straddle lanes)
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+      const int d = lane * E + i;
+      if (d >= nope) {
+        const int pr = (d - nope) >> 1;
+        const float c = cs[pr], s = cs[rope_dim / 2 + pr];
+        const float e = y[i], od = y[i + 1];
+        y[i] = e * c + od * s;
+        y[i + 1] = od * c - e * s;
+      }
+    }
+    if (MODE == 2) {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(out_bf16 + t * ob_st + h * ob_sh) + lane * E;
+#pragma unroll
+      for (int i = 0; i < E; ++i) dst[i] = float_to_bf16_bits(y[i]);
+      continue;
+    }
+    // per-128 amax: 128 / E lanes share a chunk
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(y[i]));
+#pragma unroll
+    for (int off = 1; off < 128 / E; off <<= 1)
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const int e = ue8m0_exponent(amax, 1e-10f, false);
+    const float inv = exp2i(-e);
+    const int g = h / hpg, hh = h % hpg;
+    uint8_t* dst = out_fp8 + (static_cast<int64_t>(g) * num_tokens + t) * (hpg * D) + hh * D + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = to_e4m3(y[i] * inv);
+    // exponent byte of chunk k lives in lane k * (128 / E)
+    uint32_t packed = 0;
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int ek = __shfl_sync(0xffffffffu, e, k * (128 / E));
+      packed |= static_cast<uint32_t>(encode_ue8m0(ek)) << (8 * k);
+    }
+    if (lane == 0) {
+      if (MODE == 0) {
+        scale[(static_cast<int64_t>(g) * hpg + hh) * aligned_t + t] = static_cast<int32_t>(packed);
+      } else {
+        // chunk index within the group = hh * kChunks + k; pack = idx / 4
+        if (kChunks == 4) {
+          scale[(static_cast<int64_t>(g) * ((hpg * kChunks + 3) / 4) + hh) * aligned_t + t] =
+              static_cast<int32_t>(packed);
+        } else {
+          const int idx = hh * kChunks;
+          unsigned char* b = reinterpret_cast<unsigned char*>(
+              scale + (static_cast<int64_t>(g) * ((hpg * kChunks + 3) / 4) + idx / 4) * aligned_t + t);
+          b[idx % 4] = static_cast<unsigned char>(packed & 0xff);
+        }
+      }
+    }
+  }
+}
+
+// x * sigmoid(gate) -> 1x128 FP8; one CTA of 128 threads per (512-col pack, row).
+__global__ void __launch_bounds__(128) sigmoid_mul_quant_kernel(
+    uint8_t* out, int32_t* scale, const __nv_bfloat16* x, int64_t x_stride,
+    const __nv_bfloat16* gate, int64_t g_stride, int rows, int hidden, int aligned_rows) {
+  __shared__ int exps[4];
+  const int pack = blockIdx.x;
+  const int64_t r = blockIdx.y;
+  const int col = pack * 512 + threadIdx.x * 4;
+  float y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float gv = __bfloat162float(gate[r * g_stride + col + i]);
+    const float s = bf16_round(1.0f / (1.0f + expf(-gv)));
+    y[i] = bf16_round(__bfloat162float(x[r * x_stride + col + i]) * s);
+  }
+  float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+  amax = warp_max(amax);
+  const int e = ue8m0_exponent(amax, 1e-10f, false);
+  const float inv = exp2i(-e);
+  uint32_t q = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q |= static_cast<uint32_t>(to_e4m3(y[i] * inv)) << (8 * i);
+  *reinterpret_cast<uint32_t*>(out + r * hidden + col) = q;
+  if ((threadIdx.x & 31) == 0) exps[threadIdx.x >> 5] = e;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) packed |= static_cast<uint32_t>(exps[k] + 127) << (8 * k);
+    scale[static_cast<int64_t>(pack) * aligned_rows + r] = static_cast<int32_t>(packed);
+  }
+}
+
+template <int MODE>
+int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_t ob_st,
+               int64_t ob_sh, const void* o, int64_t o_st, int64_t o_sh, const void* mix,
+               const int64_t* positions, const float* cos_sin, int64_t cs_stride, int num_tokens,
+               int num_heads, int n_groups, int head_dim, int rope_dim, cudaStream_t s) {
+  const int aligned = MODE == 2 ? num_tokens : (num_tokens + 3) / 4 * 4;
+  if (aligned == 0) return HCA_OK;
+  auto* op = static_cast<const __nv_bfloat16*>(o);
+  auto* mp = static_cast<const __nv_bfloat16*>(mix);
+  if (head_dim == 128)
+    vha_out_kernel<128, MODE><<<aligned, 256, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op,
+                                                      o_st, o_sh, mp, positions, cos_sin,
+                                                      cs_stride, num_tokens, aligned, num_heads,
+                                                      n_groups, rope_dim);
+  else
+    vha_out_kernel<512, MODE><<<aligned, 256, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op,
+                                                      o_st, o_sh, mp, positions, cos_sin,
+                                                      cs_stride, num_tokens, aligned, num_heads,
+                                                      n_groups, rope_dim);
+  return HCA_LAUNCH_STATUS();
+}
+
+bool out_geom_ok(int head_dim, int rope_dim) {
+  return (head_dim == 128 || head_dim == 512) && valid_geom(head_dim, rope_dim) &&
+         // the RoPE tail must sit inside the last 128-chunk (fused_inv_rope_fp8_quant.py:170)
+         rope_dim <= 128;
+}
+
+}  // namespace
+}  // namespace hca
+
+using namespace hca;
+
+extern "C" int hca_vha_inv_rope_fp8_quant(uint8_t* out, int32_t* scale, const void* o,
+                                          int64_t o_stride_tok, int64_t o_stride_head,
+                                          const void* mix, const int64_t* positions,
+                                          const float* cos_sin, int64_t cos_sin_stride,
+                                          int32_t num_tokens, int32_t num_heads,
+                                          int32_t n_groups, int32_t head_dim, int32_t rope_dim,
+                                          void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && num_heads > 0 && n_groups > 0 && num_heads % n_groups == 0);
+  if (!out_geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && scale && o && mix && positions && cos_sin);
+  return launch_vha<0>(out, scale, nullptr, 0, 0, o, o_stride_tok, o_stride_head, mix, positions,
+                       cos_sin, cos_sin_stride, num_tokens, num_heads, n_groups, head_dim,
+                       rope_dim, as_stream(stream));
+}
+
+extern "C" int hca_inv_rope_fp8_quant(uint8_t* out, int32_t* scale, const void* o,
+                                      int64_t o_stride_tok, int64_t o_stride_head,
+                                      const int64_t* positions, const float* cos_sin,
+                                      int64_t cos_sin_stride, int32_t num_tokens,
+                                      int32_t num_heads, int32_t n_groups, int32_t head_dim,
+                                      int32_t rope_dim, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && num_heads > 0 && n_groups > 0 && num_heads % n_groups == 0);
+  if (!out_geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && scale && o && positions && cos_sin);
+  if (head_dim == 128) {
+    // bytes of a pack are written by different warps: clear the packs first
+    const int hpg = num_heads / n_groups;
+    const int packs = (hpg + 3) / 4;
+    const int aligned = (num_tokens + 3) / 4 * 4;
+    if (cudaMemsetAsync(scale, 0, sizeof(int32_t) * static_cast<size_t>(n_groups) * packs * aligned,
+                        as_stream(stream)) != cudaSuccess)
+      return HCA_E_CUDA;
+  }
+  return launch_vha<1>(out, scale, nullptr, 0, 0, o, o_stride_tok, o_stride_head, nullptr,
+                       positions, cos_sin, cos_sin_stride, num_tokens, num_heads, n_groups,
+                       head_dim, rope_dim, as_stream(stream));
+}
+
+extern "C" int hca_vha_inv_rope(void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                                const void* o, int64_t o_stride_tok, int64_t o_stride_head,
+                                const void* mix, const int64_t* positions, const float* cos_sin,
+                                int64_t cos_sin_stride, int32_t num_tokens, int32_t num_heads,
+                                int32_t head_dim, int32_t rope_dim, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && num_heads > 0);
+  if (!out_geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && o && positions && cos_sin);
+  return launch_vha<2>(nullptr, nullptr, static_cast<__nv_bfloat16*>(out), out_stride_tok,
+                       out_stride_head, o, o_stride_tok, o_stride_head, mix, positions, cos_sin,
+                       cos_sin_stride, num_tokens, num_heads, 1, head_dim, rope_dim,
+                       as_stream(stream));
+}
+
+extern "C" int hca_sigmoid_mul_quant_fp8(uint8_t* out, int32_t* scale, const void* x,
+                                         int64_t x_stride, const void* gate, int64_t gate_stride,
+                                         int32_t rows, int32_t hidden, void* stream) {
+  HCA_CHECK_ARG(rows >= 0 && hidden > 0 && hidden % 512 == 0);
+  if (rows == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && scale && x && gate);
+  const int aligned = (rows + 3) / 4 * 4;
+  sigmoid_mul_quant_kernel<<<dim3(hidden / 512, rows), 128, 0, as_stream(stream)>>>(
+      out, scale, static_cast<const __nv_bfloat16*>(x), x_stride,
+      static_cast<const __nv_bfloat16*>(gate), gate_stride, rows, hidden, aligned);
+  return HCA_LAUNCH_STATUS();
+}

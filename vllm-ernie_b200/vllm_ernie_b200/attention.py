@@ -1,0 +1,341 @@
+"""The ERNIE 5.5 HCA attention module, as the model code calls it.
+
+Mirrors the plugin's module API (``E/nvidia/attention.py``):
+
+* ``select_ernie5_5_hca_cls(kv_cache_dtype)`` (``:554-558``) returns the
+  fp8 (``fp8_ds_mla``) HCA class;
+* ``Ernie5_5HCAAttention(vllm_config, prefix, topk_indices_buffer=None,
+  aux_stream_list=None)`` owns the parameters under the names the checkpoint
+  mapper fills (``E/nvidia/model.py:656-704``) and exposes
+  ``forward(positions, hidden_states, llama_4_scaling=None) -> [T, hidden]``
+  (``:471-539``) reading per-step metadata from the forward context under
+  ``{prefix}``, ``{prefix}.swa_cache`` and ``{prefix}.compressor.state_cache``;
+* ``VHAPostMix`` / ``fold_vha`` (``:121-163``) including the TP branch
+  (``o + V all_reduce(U^T o)`` in fp32 over this rank's heads).
+
+The attention-side work is the library's CUDA kernels; the projections
+(``fused_wqa_wkv``, ``wq_b``, compressor ``kv_score``, ``o_gate``, grouped
+``wo_a``, gated ``wo_b``) are plain torch/cuBLAS GEMMs, bf16 ``wo_a``
+(block-FP8 checkpoints are dequantised at load).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from types import SimpleNamespace
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import ops
+from .backend import HCACacheSpec, hca_kv_cache_specs
+from .cache_layout import SWA_BLOCK_SIZE, STATE_BLOCK_SIZE, compressed_page_size
+from .forward_context import get_forward_context
+
+VHA_RANK = 16
+
+
+@dataclass
+class Ernie5_5HCAConfig:
+    """The HCA fields of ``Ernie5_5Config`` (``E/config.py:14-102``), same
+    names and defaults."""
+
+    hidden_size: int = 4096
+    num_hidden_layers: int = 43
+    num_attention_heads: int = 64
+    num_key_value_heads: int = 1
+    head_dim: int = 512
+    q_lora_rank: int = 1024
+    qk_rope_head_dim: int = 64
+    o_groups: int = 8
+    o_lora_rank: int = 1024
+    sliding_window: int = 128
+    compress_ratios: list[int] | None = None
+    hybrid_mla_num_attention_heads: int = 64
+    max_position_embeddings: int = 200192
+    rope_theta: float = 2500000.0
+    compress_rope_theta: float = 160000.0
+    rms_norm_eps: float = 1e-6
+    num_nextn_predict_layers: int = 1
+    rope_parameters: dict = field(default_factory=lambda: {"rope_type": "default"})
+
+    def __post_init__(self):
+        if self.compress_ratios is None:
+            self.compress_ratios = [128] * (self.num_hidden_layers + self.num_nextn_predict_layers)
+
+    def is_dsa_layer(self, layer_id: int) -> bool:
+        return layer_id < len(self.compress_ratios) and self.compress_ratios[layer_id] <= 0
+
+
+def make_vllm_config(hf_config: Any, max_model_len: int = 131072, max_num_batched_tokens: int = 8192,
+                     kv_cache_dtype: str = "fp8", num_speculative_tokens: int = 0) -> SimpleNamespace:
+    """A duck-typed stand-in for the ``VllmConfig`` fields the module reads."""
+    spec = SimpleNamespace(num_speculative_tokens=num_speculative_tokens) if num_speculative_tokens else None
+    return SimpleNamespace(
+        model_config=SimpleNamespace(hf_config=hf_config, max_model_len=max_model_len),
+        cache_config=SimpleNamespace(cache_dtype=kv_cache_dtype, block_size=256),
+        scheduler_config=SimpleNamespace(max_num_batched_tokens=max_num_batched_tokens),
+        speculative_config=spec, quant_config=None)
+
+
+def _tp(group) -> tuple[int, int]:
+    if group is None or not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _check_attn_tp(config: Any, tp_size: int) -> None:
+    """TP must divide ``o_groups`` and the head counts (``E/nvidia/attention.py:111-118``)."""
+    for name in ("o_groups", "num_attention_heads", "hybrid_mla_num_attention_heads"):
+        if getattr(config, name) % tp_size:
+            raise ValueError(
+                f"ERNIE 5.5 attention TP size {tp_size} must divide {name}={getattr(config, name)}.")
+
+
+class VHAPostMix(nn.Module):
+    """Head mixing ``o[h] <- sum_g m[h, g] o[g]`` with ``m = I + V U^T``
+    (``E/nvidia/attention.py:121-157``)."""
+
+    def __init__(self, num_heads: int, rank: int = VHA_RANK, tp_group=None):
+        super().__init__()
+        self.tp_group = tp_group
+        self.tp_size, self.tp_rank = _tp(tp_group)
+        local = num_heads // self.tp_size
+        self.U = nn.Parameter(torch.zeros(local, rank), requires_grad=False)
+        self.V = nn.Parameter(torch.zeros(local, rank), requires_grad=False)
+        if self.tp_size == 1:
+            self.register_buffer("m", torch.eye(num_heads), persistent=False)
+
+    def load_local_heads(self, param: nn.Parameter, loaded: torch.Tensor) -> None:
+        rows = param.shape[0]
+        param.data.copy_(loaded[self.tp_rank * rows:(self.tp_rank + 1) * rows])
+
+    def fold(self) -> None:
+        """Idempotent, in place (graph-stable address)."""
+        if self.tp_size != 1:
+            return
+        eye = torch.eye(self.U.shape[0], dtype=self.U.dtype, device=self.U.device)
+        self.m.copy_(torch.addmm(eye, self.V, self.U.t()))
+
+    def forward(self, o: torch.Tensor) -> torch.Tensor:
+        if self.tp_size == 1:
+            return torch.matmul(self.m.to(o.dtype), o)
+        t = o.shape[0]
+        u = self.U.t().to(o.dtype).expand(t, -1, -1)
+        z = torch.bmm(u.float(), o.float())
+        dist.all_reduce(z, group=self.tp_group)
+        v = self.V.float().expand(t, -1, -1)
+        return torch.bmm(v, z).add_(o.float()).to(o.dtype)
+
+
+def fold_vha(model: nn.Module) -> None:
+    for m in model.modules():
+        if isinstance(m, VHAPostMix):
+            m.fold()
+
+
+class _Linear(nn.Module):
+    def __init__(self, in_features: int, out_features: int, dtype):
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(out_features, in_features, dtype=dtype), requires_grad=False)
+
+    def forward(self, x):
+        return x @ self.weight.t()
+
+
+class _RMSNorm(nn.Module):
+    def __init__(self, n: int, dtype):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(n, dtype=dtype), requires_grad=False)
+
+
+class _Compressor(nn.Module):
+    """Parameters of ``DeepseekCompressor`` (``V/models/deepseek_v4/compressor.py:212-235``)."""
+
+    def __init__(self, hidden: int, head_dim: int, ratio: int, dtype, prefix: str):
+        super().__init__()
+        self.compress_ratio = ratio
+        self.head_dim = head_dim
+        self.ape = nn.Parameter(torch.zeros(ratio, head_dim, dtype=torch.float32), requires_grad=False)
+        self.fused_wkv_wgate = _Linear(hidden, 2 * head_dim, dtype)
+        self.norm = _RMSNorm(head_dim, torch.float32)
+        self.state_cache_prefix = f"{prefix}.state_cache"
+
+
+class Ernie5_5HCAAttention(nn.Module):
+    """One HCA layer on the fp8 ``fp8_ds_mla`` cache (replaces
+    ``Ernie5_5HCAFlashMLAAttention``, ``E/nvidia/attention.py:548-551``)."""
+
+    def __init__(self, vllm_config: Any, prefix: str, topk_indices_buffer=None,
+                 aux_stream_list: list | None = None, tp_group=None, dtype=torch.bfloat16):
+        super().__init__()
+        cfg = vllm_config.model_config.hf_config
+        self.tp_group = tp_group
+        tp_size, self.tp_rank = _tp(tp_group)
+        _check_attn_tp(cfg, tp_size)
+        self.prefix = prefix
+        self.layer_name = f"{prefix}.deepseek_v4_multi_head_latent_attention"
+        self.hidden_size = cfg.hidden_size
+        self.n_heads = cfg.num_attention_heads
+        self.n_local_heads = self.n_heads // tp_size
+        self.head_dim = cfg.head_dim
+        self.rope_head_dim = cfg.qk_rope_head_dim
+        self.nope_head_dim = self.head_dim - self.rope_head_dim
+        self.q_lora_rank = cfg.q_lora_rank
+        self.o_lora_rank = cfg.o_lora_rank
+        self.n_groups = cfg.o_groups
+        self.n_local_groups = self.n_groups // tp_size
+        self.window_size = cfg.sliding_window
+        self.eps = cfg.rms_norm_eps
+        layer_id = _layer_index(prefix)
+        ratios = cfg.compress_ratios
+        self.compress_ratio = max(1, ratios[layer_id]) if layer_id < cfg.num_hidden_layers else 1
+        if self.compress_ratio != 128:
+            raise ValueError(f"{prefix}: HCA layers compress 128 tokens per entry, got {self.compress_ratio}")
+        self.scale = self.head_dim ** -0.5
+        self.padded_heads = self.n_local_heads  # no head padding (FlashMLA pads to 64/128)
+        self.aux_stream_list = aux_stream_list
+        self.max_model_len = vllm_config.model_config.max_model_len
+
+        self.fused_wqa_wkv = _Linear(self.hidden_size, self.q_lora_rank + self.head_dim, dtype)
+        self.q_norm = _RMSNorm(self.q_lora_rank, dtype)
+        self.wq_b = _Linear(self.q_lora_rank, self.n_local_heads * self.head_dim, dtype)
+        self.kv_norm = _RMSNorm(self.head_dim, dtype)
+        self.wo_a = _Linear(self.n_heads * self.head_dim // self.n_groups, self.n_local_groups * self.o_lora_rank, dtype)
+        self.wo_b = _Linear(self.n_local_groups * self.o_lora_rank, self.hidden_size, dtype)
+        self.o_gate = _Linear(self.q_lora_rank, self.n_local_groups * self.o_lora_rank, dtype)
+        self.vha = VHAPostMix(self.n_heads, tp_group=tp_group)
+        self.attn_sink = nn.Parameter(torch.full((max(self.n_local_heads, 64),), -float("inf")),
+                                      requires_grad=False)
+        self.compressor = _Compressor(self.hidden_size, self.head_dim, self.compress_ratio, dtype,
+                                      f"{prefix}.compressor")
+        theta = cfg.compress_rope_theta
+        inv = 1.0 / (theta ** (torch.arange(0, self.rope_head_dim, 2, dtype=torch.float) / self.rope_head_dim))
+        t = torch.arange(min(cfg.max_position_embeddings, self.max_model_len + 1), dtype=torch.float)
+        f = torch.outer(t, inv)
+        self.register_buffer("cos_sin_cache", torch.cat([f.cos(), f.sin()], -1), persistent=False)
+        # caches are bound by the engine (bind_kv_cache)
+        self.swa_cache = torch.tensor([])
+        self.kv_cache = torch.tensor([])
+        self.state_cache = torch.tensor([])
+        self.comp_page = compressed_page_size(self.compress_ratio)
+
+    # -- engine-facing -----------------------------------------------------
+    def get_kv_cache_spec(self) -> dict[str, HCACacheSpec]:
+        return hca_kv_cache_specs(self.head_dim, self.rope_head_dim, self.window_size, self.compress_ratio)
+
+    def bind_kv_cache(self, swa_cache: torch.Tensor, kv_cache: torch.Tensor, state_cache: torch.Tensor) -> None:
+        """``swa_cache``/``kv_cache``: uint8 ``[pages, ...]`` (page stride =
+        ``stride(0)`` bytes); ``state_cache``: fp32 ``[pages, 8, 2 * D]``."""
+        self.swa_cache, self.kv_cache, self.state_cache = swa_cache, kv_cache, state_cache
+
+    def process_weights_after_loading(self) -> None:
+        self.vha.fold()
+
+    # -- forward -----------------------------------------------------------
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor,
+                llama_4_scaling: torch.Tensor | None = None) -> torch.Tensor:
+        T = hidden_states.shape[0]
+        d, r = self.head_dim, self.rope_head_dim
+        qr_kv = self.fused_wqa_wkv(hidden_states)
+        kv_score = hidden_states.float() @ self.compressor.fused_wkv_wgate.weight.float().t()
+        qr, kv = qr_kv.split([self.q_lora_rank, d], dim=-1)
+        qr, kv = ops.fused_q_kv_rmsnorm(qr, kv, self.q_norm.weight, self.kv_norm.weight, self.eps)
+        q = self.wq_b(qr).view(T, self.n_local_heads, d)
+        gate = torch.sigmoid(self.o_gate(qr))
+        attn_metadata = get_forward_context().attn_metadata
+        o = torch.empty((T, self.n_local_heads, d), dtype=hidden_states.dtype, device=hidden_states.device)
+        if not isinstance(attn_metadata, dict):  # profile / dummy run
+            o.zero_()
+        else:
+            self._attention(q, kv, kv_score, positions, o, attn_metadata)
+        return self._output(o, positions, gate)
+
+    def _attention(self, q, kv, kv_score, positions, o, md: dict) -> None:
+        d, r = self.head_dim, self.rope_head_dim
+        swa = md[f"{self.prefix}.swa_cache"]
+        c128 = md[self.prefix]
+        comp = md[self.compressor.state_cache_prefix]
+        n = swa.slot_mapping.shape[0]
+        qp = ops.fused_qnorm_rope_kv_insert(q, kv, self.swa_cache, swa.slot_mapping, positions, self.cos_sin_cache,
+                                            self.padded_heads, self.eps, SWA_BLOCK_SIZE, r)
+        ops.save_partial_states(kv_score[:, :d], kv_score[:, d:], self.compressor.ape, positions,
+                                self.state_cache, comp.slot_mapping, STATE_BLOCK_SIZE, d, self.compress_ratio)
+        ops.compress_norm_rope_store(self.state_cache, n, comp.token_to_req_indices, positions, comp.slot_mapping,
+                                     comp.block_table, STATE_BLOCK_SIZE, d, self.cos_sin_cache, self.kv_cache,
+                                     c128.slot_mapping, self.comp_page, d, r, self.compress_ratio,
+                                     self.compressor.norm.weight, self.eps)
+        ndt, nd = swa.num_decode_tokens, swa.num_decodes
+        sink = self.attn_sink[: self.n_local_heads].contiguous()
+        if ndt:
+            ops.sparse_decode(qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,
+                              self.kv_cache, self.comp_page, c128.c128a_global_decode_topk_indices,
+                              c128.c128a_decode_topk_lens, self.scale, sink, out=o[:ndt],
+                              group_starts=swa.decode_group_starts, max_group_tokens=swa.decode_max_group_tokens,
+                              num_splits=c128.num_splits, rope_dim=r)
+        if swa.num_prefills:
+            qsl = swa.query_start_loc[nd:] - ndt
+            ops.sparse_prefill(qp[ndt:n], qsl, swa.seq_lens[nd:], self.swa_cache, SWA_BLOCK_SIZE,
+                               swa.block_table[nd:], self.kv_cache, self.comp_page, c128.block_table[nd:],
+                               self.window_size, self.compress_ratio, self.scale, sink, out=o[ndt:n], rope_dim=r)
+
+    def _output(self, o, positions, gate):
+        T = o.shape[0]
+        if self.vha.tp_size == 1:
+            o = ops.vha_inv_rope(o, self.vha.m.to(o.dtype), positions, self.cos_sin_cache, self.rope_head_dim)
+        else:
+            o = ops.vha_inv_rope(self.vha(o), None, positions, self.cos_sin_cache, self.rope_head_dim)
+        og = o.view(T, self.n_local_groups, -1).transpose(0, 1)            # [G, T, HPG*D]
+        wa = self.wo_a.weight.view(self.n_local_groups, self.o_lora_rank, -1)  # [G, o_lora, HPG*D]
+        z = torch.bmm(og, wa.transpose(1, 2)).transpose(0, 1).reshape(T, -1)  # [T, G*o_lora]
+        y = self.wo_b(z * gate)
+        if self.tp_group is not None and self.vha.tp_size > 1:
+            dist.all_reduce(y, group=self.tp_group)
+        return y
+
+    # -- weights -----------------------------------------------------------
+    def load_weights(self, weights) -> set[str]:
+        """Load already-mapped names (``E/nvidia/model.py:656-704``); stacked
+        shards arrive as ``(name, tensor, shard_id)``."""
+        params = dict(self.named_parameters())
+        loaded = set()
+        for item in weights:
+            name, w = item[0], item[1]
+            shard = item[2] if len(item) > 2 else None
+            p = params[name]
+            if name in ("vha.U", "vha.V"):
+                self.vha.load_local_heads(p, w)
+            elif name == "attn_sink":
+                p.data[: self.n_local_heads].copy_(w[self.tp_rank * self.n_local_heads:(self.tp_rank + 1) * self.n_local_heads])
+            elif shard is not None:
+                sizes = {"fused_wqa_wkv.weight": [self.q_lora_rank, self.head_dim],
+                         "compressor.fused_wkv_wgate.weight": [self.head_dim, self.head_dim]}[name]
+                off = sum(sizes[:shard])
+                p.data[off:off + sizes[shard]].copy_(w)
+            elif name in ("wq_b.weight", "wo_a.weight", "o_gate.weight"):
+                rows = p.shape[0]
+                p.data.copy_(w[self.tp_rank * rows:(self.tp_rank + 1) * rows])
+            elif name == "wo_b.weight":
+                cols = p.shape[1]
+                p.data.copy_(w[:, self.tp_rank * cols:(self.tp_rank + 1) * cols])
+            else:
+                p.data.copy_(w)
+            loaded.add(name)
+        return loaded
+
+
+def _layer_index(prefix: str) -> int:
+    for part in prefix.split("."):
+        if part.isdigit():
+            return int(part)
+    return 0
+
+
+def select_ernie5_5_hca_cls(kv_cache_dtype: str) -> type[nn.Module]:
+    """fp8 KV caches take this path (``E/nvidia/attention.py:554-558``);
+    the bf16 FlashInfer variant is not part of this build."""
+    if kv_cache_dtype.startswith("fp8"):
+        return Ernie5_5HCAAttention
+    raise ValueError(f"HCA on B200 stores fp8_ds_mla caches; kv_cache_dtype={kv_cache_dtype!r} is not supported")
