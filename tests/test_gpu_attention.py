@@ -24,6 +24,8 @@ MAX_ABS, MAX_REL_L2 = 2e-2, 5e-3
 
 
 def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_REL_L2):
+    assert np.isfinite(ref).all(), f"oracle non-finite at {np.argwhere(~np.isfinite(ref))[:8].tolist()}"
+    assert np.isfinite(got).all(), f"kernel non-finite at {np.argwhere(~np.isfinite(got))[:8].tolist()}"
     err = np.abs(got.astype(np.float64) - ref)
     rel = np.linalg.norm(got.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30)
     assert err.max() <= max_abs, (err.max(), rel)
@@ -76,6 +78,7 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
                           dl if comp else None, 128 ** -0.5,
                           sink.cpu().numpy() if sink is not None else None, 128, 64)
     check_close(out.float().cpu().numpy(), ref)
+    assert ops.device_error() == 0
     return out
 
 

@@ -17,6 +17,7 @@
 // accumulate), softmax online in base 2.  Decode splits a group's rows
 // across CTAs (split-K) and the last CTA to finish combines the partials.
 #include "hca_common.cuh"
+#include "hca_tc.cuh"
 
 namespace hca {
 namespace {
@@ -553,12 +554,545 @@ __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnPa
   }
 }
 
+// ============================================================================
+// tcgen05 decode kernel (head_dim 128 = 64 e4m3 NoPE + 64 bf16 RoPE)
+//
+// One CTA per (group, split); up to 256 query rows = two M=128 tiles.
+//   warps 0-7  softmax: tile t = warp / 4, TMEM lane quadrant = warp % 4,
+//              one thread per query row (S row read from TMEM, P written back)
+//   warp  8    MMA issuer (lane 0) + TMEM owner
+//   warp  9    loader: row slots from the index tables, one cp.async.bulk per
+//              192-byte row into a 4-stage raw ring (mbarrier tx completion)
+//   warps 10-13 dequant: e4m3 x UE8M0 -> bf16 into the 128B-swizzled K tile
+// S = Q K^T: M=128, N=64, K=128 (8 x K16), Q and K tile K-major in smem.
+// O += P V: M=128, N=128, K=64 (4 x K16), P from TMEM, V = the same K tile
+// read MN-major.  TMEM: O tiles at columns 0 / 128, S/P double-buffered at
+// 256 + (tile * 2 + buf) * 64.  Softmax runs in base 2 with the row max
+// raised lazily (O is rescaled only when the max grows by more than 2^8).
+// Every mbarrier wait is bounded; a timeout sets the device error word.
+// ============================================================================
+namespace tcd {
+constexpr int kD = 128;
+constexpr int kNope = 64;
+constexpr int kRowBytes = 192;  // kNope e4m3 + 64 bf16
+constexpr int kCh = 64;         // KV rows per step
+constexpr int kStages = 4;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr int kDqWarp0 = 10;
+constexpr int kDqWarps = 4;
+constexpr int kThreads = 14 * 32;
+constexpr int kMaxRows = 256;
+constexpr int kQTile = 2 * 128 * 128;          // two 64-column regions of 128 rows x 128 B
+constexpr int kQRegion = 128 * 128;
+constexpr int kQOff = 0;
+constexpr int kKBufs = 2;                      // bf16 K-tile ring: dequant runs ahead of the MMAs
+constexpr int kKOff = kQOff + 2 * kQTile;      // 65536
+constexpr int kKRegion = kCh * 128;            // 8192
+constexpr int kKBuf = 2 * kKRegion;            // 16384
+constexpr int kRawOff = kKOff + kKBufs * kKBuf;
+constexpr int kRawStage = kCh * kRowBytes;     // 12288
+constexpr int kScaleOff = kRawOff + kStages * kRawStage;  // byte index of the scale in its block
+constexpr int kSBlkOff = kScaleOff + kStages * kCh;        // [stage][row] 16-byte scale blocks
+constexpr int kMaskOff = kSBlkOff + kStages * kCh * 16;
+constexpr int kKMaskOff = kMaskOff + kStages * kCh * 4;
+constexpr int kBarOff = kKMaskOff + kKBufs * kCh * 4;
+// raw_full[4] raw_empty[4] k_full[kKBufs] k_empty[kKBufs] s_full[2] p_full[2] pv_done[2] q_full
+constexpr int kNumBars = 2 * kStages + 2 * kKBufs + 7;
+constexpr int kMiscOff = kBarOff + kNumBars * 8;
+constexpr int kTokOff = kMiscOff + 64;  // [32] + [32] ints
+constexpr int kSmemBytes = kTokOff + 256 + 1024;  // + 1024 alignment slack
+constexpr int kQWarps = 9;  // softmax warps + MMA warp load Q
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOkBit = 1u << 31;
+
+__device__ __forceinline__ uint32_t s_col(int tile, int buf) { return 256u + (tile * 2 + buf) * 64u; }
+
+// Query row held by TMEM lane / smem row `rit` of M-tile `tile`, or -1: a
+// tile with R valid rows puts q = ceil(R / 4) of them at the start of each
+// 32-lane quadrant.
+__device__ __forceinline__ int tile_row_to_query(int tile, int rit, int rows_q) {
+  const int R = min(128, rows_q - tile * 128);
+  if (R <= 0) return -1;
+  const int q = (R + 3) >> 2;
+  const int quad = rit >> 5, ln = rit & 31;
+  const int local = quad * q + ln;
+  return (ln < q && local < R) ? tile * 128 + local : -1;
+}
+
+__device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
+  *s_err = 1;
+  if (err) atomicOr(err, code);
+}
+}  // namespace tcd
+
+__global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const AttnParams P, int* err) {
+  using namespace tcd;
+  using namespace tc;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+
+  const int gidx = blockIdx.y, split = blockIdx.x;
+  Group G;
+  if (!resolve_group<false>(P, gidx, G)) return;
+  const int H = P.num_heads;
+  const int rows_q = G.ntok * H;
+  if (rows_q > kMaxRows || rows_q > P.max_rows) return;
+  const int ntiles = (rows_q + 127) / 128;
+  const int n_u = G.n_win + G.n_comp;
+  const int nchunks = (n_u + kCh - 1) / kCh;
+  const int c_begin = static_cast<int>((static_cast<int64_t>(split) * nchunks) / P.num_splits);
+  const int c_end = static_cast<int>((static_cast<int64_t>(split + 1) * nchunks) / P.num_splits);
+  const int n = c_end - c_begin;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + 4;
+  uint64_t* k_full = bars + 8;
+  uint64_t* k_empty = bars + 10;
+  uint64_t* s_full = bars + 12;
+  uint64_t* p_full = bars + 14;
+  uint64_t* pv_done = bars + 16;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kMiscOff);  // [0] tmem, [1] err, [2] consumed
+  uint8_t* scale_s = smem + kScaleOff;
+  uint32_t* mask_s = reinterpret_cast<uint32_t*>(smem + kMaskOff);
+  uint32_t* kmask = reinterpret_cast<uint32_t*>(smem + kKMaskOff);
+
+  int* tok_len = reinterpret_cast<int*>(smem + kTokOff);  // [32] window length per token
+  int* tok_clen = tok_len + 32;                             // [32] compressed length per token
+  uint64_t* q_full = bars + 18;
+
+  if (warp == kMmaWarp) {
+    tmem_alloc(misc, kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(raw_full + s, 32 + 1);  // 32 cp.async completions + the mask arrival
+      mbar_init(raw_empty + s, kDqWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(k_full + b, kDqWarps);
+      mbar_init(k_empty + b, 1);
+      mbar_init(s_full + b, 1);
+      mbar_init(p_full + b, 4 * ntiles);
+      mbar_init(pv_done + b, 1);
+    }
+    mbar_init(q_full, kQWarps);
+    misc[1] = 0;
+    misc[2] = 0;
+    mbar_fence_init();
+  }
+  if (threadIdx.x < G.ntok) {
+    tok_len[threadIdx.x] = P.swa_lens[G.t0 + threadIdx.x];
+    tok_clen[threadIdx.x] = P.comp_cache ? P.comp_lens[G.t0 + threadIdx.x] : 0;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+  int issued = 0;
+
+  if (warp < kSoftmaxWarps || warp == kMmaWarp) {
+    // Q rows -> two K-major 128B-swizzled M=128 tiles (rows past rows_q zero),
+    // loaded by the softmax and MMA warps while the loader already streams KV.
+    // A tile with R < 128 query rows spreads them evenly over the four TMEM
+    // lane quadrants (q = ceil(R / 4) rows each) so every SM sub-partition
+    // runs the same softmax load.
+    const int qt = warp < kSoftmaxWarps ? threadIdx.x : kSoftmaxWarps * 32 + lane;
+    for (int item = qt; item < kMaxRows * (kD / 8); item += kQWarps * 32) {
+      const int row = item >> 4, ch = item & 15;
+      const int tile = row >> 7, rit = row & 127, region = ch >> 3, c8 = ch & 7;
+      const int r = tile_row_to_query(tile, rit, rows_q);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r >= 0) {
+        const int tok = G.t0 + r / H, h = r % H;
+        v = *reinterpret_cast<const uint4*>(P.q + tok * P.q_st + h * P.q_sh + ch * 8);
+      }
+      *reinterpret_cast<uint4*>(smem + kQOff + tile * kQTile + region * kQRegion + rit * 128 +
+                                ((c8 ^ (rit & 7)) << 4)) = v;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_full);
+  }
+
+  if (warp == kLoadWarp) {
+    // ---------------------------------------------------------------- loader
+    // Row slots of chunk c from the index tables (one global load per row;
+    // the per-token lengths that decide the masks are in shared memory).
+    auto resolve = [&](int c, int64_t* slot, uint32_t* mask, bool* comp) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int u = c * kCh + lane + rr * 32;
+        slot[rr] = -1;
+        mask[rr] = 0;
+        comp[rr] = false;
+        if (u < n_u) {
+          uint32_t m = 0;
+          int64_t idx;
+          if (u < G.n_win) {
+            idx = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
+                             : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
+            for (int k = 0; k < G.ntok; ++k) {
+              const int lk = tok_len[k];
+              if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) m |= 1u << k;
+            }
+          } else {
+            const int ci = u - G.n_win;
+            idx = P.comp_idx[G.last_tok * P.comp_idx_st + ci];
+            comp[rr] = true;
+            for (int k = 0; k < G.ntok; ++k)
+              if (ci < tok_clen[k]) m |= 1u << k;
+          }
+          slot[rr] = idx;
+          mask[rr] = idx >= 0 ? m : 0u;
+        }
+      }
+    };
+    int64_t nslot[2];
+    uint32_t nmask[2];
+    bool ncomp[2];
+    if (n > 0) resolve(c_begin, nslot, nmask, ncomp);
+    for (int i = 0; i < n; ++i) {
+      const int s = i % kStages;
+      int64_t slot[2] = {nslot[0], nslot[1]};
+      uint32_t mask[2] = {nmask[0], nmask[1]};
+      bool comp[2] = {ncomp[0], ncomp[1]};
+      if (i >= kStages && !mbar_wait(raw_empty + s, ((i / kStages) - 1) & 1)) {
+        report(err, misc + 1, 1);
+        break;
+      }
+      const RowGeom g = {kNope, kRowBytes, kNope / kQuantBlock + 1};
+      RowPtr rp[2];
+      bool ok[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        ok[rr] = slot[rr] >= 0;
+        if (ok[rr])
+          rp[rr] = comp[rr] ? row_ptr(const_cast<uint8_t*>(P.comp_cache), slot[rr], P.comp_page, P.comp_pstride, g)
+                            : row_ptr(const_cast<uint8_t*>(P.swa_cache), slot[rr], P.swa_page, P.swa_pstride, g);
+      }
+      // 12 x 16 B of row data + the 16-byte block holding the row's scale byte
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int row = lane + rr * 32;
+        if (ok[rr]) {
+          uint8_t* dst = smem + kRawOff + s * kRawStage + row * kRowBytes;
+#pragma unroll
+          for (int j = 0; j < kRowBytes / 16; ++j) cp_async16(dst + 16 * j, rp[rr].data + 16 * j);
+          const uintptr_t sa = reinterpret_cast<uintptr_t>(rp[rr].scale);
+          cp_async16(smem + kSBlkOff + (s * kCh + row) * 16, reinterpret_cast<const void*>(sa & ~uintptr_t(15)));
+          scale_s[s * kCh + row] = static_cast<uint8_t>(sa & 15);
+        }
+        mask_s[s * kCh + row] = ok[rr] ? (mask[rr] | kOkBit) : 0u;
+      }
+      cp_async_arrive_noinc(raw_full + s);
+      // the next chunk's index loads overlap this chunk's copies
+      if (i + 1 < n) resolve(c_begin + i + 1, nslot, nmask, ncomp);
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(raw_full + s);
+      issued = i + 1;
+    }
+  } else if (warp >= kDqWarp0) {
+    // --------------------------------------------------------------- dequant
+    const int t = threadIdx.x - kDqWarp0 * 32;
+    const int row = t & (kCh - 1), half = t >> 6;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % kStages, b = i & 1;
+      if (!mbar_wait(raw_full + s, (i / kStages) & 1)) {
+        report(err, misc + 1, 2);
+        break;
+      }
+      if (i >= 2 && !mbar_wait(k_empty + b, ((i >> 1) - 1) & 1)) {
+        report(err, misc + 1, 2);
+        break;
+      }
+      const uint32_t mask = mask_s[s * kCh + row];
+      const bool ok = (mask & kOkBit) != 0;
+      uint8_t* dst = smem + kKOff + b * kKBuf + half * kKRegion + row * 128;
+      const uint8_t* src = smem + kRawOff + s * kRawStage + row * kRowBytes;
+      if (half == 0) {
+        uint4 in[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) in[j] = ok ? reinterpret_cast<const uint4*>(src)[j] : make_uint4(0, 0, 0, 0);
+        // rows that are not loaded must come out exactly zero: their smem
+        // bytes are stale (a stale scale of 255 would be inf, 0 * inf = NaN)
+        const float sc =
+            ok ? exp2i(static_cast<int>(smem[kSBlkOff + (s * kCh + row) * 16 + scale_s[s * kCh + row]]) - 127) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t w0 = (j & 1) ? in[j >> 1].z : in[j >> 1].x;
+          const uint32_t w1 = (j & 1) ? in[j >> 1].w : in[j >> 1].y;
+          const float2 f0 = e4m3x2_to_float2(static_cast<uint16_t>(w0 & 0xffff));
+          const float2 f1 = e4m3x2_to_float2(static_cast<uint16_t>(w0 >> 16));
+          const float2 f2 = e4m3x2_to_float2(static_cast<uint16_t>(w1 & 0xffff));
+          const float2 f3 = e4m3x2_to_float2(static_cast<uint16_t>(w1 >> 16));
+          uint4 o;
+          o.x = pack_bf16(f0.x * sc, f0.y * sc);
+          o.y = pack_bf16(f1.x * sc, f1.y * sc);
+          o.z = pack_bf16(f2.x * sc, f2.y * sc);
+          o.w = pack_bf16(f3.x * sc, f3.y * sc);
+          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = o;
+        }
+        // per-token 64-bit column masks of this chunk: warp kDqWarp0 writes
+        // the low 32 rows, the next warp the high 32 (word k*2 + hi of buf b)
+        for (int k = 0; k < G.ntok; ++k) {
+          const uint32_t bits = __ballot_sync(0xffffffffu, (mask >> k) & 1u);
+          if (lane == 0) kmask[b * kCh + k * 2 + (row >> 5)] = bits;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v = ok ? reinterpret_cast<const uint4*>(src + kNope)[j] : make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(raw_empty + s);
+        mbar_arrive(k_full + b);
+        if (warp == kDqWarp0) misc[2] = i + 1;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------------- MMA
+    if (lane == 0) {
+      const uint32_t idesc_s = umma_idesc_bf16(128, kCh, false, false);
+      const uint32_t idesc_o = umma_idesc_bf16(128, kD, false, true);
+      const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_s = [&](int i) -> bool {
+        const int b = i & 1;
+        if (!mbar_wait(k_full + b, (i >> 1) & 1)) return false;
+        tc_fence_after();
+        for (int t = 0; t < ntiles; ++t) {
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t qa = q_base + t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32;
+            const uint32_t kb = k_base + b * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32;
+            umma_ss(tmem + s_col(t, b), umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(kb, 16, 1024), idesc_s,
+                    kk > 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(s_full + b);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_s(0);
+      for (int i = 0; ok && i < n; ++i) {
+        const int b = i & 1;
+        if (i + 1 < n && !issue_s(i + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(p_full + b, (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int t = 0; t < ntiles; ++t) {
+#pragma unroll
+          for (int kk = 0; kk < kCh / 16; ++kk) {
+            const uint32_t vb = k_base + b * kKBuf + kk * 2048;
+            umma_ts(tmem + t * 128, tmem + s_col(t, b) + kk * 8, umma_desc_sw128(vb, kKRegion, 1024), idesc_o,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        umma_commit(k_empty + b);
+        umma_commit(pv_done + b);
+      }
+      if (!ok) report(err, misc + 1, 4);
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------------- softmax
+    // one thread per query row: its S row lives in TMEM lane `rit` of tile t
+    const int t = warp >> 2, quad = warp & 3;
+    const int rit = quad * 32 + lane;
+    const int r = tile_row_to_query(t, rit, rows_q);
+    const bool row_valid = r >= 0;
+    const bool warp_active = __any_sync(0xffffffffu, row_valid);
+    const int tok = row_valid ? r / H : 0;
+    const int head = row_valid ? r % H : 0;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t o_col = static_cast<uint32_t>(t) * 128u;
+    const float scale = P.scale_log2;
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    if (warp_active) {
+      for (int i = 0; i < n; ++i) {
+        const int b = i & 1;
+        if (!mbar_wait(s_full + b, (i >> 1) & 1) || !mbar_wait(k_full + b, (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // valid columns of this row's token: bit j of lo / hi = KV row j / 32 + j
+        const uint32_t lo = row_valid ? kmask[b * kCh + tok * 2] : 0u;
+        const uint32_t hi = row_valid ? kmask[b * kCh + tok * 2 + 1] : 0u;
+        const bool full = (lo & hi) == 0xffffffffu;
+        const uint32_t s_addr = tmem + lane_addr + s_col(t, b);
+        uint32_t sr[kCh];
+        tmem_ld32(s_addr, sr);
+        tmem_ld32(s_addr + 32, sr + 32);
+        tmem_wait_ld();
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < kCh; ++j) mx = fmaxf(mx, __uint_as_float(sr[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if ((lo >> j) & 1u) mx = fmaxf(mx, __uint_as_float(sr[j]));
+            if ((hi >> j) & 1u) mx = fmaxf(mx, __uint_as_float(sr[32 + j]));
+          }
+        }
+        mx *= scale;  // scale > 0 commutes with the max
+        // raise the running max lazily: only when it grows by more than 2^8
+        const bool need = mx > m_used + 8.0f;
+        const bool rescale = __any_sync(0xffffffffu, need);
+        float f = 1.0f;
+        if (rescale) {
+          const float new_m = fmaxf(m_used, mx);
+          f = m_used == -INFINITY ? 0.0f : exp2f(m_used - new_m);
+          l *= f;
+          m_used = new_m;
+        }
+        // P = 2^(s * scale - m) as bf16 pairs over the S columns already read
+        const float nb = m_used == -INFINITY ? 0.0f : -m_used;
+        float rs = 0.0f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const uint32_t w = hh ? hi : lo;
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float p0 = ex2_approx(fmaf(__uint_as_float(sr[hh * 32 + 2 * j]), scale, nb));
+            float p1 = ex2_approx(fmaf(__uint_as_float(sr[hh * 32 + 2 * j + 1]), scale, nb));
+            if (!full) {
+              p0 = ((w >> (2 * j)) & 1u) ? p0 : 0.0f;
+              p1 = ((w >> (2 * j + 1)) & 1u) ? p1 : 0.0f;
+            }
+            rs += p0 + p1;
+            pk[j] = pack_bf16(p0, p1);
+          }
+          tmem_st16(s_addr + hh * 16, pk);
+        }
+        l += rs;
+        if (rescale && i > 0) {
+          // O holds chunks < i at the old max: wait for PV(i-1), then scale it
+          if (!mbar_wait(pv_done + ((i - 1) & 1), ((i - 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int q4 = 0; q4 < kD / 32; ++q4) {
+            uint32_t o[32];
+            tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st32(tmem + lane_addr + o_col + q4 * 32, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full + b);
+      }
+      if (ok && n > 0) {
+        if (!mbar_wait(pv_done + ((n - 1) & 1), ((n - 1) >> 1) & 1)) ok = false;
+        tc_fence_after();
+      }
+      if (!ok) report(err, misc + 1, 8);
+      // ---- epilogue: normalise (single split) or write the partial ----
+      const bool have_o = ok && n > 0 && l > 0.0f;
+      if (P.num_splits == 1) {
+        const float sink2 = (P.sink && row_valid) ? P.sink[head] * kLog2e : -INFINITY;
+        const float inv = have_o ? 1.0f / (l + exp2f(sink2 - m_used)) : 0.0f;
+        __nv_bfloat16* orow = P.out + (G.t0 + tok) * P.o_st + head * P.o_sh;
+#pragma unroll 1
+        for (int q4 = 0; q4 < kD / 32; ++q4) {
+          uint32_t o[32];
+          if (ok && n > 0) {
+            tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
+            tmem_wait_ld();
+          }
+          if (row_valid) {
+            uint32_t pkd[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pkd[e] = have_o ? pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv) : 0u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              reinterpret_cast<uint4*>(orow + q4 * 32)[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2], pkd[4 * e + 3]);
+          }
+        }
+        if (P.lse && row_valid)
+          P.lse[(G.t0 + tok) * H + head] = have_o ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
+      } else {
+        const int64_t rr = (static_cast<int64_t>(gidx) * P.num_splits + split) * P.max_rows + (row_valid ? r : 0);
+#pragma unroll 1
+        for (int q4 = 0; q4 < kD / 32; ++q4) {
+          uint32_t o[32];
+          if (ok && n > 0) {
+            tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
+            tmem_wait_ld();
+          }
+          if (row_valid && have_o) {
+            float4* dst = reinterpret_cast<float4*>(P.ws_o + rr * kD + q4 * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                   __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+          }
+        }
+        if (row_valid) {
+          P.ws_ml[rr * 2] = have_o ? m_used : -INFINITY;
+          P.ws_ml[rr * 2 + 1] = have_o ? l : 0.0f;
+        }
+      }
+    }
+  }
+
+  // ---- teardown: drain any bulk copies still in flight, free TMEM ----
+  __syncthreads();
+  if (warp == kLoadWarp && lane == 0) {
+    for (int k = static_cast<int>(misc[2]); k < issued; ++k)
+      if (!mbar_wait(raw_full + (k % kStages), (k / kStages) & 1)) break;
+  }
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
 }  // namespace hca
 
 using namespace hca;
+
+// Device error word: bit 0 loader, bit 1 dequant, bit 2 MMA, bit 3 softmax
+// timed out on an mbarrier.  Zero in normal operation.
+__device__ int g_hca_device_error;
+
+extern "C" int hca_device_error(int32_t* value, int32_t clear) {
+  if (!value) return HCA_E_INVALID;
+  if (cudaMemcpyFromSymbol(value, g_hca_device_error, sizeof(int)) != cudaSuccess) return HCA_E_CUDA;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_hca_device_error, &zero, sizeof(int)) != cudaSuccess) return HCA_E_CUDA;
+  }
+  return HCA_OK;
+}
 
 extern "C" int64_t hca_sparse_decode_workspace_bytes(int32_t num_groups, int32_t max_group_tokens,
                                                      int32_t num_heads, int32_t head_dim,
@@ -611,11 +1145,15 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
   }
   HCA_CHECK_ARG(num_tokens >= 0 && num_groups >= 0 && num_splits >= 1 && num_splits <= 16 &&
                 swa_page_size > 0);
-  if (!attn_shape_ok(num_heads, head_dim, rope_dim, max_group_tokens)) return HCA_E_UNSUPPORTED;
+  if (head_dim != 128 || rope_dim != 64 || num_heads < 1 || max_group_tokens < 1 || max_group_tokens > 30 ||
+      max_group_tokens * num_heads > tcd::kMaxRows)
+    return HCA_E_UNSUPPORTED;
   if (num_tokens == 0 || num_groups == 0) return HCA_OK;
   HCA_CHECK_ARG(out && q && swa_cache && swa_indices && swa_lens);
   HCA_CHECK_ARG(!comp_cache || (comp_indices && comp_lens && comp_page_size > 0));
   HCA_CHECK_ARG(swa_page_stride_bytes % 16 == 0 && (!comp_cache || comp_page_stride_bytes % 16 == 0));
+  HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(swa_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(comp_cache) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride_tok % 8 == 0 && q_stride_head % 8 == 0);
   HCA_CHECK_ARG(q_stride_head % 2 == 0 && q_stride_tok % 2 == 0);
   // the split-K combine stores 16-byte vectors
   HCA_CHECK_ARG(out_stride_head % 8 == 0 && out_stride_tok % 8 == 0 &&
@@ -659,7 +1197,20 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
     P.ws_o = reinterpret_cast<float*>(w);
     P.ws_ml = reinterpret_cast<float*>(w + o);
   }
-  return launch_attention<false>(P, num_groups, max_group_tokens, as_stream(stream));
+  cudaStream_t s = as_stream(stream);
+  static bool smem_set = false;  // one attribute call per process (same value every time)
+  if (!smem_set) {
+    if (cudaFuncSetAttribute(hca_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             tcd::kSmemBytes) != cudaSuccess)
+      return HCA_E_CUDA;
+    smem_set = true;
+  }
+  int* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
+  hca_decode_tc_kernel<<<dim3(num_splits, num_groups), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
+  if (num_splits > 1)
+    hca_attention_combine_kernel<128, false><<<dim3(num_groups, (P.max_rows + 15) / 16), 256, 0, s>>>(P);
+  return HCA_LAUNCH_STATUS();
 }
 
 extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out_stride_head,

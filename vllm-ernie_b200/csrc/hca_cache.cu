@@ -231,43 +231,87 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
 }
 
 // ----------------------------------------------------------------------------
-// Block compressor: one CTA of D threads per boundary token; thread c owns
-// channel c.  Softmax over the `ratio` tokens per channel, weighted sum,
-// RMSNorm, NoPE quant from the bf16 rounding, RoPE of the fp32 normed value
-// at the block start position, store into the compressed cache.
+// Block compressor: one 512-thread CTA per boundary token.  Thread (g, c)
+// owns channel c of token group g (512 / D groups split the `ratio` pooled
+// tokens); each thread pools its tokens 32 at a time with independent loads
+// (online softmax per channel), the groups merge in shared memory, then the
+// D threads of group 0 apply RMSNorm, the NoPE quant of the bf16 rounding,
+// and RoPE of the fp32 normed value at the block start position, and store
+// the row into the compressed cache.
 // ----------------------------------------------------------------------------
+constexpr int kCompressThreads = 512;
+
 template <int D>
-__global__ void __launch_bounds__(D) compress_kernel(
+__global__ void __launch_bounds__(kCompressThreads) compress_kernel(
     const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
     const int64_t* positions, const int64_t* state_slot, const int32_t* bt, int64_t bt_stride,
     int block_size, const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride,
     uint8_t* kv_cache, const int64_t* kv_slot, int kv_page_size, int64_t kv_page_stride,
     int rope_dim, int ratio) {
+  constexpr int kGroups = kCompressThreads / D;
+  constexpr int kSub = 32;  // tokens per batch of independent loads
   __shared__ float red[32];
   __shared__ int64_t row_off[512];
+  __shared__ float part[3][kGroups][D];
   const int64_t t = blockIdx.x;
   if (state_slot[t] < 0) return;
   const int64_t p = positions[t];
   if ((p + 1) % ratio != 0) return;
   const int req = t2r[t];
-  const int c = threadIdx.x;
+  const int c = threadIdx.x % D, grp = threadIdx.x / D;
   // Row offsets of the `ratio` states (all positions are >= 0 at a boundary).
-  for (int i = c; i < ratio; i += D) {
+  for (int i = threadIdx.x; i < ratio; i += kCompressThreads) {
     const int64_t pos = p - ratio + 1 + i;
     const int64_t blk = bt[req * bt_stride + pos / block_size];
     row_off[i] = blk * s_blk + (pos % block_size) * s_tok;
   }
   __syncthreads();
-  float m = -INFINITY;
-  for (int i = 0; i < ratio; ++i) m = fmaxf(m, state[row_off[i] + state_width + c]);
-  float den = 0.0f, acc = 0.0f;
-  for (int i = 0; i < ratio; ++i) {
-    const float w = expf(state[row_off[i] + state_width + c] - m);
-    den += w;
-    acc += w * state[row_off[i] + c];
+  const int per = (ratio + kGroups - 1) / kGroups;
+  const int i0 = grp * per, i1 = min(ratio, i0 + per);
+  float m = -INFINITY, den = 0.0f, acc = 0.0f;
+  for (int b0 = i0; b0 < i1; b0 += kSub) {
+    float sc[kSub], kv[kSub];
+#pragma unroll
+    for (int j = 0; j < kSub; ++j) {
+      const int i = b0 + j;
+      sc[j] = i < i1 ? __ldg(state + row_off[i] + state_width + c) : -INFINITY;
+      kv[j] = i < i1 ? __ldg(state + row_off[i] + c) : 0.0f;
+    }
+    float mb = m;
+#pragma unroll
+    for (int j = 0; j < kSub; ++j) mb = fmaxf(mb, sc[j]);
+    const float f = m == -INFINITY ? 0.0f : expf(m - mb);
+    den *= f;
+    acc *= f;
+#pragma unroll
+    for (int j = 0; j < kSub; ++j) {
+      const float w = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - mb);
+      den += w;
+      acc += w * kv[j];
+    }
+    m = mb;
   }
-  const float comp = acc / den;
+  part[0][grp][c] = m;
+  part[1][grp][c] = den;
+  part[2][grp][c] = acc;
+  __syncthreads();
+  float comp = 0.0f;
+  if (grp == 0) {
+    float mm = -INFINITY;
+#pragma unroll
+    for (int g2 = 0; g2 < kGroups; ++g2) mm = fmaxf(mm, part[0][g2][c]);
+    float dd = 0.0f, aa = 0.0f;
+#pragma unroll
+    for (int g2 = 0; g2 < kGroups; ++g2) {
+      const float mg = part[0][g2][c];
+      const float w = mg == -INFINITY ? 0.0f : expf(mg - mm);
+      dd += part[1][g2][c] * w;
+      aa += part[2][g2][c] * w;
+    }
+    comp = aa / dd;
+  }
   const float ss = block_sum(comp * comp, red);
+  if (grp != 0) return;  // no barrier below involves the other groups
   const float normed = comp * rsqrtf(ss / static_cast<float>(D) + eps) * norm_w[c];
   const int64_t slot = kv_slot[t];
   if (slot < 0) return;  // uniform across the CTA
@@ -277,9 +321,10 @@ __global__ void __launch_bounds__(D) compress_kernel(
   // NoPE: UE8M0 quant of the bf16 rounding; 64-channel blocks = 2 warps.
   const float qv = bf16_round(normed);
   float amax = warp_max(c < nope ? fabsf(qv) : 0.0f);
-  __syncthreads();
+  // only the D threads of group 0 are left: sync them with a named barrier
+  asm volatile("bar.sync 1, %0;\n" ::"r"(D) : "memory");
   if ((c & 31) == 0) red[c >> 5] = amax;
-  __syncthreads();
+  asm volatile("bar.sync 1, %0;\n" ::"r"(D) : "memory");
   amax = fmaxf(red[(c >> 6) * 2], red[(c >> 6) * 2 + 1]);
   // RoPE partner (adjacent channel) in fp32.
   const float partner = __shfl_xor_sync(0xffffffffu, normed, 1);
@@ -432,13 +477,13 @@ extern "C" int hca_compress_norm_rope_store(
   HCA_CHECK_ARG(state && token_to_req && positions && state_slot_mapping && block_table &&
                 norm_weight && cos_sin && kv_cache && kv_slot_mapping);
   if (head_dim == 128)
-    compress_kernel<128><<<num_tokens, 128, 0, as_stream(stream)>>>(
+    compress_kernel<128><<<num_tokens, kCompressThreads, 0, as_stream(stream)>>>(
         state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
         state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
         cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,
         compress_ratio);
   else
-    compress_kernel<512><<<num_tokens, 512, 0, as_stream(stream)>>>(
+    compress_kernel<512><<<num_tokens, kCompressThreads, 0, as_stream(stream)>>>(
         state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
         state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
         cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,

@@ -118,6 +118,148 @@ __global__ void __launch_bounds__(256) vha_out_kernel(
   }
 }
 
+// ----------------------------------------------------------------------------
+// VHA head mix on the tensor cores: one CTA per token row (padded to
+// aligned_T), H / 16 warps; warp w computes heads 16w .. 16w+15 of
+// y = mix @ o[t] (m16n8k16 bf16 -> fp32) 128 dims at a time, applies the
+// inverse RoPE in registers (pairs never straddle a thread) and either
+// quantises per (head, 128-chunk) to e4m3 (MODE 0) or stores bf16 (MODE 2).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void mma16816_o(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p, bool trans) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  if (trans)
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+  else
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(256) vha_mma_kernel(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16,
+                                                      int64_t ob_st, int64_t ob_sh, const __nv_bfloat16* o,
+                                                      int64_t o_st, int64_t o_sh, const __nv_bfloat16* mix,
+                                                      const int64_t* positions, const float* cos_sin,
+                                                      int64_t cs_stride, int num_tokens, int aligned_t,
+                                                      int num_heads, int n_groups, int rope_dim) {
+  constexpr int kCk = 128;             // dims per pass
+  constexpr int kMaxH = 64;            // heads of one (TP-local) layer
+  constexpr int kMixStride = kMaxH + 8;  // padded rows: conflict-free ldmatrix
+  constexpr int kOStride = kCk + 8;
+  constexpr int kChunks = D / kCk;
+  __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
+  __shared__ __align__(16) __nv_bfloat16 o_s[kMaxH * kOStride];
+  const int H = num_heads;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t = blockIdx.x;
+  const int hpg = H / n_groups;
+  if (t >= num_tokens) {
+    if (MODE == 0)
+      for (int h = threadIdx.x; h < H; h += blockDim.x)
+        scale[(static_cast<int64_t>(h / hpg) * hpg + h % hpg) * aligned_t + t] = 0;
+    return;
+  }
+  for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
+    const int r = i / (H / 8), c8 = i % (H / 8);
+    *reinterpret_cast<uint4*>(&mix_s[r * kMixStride + c8 * 8]) =
+        *reinterpret_cast<const uint4*>(mix + static_cast<int64_t>(r) * H + c8 * 8);
+  }
+  const float* cs = cos_sin + positions[t] * cs_stride;
+  const int nope = D - rope_dim;
+  const int g = lane >> 2, cq = lane & 3;
+  const int h0 = warp * 16 + g, h1 = h0 + 8;
+  uint32_t packed0 = 0, packed1 = 0;  // exponent bytes of heads h0 / h1
+  for (int ck = 0; ck < kChunks; ++ck) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < H * (kCk / 8); i += blockDim.x) {
+      const int r = i / (kCk / 8), c8 = i % (kCk / 8);
+      *reinterpret_cast<uint4*>(&o_s[r * kOStride + c8 * 8]) =
+          *reinterpret_cast<const uint4*>(o + t * o_st + r * o_sh + ck * kCk + c8 * 8);
+    }
+    __syncthreads();
+    if (warp * 16 >= H) continue;
+    float acc[kCk / 8][4];
+#pragma unroll
+    for (int j = 0; j < kCk / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    for (int kk = 0; kk < H / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, &mix_s[(warp * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8], false);
+#pragma unroll
+      for (int j = 0; j < kCk / 8; j += 2) {
+        uint32_t b[4];
+        ldsm_x4(b, &o_s[(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kOStride + j * 8 + (lane >> 4) * 8], true);
+        mma16816_o(acc[j], a, b);
+        mma16816_o(acc[j + 1], a, b + 2);
+      }
+    }
+    // inverse GPT-J RoPE on the dims >= nope
+#pragma unroll
+    for (int j = 0; j < kCk / 8; ++j) {
+      const int d = ck * kCk + j * 8 + 2 * cq;
+      if (d >= nope) {
+        const int pr = (d - nope) >> 1;
+        const float c = cs[pr], s = cs[rope_dim / 2 + pr];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float e = acc[j][2 * h], od = acc[j][2 * h + 1];
+          acc[j][2 * h] = e * c + od * s;
+          acc[j][2 * h + 1] = od * c - e * s;
+        }
+      }
+    }
+    if (MODE == 2) {
+#pragma unroll
+      for (int j = 0; j < kCk / 8; ++j) {
+        const int d = ck * kCk + j * 8 + 2 * cq;
+        __nv_bfloat162 v0 = __floats2bfloat162_rn(acc[j][0], acc[j][1]);
+        __nv_bfloat162 v1 = __floats2bfloat162_rn(acc[j][2], acc[j][3]);
+        *reinterpret_cast<__nv_bfloat162*>(out_bf16 + t * ob_st + h0 * ob_sh + d) = v0;
+        *reinterpret_cast<__nv_bfloat162*>(out_bf16 + t * ob_st + h1 * ob_sh + d) = v1;
+      }
+      continue;
+    }
+    float am0 = 0.0f, am1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kCk / 8; ++j) {
+      am0 = fmaxf(am0, fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])));
+      am1 = fmaxf(am1, fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])));
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
+    }
+    const int e0 = ue8m0_exponent(am0, 1e-10f, false), e1 = ue8m0_exponent(am1, 1e-10f, false);
+    const float i0 = exp2i(-e0), i1 = exp2i(-e1);
+    packed0 |= static_cast<uint32_t>(encode_ue8m0(e0)) << (8 * ck);
+    packed1 |= static_cast<uint32_t>(encode_ue8m0(e1)) << (8 * ck);
+    uint8_t* r0 = out_fp8 + (static_cast<int64_t>(h0 / hpg) * num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
+    uint8_t* r1 = out_fp8 + (static_cast<int64_t>(h1 / hpg) * num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+#pragma unroll
+    for (int j = 0; j < kCk / 8; ++j) {
+      const int d = ck * kCk + j * 8 + 2 * cq;
+      *reinterpret_cast<uint16_t*>(r0 + d) =
+          static_cast<uint16_t>(to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8));
+      *reinterpret_cast<uint16_t*>(r1 + d) =
+          static_cast<uint16_t>(to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8));
+    }
+  }
+  if (MODE == 0 && cq == 0 && warp * 16 < H) {
+    scale[(static_cast<int64_t>(h0 / hpg) * hpg + h0 % hpg) * aligned_t + t] = static_cast<int32_t>(packed0);
+    scale[(static_cast<int64_t>(h1 / hpg) * hpg + h1 % hpg) * aligned_t + t] = static_cast<int32_t>(packed1);
+  }
+}
+
 // x * sigmoid(gate) -> 1x128 FP8; one CTA of 128 threads per (512-col pack, row).
 __global__ void __launch_bounds__(128) sigmoid_mul_quant_kernel(
     uint8_t* out, int32_t* scale, const __nv_bfloat16* x, int64_t x_stride,
@@ -160,6 +302,22 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
   if (aligned == 0) return HCA_OK;
   auto* op = static_cast<const __nv_bfloat16*>(o);
   auto* mp = static_cast<const __nv_bfloat16*>(mix);
+  if (MODE != 1 && mp != nullptr) {
+    // head mix on the tensor cores: H % 16 == 0, H <= 64, 16-byte aligned rows
+    if (num_heads % 16 || num_heads > 64 || o_sh % 8 || o_st % 8 || reinterpret_cast<uintptr_t>(o) % 16 ||
+        reinterpret_cast<uintptr_t>(mix) % 16)
+      return HCA_E_UNSUPPORTED;
+    const int threads = (num_heads / 16) * 32;
+    if (head_dim == 128)
+      vha_mma_kernel<128, MODE><<<aligned, threads, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh,
+                                                            mp, positions, cos_sin, cs_stride, num_tokens, aligned,
+                                                            num_heads, n_groups, rope_dim);
+    else
+      vha_mma_kernel<512, MODE><<<aligned, threads, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh,
+                                                            mp, positions, cos_sin, cs_stride, num_tokens, aligned,
+                                                            num_heads, n_groups, rope_dim);
+    return HCA_LAUNCH_STATUS();
+  }
   if (head_dim == 128)
     vha_out_kernel<128, MODE><<<aligned, 256, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op,
                                                       o_st, o_sh, mp, positions, cos_sin,

@@ -233,7 +233,7 @@ class SWAMetadataBuilder:
             md.prefill_gather_lens = ops.compute_prefill_gather_lens(cm.seq_lens, cm.query_start_loc, npf, nd,
                                                                      self.window_size)
         if ndt > 0:
-            max_g = max(1, (12 * 16) // self.num_heads)
+            max_g = max(1, 256 // self.num_heads)
             md.decode_max_group_tokens = min(max_g, self.decode_threshold)
             md.decode_group_starts = _decode_groups(cm.query_start_loc_cpu.tolist(), nd,
                                                     md.decode_max_group_tokens, self.device)

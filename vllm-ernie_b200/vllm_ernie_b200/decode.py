@@ -39,11 +39,13 @@ class DecodeMetadata:
     num_splits: int
 
 
-def choose_num_splits(num_groups: int, sm_count: int = SM_COUNT_B200, waves: float = 2.0) -> int:
-    """Split-K factor: enough CTAs for ``waves`` waves of one CTA per SM."""
+def choose_num_splits(num_groups: int, sm_count: int = SM_COUNT_B200) -> int:
+    """Split-K factor: as many splits per group as fit one wave of one CTA
+    per SM (the decode kernel holds a whole SM: 512 TMEM columns, ~150 KB
+    shared memory)."""
     if num_groups <= 0:
         return 1
-    return max(1, min(16, round(waves * sm_count / num_groups)))
+    return max(1, min(16, sm_count // num_groups))
 
 
 def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: int | None = None,
@@ -79,7 +81,7 @@ def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: i
     pre = get("comp_prefill", (1, max_compressed), torch.int32)
     ops.build_c128a_topk_metadata(batch.positions, d.ratio, T, t2r, batch.comp_bt, d.comp_page,
                                   swa_slot, cidx, clens, pre, max_compressed)
-    max_g = max(1, min(batch.q_per_seq, (12 * 16) // d.heads))
+    max_g = max(1, min(batch.q_per_seq, 256 // d.heads))
     if max_g < batch.q_per_seq:
         # split each request's tokens into sub-groups of max_g tokens
         starts = [t for r in range(batch.num_reqs) for t in

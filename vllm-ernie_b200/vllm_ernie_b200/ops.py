@@ -203,6 +203,16 @@ def compress_norm_rope_store(state_cache, num_actual: int, token_to_req_indices,
 # ---------------------------------------------------------------------------
 
 
+def device_error(clear: bool = True) -> int:
+    """The library's device error word (non-zero if a kernel gave up on a
+    bounded wait); synchronous."""
+    import ctypes
+
+    v = ctypes.c_int32(0)
+    call("hca_device_error", ctypes.addressof(v), 1 if clear else 0)
+    return int(v.value)
+
+
 class DecodeWorkspace:
     """Persistent zero-initialised split-K workspace (graph-stable address)."""
 
