@@ -561,9 +561,13 @@ __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnPa
 //   warps 0-7  softmax: tile t = warp / 4, TMEM lane quadrant = warp % 4,
 //              one thread per query row (S row read from TMEM, P written back)
 //   warp  8    MMA issuer (lane 0) + TMEM owner
-//   warp  9    loader: row slots from the index tables, one cp.async.bulk per
-//              192-byte row into a 4-stage raw ring (mbarrier tx completion)
-//   warps 10-13 dequant: e4m3 x UE8M0 -> bf16 into the 128B-swizzled K tile
+//   warps 9-12 producers: each owns 16 of the 64 KV rows of every chunk.  It
+//              resolves their slots from the index tables, gathers the rows
+//              with 16-byte cp.async into its slice of a kStages-deep raw ring
+//              (kStages - 1 chunks in flight, completion by cp.async groups),
+//              then dequantises them (e4m3 x UE8M0 -> bf16, RoPE half copied)
+//              into the 128B-swizzled K tile.  A random-row gather is bound by
+//              the requests one SM keeps in flight, so four warps issue them.
 // S = Q K^T: M=128, N=64, K=128 (8 x K16), Q and K tile K-major in smem.
 // O += P V: M=128, N=128, K=64 (4 x K16), P from TMEM, V = the same K tile
 // read MN-major.  TMEM: O tiles at columns 0 / 128, S/P double-buffered at
@@ -579,27 +583,30 @@ constexpr int kCh = 64;         // KV rows per step
 constexpr int kStages = 4;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kMmaWarp = 8;
-constexpr int kLoadWarp = 9;
-constexpr int kDqWarp0 = 10;
-constexpr int kDqWarps = 4;
-constexpr int kThreads = 14 * 32;
+constexpr int kProdWarp0 = 9;
+constexpr int kProdWarps = 4;
+constexpr int kProdRows = kCh / kProdWarps;  // 16 rows of each chunk per producer warp
+constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;
 constexpr int kMaxRows = 256;
 constexpr int kQTile = 2 * 128 * 128;          // two 64-column regions of 128 rows x 128 B
 constexpr int kQRegion = 128 * 128;
 constexpr int kQOff = 0;
-constexpr int kKBufs = 2;                      // bf16 K-tile ring: dequant runs ahead of the MMAs
+constexpr int kKBufs = 4;                      // bf16 K-tile ring: dequant runs ahead of the MMAs
 constexpr int kKOff = kQOff + 2 * kQTile;      // 65536
 constexpr int kKRegion = kCh * 128;            // 8192
 constexpr int kKBuf = 2 * kKRegion;            // 16384
 constexpr int kRawOff = kKOff + kKBufs * kKBuf;
-constexpr int kRawStage = kCh * kRowBytes;     // 12288
-constexpr int kScaleOff = kRawOff + kStages * kRawStage;  // byte index of the scale in its block
-constexpr int kSBlkOff = kScaleOff + kStages * kCh;        // [stage][row] 16-byte scale blocks
-constexpr int kMaskOff = kSBlkOff + kStages * kCh * 16;
-constexpr int kKMaskOff = kMaskOff + kStages * kCh * 4;
+// raw stage: e4m3 NoPE [64][64] | bf16 RoPE [64][128] | 16-byte scale blocks [64][16]
+constexpr int kRawNope = 0;
+constexpr int kRawRope = kCh * kNope;
+constexpr int kRawSblk = kRawRope + kCh * 128;
+constexpr int kRawStage = kRawSblk + kCh * 16;  // 13312
+constexpr int kScaleOff = kRawOff + kStages * kRawStage;  // [stage][row] byte index of the scale in its block
+constexpr int kMaskOff = kScaleOff + kStages * kCh;       // [stage][row] token mask | kOkBit
+constexpr int kKMaskOff = kMaskOff + kStages * kCh * 4;   // [kbuf][token][4] 16-bit column masks
 constexpr int kBarOff = kKMaskOff + kKBufs * kCh * 4;
-// raw_full[4] raw_empty[4] k_full[kKBufs] k_empty[kKBufs] s_full[2] p_full[2] pv_done[2] q_full
-constexpr int kNumBars = 2 * kStages + 2 * kKBufs + 7;
+// k_full[kKBufs] k_empty[kKBufs] s_full[2] p_full[2] pv_done[2] q_full
+constexpr int kNumBars = 2 * kKBufs + 7;
 constexpr int kMiscOff = kBarOff + kNumBars * 8;
 constexpr int kTokOff = kMiscOff + 64;  // [32] + [32] ints
 constexpr int kSmemBytes = kTokOff + 256 + 1024;  // + 1024 alignment slack
@@ -648,21 +655,19 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint64_t* raw_full = bars;
-  uint64_t* raw_empty = bars + 4;
-  uint64_t* k_full = bars + 8;
-  uint64_t* k_empty = bars + 10;
-  uint64_t* s_full = bars + 12;
-  uint64_t* p_full = bars + 14;
-  uint64_t* pv_done = bars + 16;
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kMiscOff);  // [0] tmem, [1] err, [2] consumed
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = k_full + kKBufs;
+  uint64_t* s_full = k_empty + kKBufs;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* q_full = pv_done + 2;
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kMiscOff);  // [0] tmem, [1] err
   uint8_t* scale_s = smem + kScaleOff;
   uint32_t* mask_s = reinterpret_cast<uint32_t*>(smem + kMaskOff);
   uint32_t* kmask = reinterpret_cast<uint32_t*>(smem + kKMaskOff);
 
   int* tok_len = reinterpret_cast<int*>(smem + kTokOff);  // [32] window length per token
   int* tok_clen = tok_len + 32;                             // [32] compressed length per token
-  uint64_t* q_full = bars + 18;
 
   if (warp == kMmaWarp) {
     tmem_alloc(misc, kTmemCols);
@@ -670,20 +675,17 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     tc_fence_before();
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(raw_full + s, 32 + 1);  // 32 cp.async completions + the mask arrival
-      mbar_init(raw_empty + s, kDqWarps);
+    for (int b = 0; b < kKBufs; ++b) {
+      mbar_init(k_full + b, kProdWarps);
+      mbar_init(k_empty + b, 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(k_full + b, kDqWarps);
-      mbar_init(k_empty + b, 1);
       mbar_init(s_full + b, 1);
       mbar_init(p_full + b, 4 * ntiles);
       mbar_init(pv_done + b, 1);
     }
-    mbar_init(q_full, kQWarps);
+    mbar_init(q_full, kQWarps * 32 + kQWarps);  // per-thread cp.async completions + one arrival per warp
     misc[1] = 0;
-    misc[2] = 0;
     mbar_fence_init();
   }
   if (threadIdx.x < G.ntok) {
@@ -693,7 +695,6 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
-  int issued = 0;
 
   if (warp < kSoftmaxWarps || warp == kMmaWarp) {
     // Q rows -> two K-major 128B-swizzled M=128 tiles (rows past rows_q zero),
@@ -701,164 +702,178 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     // A tile with R < 128 query rows spreads them evenly over the four TMEM
     // lane quadrants (q = ceil(R / 4) rows each) so every SM sub-partition
     // runs the same softmax load.
+    // Valid rows arrive by cp.async (all copies in flight at once, completion
+    // counted on q_full); padding rows are zeroed with plain stores.
     const int qt = warp < kSoftmaxWarps ? threadIdx.x : kSoftmaxWarps * 32 + lane;
-    for (int item = qt; item < kMaxRows * (kD / 8); item += kQWarps * 32) {
+    for (int item = qt; item < ntiles * 128 * (kD / 8); item += kQWarps * 32) {
       const int row = item >> 4, ch = item & 15;
       const int tile = row >> 7, rit = row & 127, region = ch >> 3, c8 = ch & 7;
       const int r = tile_row_to_query(tile, rit, rows_q);
-      uint4 v = make_uint4(0, 0, 0, 0);
+      uint8_t* dst = smem + kQOff + tile * kQTile + region * kQRegion + rit * 128 + ((c8 ^ (rit & 7)) << 4);
       if (r >= 0) {
         const int tok = G.t0 + r / H, h = r % H;
-        v = *reinterpret_cast<const uint4*>(P.q + tok * P.q_st + h * P.q_sh + ch * 8);
+        cp_async16(dst, P.q + tok * P.q_st + h * P.q_sh + ch * 8);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
-      *reinterpret_cast<uint4*>(smem + kQOff + tile * kQTile + region * kQRegion + rit * 128 +
-                                ((c8 ^ (rit & 7)) << 4)) = v;
     }
+    cp_async_arrive_noinc(q_full);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
   }
 
-  if (warp == kLoadWarp) {
-    // ---------------------------------------------------------------- loader
-    // Row slots of chunk c from the index tables (one global load per row;
-    // the per-token lengths that decide the masks are in shared memory).
-    auto resolve = [&](int c, int64_t* slot, uint32_t* mask, bool* comp) {
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int u = c * kCh + lane + rr * 32;
-        slot[rr] = -1;
-        mask[rr] = 0;
-        comp[rr] = false;
-        if (u < n_u) {
-          uint32_t m = 0;
-          int64_t idx;
-          if (u < G.n_win) {
-            idx = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
-                             : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
-            for (int k = 0; k < G.ntok; ++k) {
-              const int lk = tok_len[k];
-              if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) m |= 1u << k;
-            }
-          } else {
-            const int ci = u - G.n_win;
-            idx = P.comp_idx[G.last_tok * P.comp_idx_st + ci];
-            comp[rr] = true;
-            for (int k = 0; k < G.ntok; ++k)
-              if (ci < tok_clen[k]) m |= 1u << k;
+  if (warp >= kProdWarp0) {
+    // -------------------------------------------------------------- producer
+    const int row0 = (warp - kProdWarp0) * kProdRows;  // this warp's rows of every chunk
+    // Slot, token mask and cache of row row0 + lane (lanes < kProdRows) of
+    // chunk c, from the index tables; the per-token lengths deciding the mask
+    // are in shared memory.
+    struct Resolved {
+      int64_t slot;
+      uint32_t mask;
+      bool comp;
+    };
+    auto resolve = [&](int c, Resolved& R) {
+      const int u = c * kCh + row0 + lane;
+      R.slot = -1;
+      R.mask = 0;
+      R.comp = false;
+      if (lane < kProdRows && u < n_u) {
+        uint32_t m = 0;
+        if (u < G.n_win) {
+          R.slot = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
+                              : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
+          for (int k = 0; k < G.ntok; ++k) {
+            const int lk = tok_len[k];
+            if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) m |= 1u << k;
           }
-          slot[rr] = idx;
-          mask[rr] = idx >= 0 ? m : 0u;
+        } else {
+          const int ci = u - G.n_win;
+          R.slot = P.comp_idx[G.last_tok * P.comp_idx_st + ci];
+          R.comp = true;
+          for (int k = 0; k < G.ntok; ++k)
+            if (ci < tok_clen[k]) m |= 1u << k;
         }
+        R.mask = m;
       }
     };
-    int64_t nslot[2];
-    uint32_t nmask[2];
-    bool ncomp[2];
-    if (n > 0) resolve(c_begin, nslot, nmask, ncomp);
-    for (int i = 0; i < n; ++i) {
-      const int s = i % kStages;
-      int64_t slot[2] = {nslot[0], nslot[1]};
-      uint32_t mask[2] = {nmask[0], nmask[1]};
-      bool comp[2] = {ncomp[0], ncomp[1]};
-      if (i >= kStages && !mbar_wait(raw_empty + s, ((i / kStages) - 1) & 1)) {
-        report(err, misc + 1, 1);
-        break;
-      }
-      const RowGeom g = {kNope, kRowBytes, kNope / kQuantBlock + 1};
-      RowPtr rp[2];
-      bool ok[2];
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        ok[rr] = slot[rr] >= 0;
-        if (ok[rr])
-          rp[rr] = comp[rr] ? row_ptr(const_cast<uint8_t*>(P.comp_cache), slot[rr], P.comp_page, P.comp_pstride, g)
-                            : row_ptr(const_cast<uint8_t*>(P.swa_cache), slot[rr], P.swa_page, P.swa_pstride, g);
-      }
-      // 12 x 16 B of row data + the 16-byte block holding the row's scale byte
-#pragma unroll
-      for (int rr = 0; rr < 2; ++rr) {
-        const int row = lane + rr * 32;
-        if (ok[rr]) {
-          uint8_t* dst = smem + kRawOff + s * kRawStage + row * kRowBytes;
-#pragma unroll
-          for (int j = 0; j < kRowBytes / 16; ++j) cp_async16(dst + 16 * j, rp[rr].data + 16 * j);
-          const uintptr_t sa = reinterpret_cast<uintptr_t>(rp[rr].scale);
-          cp_async16(smem + kSBlkOff + (s * kCh + row) * 16, reinterpret_cast<const void*>(sa & ~uintptr_t(15)));
+    // Gather this warp's rows of local chunk i into raw stage i % kStages and
+    // close one cp.async group (an empty group past the last chunk keeps the
+    // group count uniform).
+    auto issue = [&](int i, const Resolved& R) {
+      if (i < n) {
+        const int s = i % kStages;
+        uint8_t* const stage = smem + kRawOff + s * kRawStage;
+        const int row = row0 + lane;
+        // Row addresses in 32-bit slot arithmetic: a slot is below 2^31 in
+        // any cache that fits in device memory (every row takes > 64 bytes).
+        const bool ok = R.slot >= 0;
+        uint64_t rbase = 0;
+        if (ok) {
+          const uint32_t sl = static_cast<uint32_t>(R.slot);
+          const uint32_t psz = R.comp ? static_cast<uint32_t>(P.comp_page) : static_cast<uint32_t>(P.swa_page);
+          const uint32_t page = sl / psz, off = sl - page * psz;
+          const uint8_t* base =
+              (R.comp ? P.comp_cache : P.swa_cache) + static_cast<int64_t>(page) * (R.comp ? P.comp_pstride : P.swa_pstride);
+          rbase = reinterpret_cast<uint64_t>(base + off * kRowBytes);
+          const uintptr_t sa = reinterpret_cast<uintptr_t>(base + psz * kRowBytes + off * (kNope / kQuantBlock + 1));
+          cp_async16(stage + kRawSblk + row * 16, reinterpret_cast<const void*>(sa & ~uintptr_t(15)));
           scale_s[s * kCh + row] = static_cast<uint8_t>(sa & 15);
         }
-        mask_s[s * kCh + row] = ok[rr] ? (mask[rr] | kOkBit) : 0u;
-      }
-      cp_async_arrive_noinc(raw_full + s);
-      // the next chunk's index loads overlap this chunk's copies
-      if (i + 1 < n) resolve(c_begin + i + 1, nslot, nmask, ncomp);
-      __threadfence_block();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(raw_full + s);
-      issued = i + 1;
-    }
-  } else if (warp >= kDqWarp0) {
-    // --------------------------------------------------------------- dequant
-    const int t = threadIdx.x - kDqWarp0 * 32;
-    const int row = t & (kCh - 1), half = t >> 6;
-    for (int i = 0; i < n; ++i) {
-      const int s = i % kStages, b = i & 1;
-      if (!mbar_wait(raw_full + s, (i / kStages) & 1)) {
-        report(err, misc + 1, 2);
-        break;
-      }
-      if (i >= 2 && !mbar_wait(k_empty + b, ((i >> 1) - 1) & 1)) {
-        report(err, misc + 1, 2);
-        break;
-      }
-      const uint32_t mask = mask_s[s * kCh + row];
-      const bool ok = (mask & kOkBit) != 0;
-      uint8_t* dst = smem + kKOff + b * kKBuf + half * kKRegion + row * 128;
-      const uint8_t* src = smem + kRawOff + s * kRawStage + row * kRowBytes;
-      if (half == 0) {
-        uint4 in[4];
+        if (lane < kProdRows) mask_s[s * kCh + row] = ok ? (R.mask | kOkBit) : 0u;
+        // 12 pieces of 16 bytes per row, consecutive lanes on consecutive
+        // pieces (a cp.async instruction touches ~3 rows); pieces 0-3 are the
+        // e4m3 NoPE bytes, 4-11 the bf16 RoPE half.
 #pragma unroll
-        for (int j = 0; j < 4; ++j) in[j] = ok ? reinterpret_cast<const uint4*>(src)[j] : make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < kProdRows * (kRowBytes / 16) / 32; ++k) {
+          const int piece = k * 32 + lane;
+          const int r = piece / (kRowBytes / 16), j = piece - r * (kRowBytes / 16);
+          const uint64_t src = __shfl_sync(0xffffffffu, rbase, r);
+          uint8_t* dst = j < 4 ? stage + kRawNope + (row0 + r) * kNope + j * 16
+                               : stage + kRawRope + (row0 + r) * 128 + (j - 4) * 16;
+          if (src) cp_async16(dst, reinterpret_cast<const void*>(src + j * 16));
+        }
+      }
+      cp_async_commit();
+    };
+    // prologue: the first kStages - 1 chunks (index loads first, all in flight)
+    Resolved rq[kStages - 1];
+#pragma unroll
+    for (int i = 0; i < kStages - 1; ++i) {
+      rq[i].slot = -1;
+      if (i < n) resolve(c_begin + i, rq[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kStages - 1; ++i) issue(i, rq[i]);
+    Resolved rn;  // slots of the next chunk to issue
+    rn.slot = -1;
+    if (kStages - 1 < n) resolve(c_begin + kStages - 1, rn);
+    for (int i = 0; i < n; ++i) {
+      const int s = i % kStages, b = i % kKBufs;
+      issue(i + kStages - 1, rn);
+      if (i + kStages < n) resolve(c_begin + i + kStages, rn);
+      cp_async_wait_group<kStages - 1>();  // chunk i's group has landed
+      __syncwarp();
+      if (i >= kKBufs && !mbar_wait(k_empty + b, ((i / kKBufs) - 1) & 1)) {
+        report(err, misc + 1, 2);
+        break;
+      }
+      const uint8_t* stage = smem + kRawOff + s * kRawStage;
+      uint8_t* kt = smem + kKOff + b * kKBuf;
+      // NoPE: lane -> row row0 + lane / 2, 32 e4m3 values (half lane & 1)
+      {
+        const int r = row0 + (lane >> 1), h = lane & 1;
+        const uint32_t mask = mask_s[s * kCh + r];
+        const bool ok = (mask & kOkBit) != 0;
         // rows that are not loaded must come out exactly zero: their smem
         // bytes are stale (a stale scale of 255 would be inf, 0 * inf = NaN)
-        const float sc =
-            ok ? exp2i(static_cast<int>(smem[kSBlkOff + (s * kCh + row) * 16 + scale_s[s * kCh + row]]) - 127) : 0.0f;
+        const float sc = ok ? exp2i(static_cast<int>(stage[kRawSblk + r * 16 + scale_s[s * kCh + r]]) - 127) : 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t w0 = (j & 1) ? in[j >> 1].z : in[j >> 1].x;
-          const uint32_t w1 = (j & 1) ? in[j >> 1].w : in[j >> 1].y;
-          const float2 f0 = e4m3x2_to_float2(static_cast<uint16_t>(w0 & 0xffff));
-          const float2 f1 = e4m3x2_to_float2(static_cast<uint16_t>(w0 >> 16));
-          const float2 f2 = e4m3x2_to_float2(static_cast<uint16_t>(w1 & 0xffff));
-          const float2 f3 = e4m3x2_to_float2(static_cast<uint16_t>(w1 >> 16));
-          uint4 o;
-          o.x = pack_bf16(f0.x * sc, f0.y * sc);
-          o.y = pack_bf16(f1.x * sc, f1.y * sc);
-          o.z = pack_bf16(f2.x * sc, f2.y * sc);
-          o.w = pack_bf16(f3.x * sc, f3.y * sc);
-          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = o;
+        for (int q = 0; q < 2; ++q) {
+          const uint4 in = ok ? *reinterpret_cast<const uint4*>(stage + kRawNope + r * kNope + h * 32 + q * 16)
+                              : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int w2 = 0; w2 < 2; ++w2) {
+            const uint32_t w0 = w2 ? in.z : in.x, w1 = w2 ? in.w : in.y;
+            const float2 f0 = e4m3x2_to_float2(static_cast<uint16_t>(w0 & 0xffff));
+            const float2 f1 = e4m3x2_to_float2(static_cast<uint16_t>(w0 >> 16));
+            const float2 f2 = e4m3x2_to_float2(static_cast<uint16_t>(w1 & 0xffff));
+            const float2 f3 = e4m3x2_to_float2(static_cast<uint16_t>(w1 >> 16));
+            uint4 o;
+            o.x = pack_bf16(f0.x * sc, f0.y * sc);
+            o.y = pack_bf16(f1.x * sc, f1.y * sc);
+            o.z = pack_bf16(f2.x * sc, f2.y * sc);
+            o.w = pack_bf16(f3.x * sc, f3.y * sc);
+            const int c8 = h * 4 + q * 2 + w2;  // 16-byte chunk of the 128-byte NoPE row
+            *reinterpret_cast<uint4*>(kt + r * 128 + ((c8 ^ (r & 7)) << 4)) = o;
+          }
         }
-        // per-token 64-bit column masks of this chunk: warp kDqWarp0 writes
-        // the low 32 rows, the next warp the high 32 (word k*2 + hi of buf b)
+      }
+      // RoPE half: 16 rows x 8 pieces, copied into K-tile region 1
+#pragma unroll
+      for (int k = 0; k < kProdRows * 8 / 32; ++k) {
+        const int piece = k * 32 + lane;
+        const int r = row0 + (piece >> 3), c8 = piece & 7;
+        const bool ok = (mask_s[s * kCh + r] & kOkBit) != 0;
+        const uint4 v = ok ? *reinterpret_cast<const uint4*>(stage + kRawRope + r * 128 + c8 * 16) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(kt + kKRegion + r * 128 + ((c8 ^ (r & 7)) << 4)) = v;
+      }
+      // per-token 16-bit column masks of these rows: halfword (k * 4 + warp
+      // slice) of buffer b, so word k * 2 + hi covers KV rows hi * 32 .. + 31
+      {
+        const uint32_t mask = lane < kProdRows ? mask_s[s * kCh + row0 + lane] : 0u;
+        uint16_t* km16 = reinterpret_cast<uint16_t*>(kmask + b * kCh);
         for (int k = 0; k < G.ntok; ++k) {
           const uint32_t bits = __ballot_sync(0xffffffffu, (mask >> k) & 1u);
-          if (lane == 0) kmask[b * kCh + k * 2 + (row >> 5)] = bits;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 v = ok ? reinterpret_cast<const uint4*>(src + kNope)[j] : make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(dst + ((j ^ (row & 7)) << 4)) = v;
+          if (lane == 0) km16[k * 4 + (row0 / kProdRows)] = static_cast<uint16_t>(bits & 0xffffu);
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(raw_empty + s);
-        mbar_arrive(k_full + b);
-        if (warp == kDqWarp0) misc[2] = i + 1;
-      }
+      if (lane == 0) mbar_arrive(k_full + b);
     }
+    cp_async_wait_group<0>();  // no copy may still target shared memory at exit
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------- MMA
     if (lane == 0) {
@@ -866,44 +881,60 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
       const uint32_t idesc_o = umma_idesc_bf16(128, kD, false, true);
       const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
       bool ok = mbar_wait(q_full, 0);
-      auto issue_s = [&](int i) -> bool {
-        const int b = i & 1;
-        if (!mbar_wait(k_full + b, (i >> 1) & 1)) return false;
+      // Q arrived through cp.async (generic proxy); the MMAs read it through
+      // the async proxy
+      fence_proxy_async_smem();
+      auto issue_s = [&](int i) {
+        const int kb = i % kKBufs, sb = i & 1;
         tc_fence_after();
         for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk) {
             const uint32_t qa = q_base + t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32;
-            const uint32_t kb = k_base + b * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32;
-            umma_ss(tmem + s_col(t, b), umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(kb, 16, 1024), idesc_s,
+            const uint32_t ka = k_base + kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32;
+            umma_ss(tmem + s_col(t, sb), umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(ka, 16, 1024), idesc_s,
                     kk > 0 ? 1u : 0u);
           }
         }
-        umma_commit(s_full + b);
-        return true;
+        umma_commit(s_full + sb);
       };
-      if (ok && n > 0) ok = issue_s(0);
-      for (int i = 0; ok && i < n; ++i) {
-        const int b = i & 1;
-        if (i + 1 < n && !issue_s(i + 1)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(p_full + b, (i >> 1) & 1)) {
-          ok = false;
-          break;
-        }
+      auto issue_pv = [&](int i) {
+        const int kb = i % kKBufs, sb = i & 1;
         tc_fence_after();
         for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < kCh / 16; ++kk) {
-            const uint32_t vb = k_base + b * kKBuf + kk * 2048;
-            umma_ts(tmem + t * 128, tmem + s_col(t, b) + kk * 8, umma_desc_sw128(vb, kKRegion, 1024), idesc_o,
+            const uint32_t vb = k_base + kb * kKBuf + kk * 2048;
+            umma_ts(tmem + t * 128, tmem + s_col(t, sb) + kk * 8, umma_desc_sw128(vb, kKRegion, 1024), idesc_o,
                     (i > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        umma_commit(k_empty + b);
-        umma_commit(pv_done + b);
+        umma_commit(k_empty + kb);
+        umma_commit(pv_done + sb);
+      };
+      // Issue S(ns) as soon as its K tile is ready (its TMEM S/P buffer was
+      // last used by chunk ns - 2, whose P.V must already be issued) and
+      // P.V(np) as soon as softmax has written P(np); neither waits for the
+      // other.  Bounded: an error after kWaitLimitNs without progress.
+      int ns = 0, np = 0;
+      uint64_t t_last = global_ns();
+      while (ok && np < n) {
+        bool progressed = false;
+        if (ns < n && ns <= np + 1 && mbar_test(k_full + ns % kKBufs, (ns / kKBufs) & 1)) {
+          issue_s(ns);
+          ++ns;
+          progressed = true;
+        }
+        if (np < ns && mbar_test(p_full + (np & 1), (np >> 1) & 1)) {
+          issue_pv(np);
+          ++np;
+          progressed = true;
+        }
+        if (progressed) {
+          t_last = global_ns();
+        } else {
+          if (global_ns() - t_last > kWaitLimitNs) ok = false;
+        }
       }
       if (!ok) report(err, misc + 1, 4);
     }
@@ -925,32 +956,41 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     bool ok = true;
     if (warp_active) {
       for (int i = 0; i < n; ++i) {
-        const int b = i & 1;
-        if (!mbar_wait(s_full + b, (i >> 1) & 1) || !mbar_wait(k_full + b, (i >> 1) & 1)) {
+        const int b = i & 1, kb = i % kKBufs;
+        if (!mbar_wait(s_full + b, (i >> 1) & 1) || !mbar_wait(k_full + kb, (i / kKBufs) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
         // valid columns of this row's token: bit j of lo / hi = KV row j / 32 + j
-        const uint32_t lo = row_valid ? kmask[b * kCh + tok * 2] : 0u;
-        const uint32_t hi = row_valid ? kmask[b * kCh + tok * 2 + 1] : 0u;
+        const uint32_t lo = row_valid ? kmask[kb * kCh + tok * 2] : 0u;
+        const uint32_t hi = row_valid ? kmask[kb * kCh + tok * 2 + 1] : 0u;
         const bool full = (lo & hi) == 0xffffffffu;
         const uint32_t s_addr = tmem + lane_addr + s_col(t, b);
         uint32_t sr[kCh];
         tmem_ld32(s_addr, sr);
         tmem_ld32(s_addr + 32, sr + 32);
         tmem_wait_ld();
-        float mx = -INFINITY;
-        if (full) {
-#pragma unroll
-          for (int j = 0; j < kCh; ++j) mx = fmaxf(mx, __uint_as_float(sr[j]));
-        } else {
+        // masked columns become -inf: they drop out of the max and 2^-inf = 0
+        if (!full) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            if ((lo >> j) & 1u) mx = fmaxf(mx, __uint_as_float(sr[j]));
-            if ((hi >> j) & 1u) mx = fmaxf(mx, __uint_as_float(sr[32 + j]));
+            sr[j] = ((lo >> j) & 1u) ? sr[j] : 0xff800000u;
+            sr[32 + j] = ((hi >> j) & 1u) ? sr[32 + j] : 0xff800000u;
           }
         }
+        // row max as a tree of 3-input maxima (short dependency chains)
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          m8[k] = fmax3(__uint_as_float(sr[k]), __uint_as_float(sr[k + 8]), __uint_as_float(sr[k + 16]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 24]), __uint_as_float(sr[k + 32]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 40]), __uint_as_float(sr[k + 48]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(sr[k + 56]));
+        float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         mx *= scale;  // scale > 0 commutes with the max
         // raise the running max lazily: only when it grows by more than 2^8
         const bool need = mx > m_used + 8.0f;
@@ -962,26 +1002,26 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
           l *= f;
           m_used = new_m;
         }
-        // P = 2^(s * scale - m) as bf16 pairs over the S columns already read
+        // P = 2^(s * scale - m) as bf16 pairs; exponents by packed FMAs,
+        // row sum in four packed accumulators
         const float nb = m_used == -INFINITY ? 0.0f : -m_used;
-        float rs = 0.0f;
+        const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(nb, nb);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const uint32_t w = hh ? hi : lo;
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            float p0 = ex2_approx(fmaf(__uint_as_float(sr[hh * 32 + 2 * j]), scale, nb));
-            float p1 = ex2_approx(fmaf(__uint_as_float(sr[hh * 32 + 2 * j + 1]), scale, nb));
-            if (!full) {
-              p0 = ((w >> (2 * j)) & 1u) ? p0 : 0.0f;
-              p1 = ((w >> (2 * j + 1)) & 1u) ? p1 : 0.0f;
-            }
-            rs += p0 + p1;
-            pk[j] = pack_bf16(p0, p1);
+            const float2 x = fma2(make_float2(__uint_as_float(sr[hh * 32 + 2 * j]), __uint_as_float(sr[hh * 32 + 2 * j + 1])),
+                                  sc2, nb2);
+            const float2 p2 = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            acc[j & 3] = add2(acc[j & 3], p2);
+            pk[j] = pack_bf16(p2.x, p2.y);
           }
           tmem_st16(s_addr + hh * 16, pk);
         }
+        const float2 a01 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
+        const float rs = a01.x + a01.y;
         l += rs;
         if (rescale && i > 0) {
           // O holds chunks < i at the old max: wait for PV(i-1), then scale it
@@ -1060,12 +1100,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     }
   }
 
-  // ---- teardown: drain any bulk copies still in flight, free TMEM ----
-  __syncthreads();
-  if (warp == kLoadWarp && lane == 0) {
-    for (int k = static_cast<int>(misc[2]); k < issued; ++k)
-      if (!mbar_wait(raw_full + (k % kStages), (k / kStages) & 1)) break;
-  }
+  // ---- teardown: free TMEM ----
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
