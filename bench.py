@@ -66,57 +66,66 @@ def algorithmic_bytes(ctx: np.ndarray, heads: int, head_dim: int) -> int:
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region."""
+    """NVML samples of the SM clock and the clock-event reasons, every 2 ms,
+    during the timed region (read only: no setting of the GPU is touched)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    # nvmlClocksEventReason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.stop = threading.Event()
+        self.handle = None
+
+    def _open(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        return pynvml, h
+
+    def _run(self):
+        nv, h = self.nv, self.handle
+        while not self.stop.is_set():
+            try:
+                mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((mhz, reasons))
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.nv, self.handle = self._open()
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.handle = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.handle is not None:
+            self.t.join(timeout=5)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:7]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        seen = set()
+        for _, r in self.samples:
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    seen.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(sm), "source": "nvml, 2 ms"}
 
 
 def setup_dist():
@@ -169,7 +178,8 @@ def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
     heads, d, r = 64, 128, 64
     cos_sin = C.rope_cos_sin_cache(CTX_HI + 8, r, 160000.0)
     done_tokens, t_total, reqs = 0, 0.0, 0
-    for b in range(len(ctx)):
+    for it in range(100 * len(ctx)):
+        b = it % len(ctx)
         L = int(ctx[b])
         end = L + Q_PER_SEQ
         ncomp = end // 128 + 1
@@ -218,7 +228,7 @@ def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
             break
     per_layer_tok_s = done_tokens / t_total
     return {"value": per_layer_tok_s / LAYERS, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{reqs} of {len(ctx)} config-2 requests x {Q_PER_SEQ} tokens through one HCA layer "
+            "sample": f"{reqs} requests (cycling the {len(ctx)} config-2 requests) x {Q_PER_SEQ} tokens through one HCA layer "
                       f"({t_total:.1f} s), scaled to the {LAYERS}-layer step"}
 
 
@@ -259,6 +269,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="HCA layers per step (37 in the model; fewer only for profiler captures)")
     args = ap.parse_args()
     ws, rank, local = setup_dist()
     if args.impl == "reference":
@@ -277,30 +289,31 @@ def main():
     ctx = contexts(rank)
     batch = make_decode_batch(ctx.tolist(), Q_PER_SEQ, dims, dev, seed=rank, max_model_len=CTX_HI)
     T = batch.num_tokens
-    caches = [alloc_layer_caches(batch, seed=10_000 * rank + l) for l in range(LAYERS)]
-    weights = [random_layer_weights(dims, dev, seed=l) for l in range(LAYERS)]
+    layers = args.layers
+    caches = [alloc_layer_caches(batch, seed=10_000 * rank + l) for l in range(layers)]
+    weights = [random_layer_weights(dims, dev, seed=l) for l in range(layers)]
     g = torch.Generator(device=dev).manual_seed(99 + rank)
-    q_raw = torch.randn((LAYERS, T, dims.heads, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
-    kv = torch.randn((LAYERS, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
-    kv_score = torch.randn((LAYERS, T, 2 * dims.head_dim), generator=g, device=dev)
+    q_raw = torch.randn((layers, T, dims.heads, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    kv = torch.randn((layers, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    kv_score = torch.randn((layers, T, 2 * dims.head_dim), generator=g, device=dev)
     cos_sin = rope_cos_sin_cache(CTX_HI + 8, dims.rope_dim, dims.rope_theta, dev)
     bufs: dict = {}
     splits = args.splits or None
     md = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs)
     q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
     o_buf = torch.empty_like(q_buf)
-    outs = [None] * LAYERS
+    outs = [None] * layers
 
     def step():
         m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=md.num_splits, buffers=bufs)
-        for l in range(LAYERS):
+        for l in range(layers):
             outs[l] = decode_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin,
                                    q_buf=q_buf, o_buf=o_buf)
 
     # metadata: token->req, 2 slot maps, compressed slot map (fill + map),
     # window indices, C128A indices; per layer: insert, state save, compress,
     # attention (+ split-K combine), VHA/inverse-RoPE/FP8
-    launches_per_step = 7 + LAYERS * (5 + (1 if md.num_splits > 1 else 0))
+    launches_per_step = 7 + layers * (5 + (1 if md.num_splits > 1 else 0))
     step()  # warm (allocations, workspace)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
@@ -331,13 +344,13 @@ def main():
 
     # --- dominant kernel: sparse attention, one launch per layer in a graph ---
     attn_graph = torch.cuda.CUDAGraph()
-    qs = [torch.empty_like(q_buf) for _ in range(LAYERS)]
-    for l in range(LAYERS):
+    qs = [torch.empty_like(q_buf) for _ in range(layers)]
+    for l in range(layers):
         ops.fused_qnorm_rope_kv_insert(q_raw[l], kv[l], caches[l].swa, md.swa_slot, batch.positions, cos_sin,
                                        dims.heads, dims.eps, dims.swa_page, dims.rope_dim, out=qs[l])
 
     def attn_all():
-        for l in range(LAYERS):
+        for l in range(layers):
             ops.sparse_decode(qs[l], caches[l].swa, dims.swa_page, md.swa_indices, md.swa_lens, caches[l].comp,
                               dims.comp_page, md.comp_indices, md.comp_lens, dims.head_dim ** -0.5,
                               weights[l].attn_sink, out=o_buf, group_starts=md.group_starts,
@@ -360,7 +373,7 @@ def main():
         attn_graph.replay()
     e1.record()
     torch.cuda.synchronize()
-    attn_us = e0.elapsed_time(e1) * 1e3 / (reps * LAYERS)
+    attn_us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
     algo = algorithmic_bytes(ctx, dims.heads, dims.head_dim)
     hbm, src = peaks()
     achieved = algo / (attn_us * 1e-6) / 1e9
@@ -393,7 +406,7 @@ def main():
         kv.copy_(h_kv, non_blocking=True)
         kv_score.copy_(h_ks, non_blocking=True)
         graph.replay()
-        for l in range(LAYERS):
+        for l in range(layers):
             h_out[l].copy_(outs[l][0].view(torch.uint8), non_blocking=True)
             h_scale[l].copy_(outs[l][1], non_blocking=True)
     t1.record()
@@ -401,6 +414,10 @@ def main():
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps, ws)
     h2d = h_q.numel() * 2 + h_kv.numel() * 2 + h_ks.numel() * 4
     d2h = sum(o[0].numel() + o[1].numel() * 4 for o in outs)
+
+    cache_bytes = sum(t.numel() * t.element_size() for c in caches for t in (c.swa, c.comp, c.state))
+    l2_note = (f"inputs larger than L2: {layers} layers' caches, {cache_bytes / 1e6:.0f} MB, cycled"
+               if cache_bytes > 126e6 else f"caches {cache_bytes / 1e6:.0f} MB fit in L2 (profiling case only)")
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -412,13 +429,14 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x 37 HCA layers",
-                       "parallelism": f"dp{ws}", "layers": LAYERS, "tokens_per_step_per_gpu": T,
-                       "num_splits": md.num_splits, "l2": "inputs larger than L2 (37 layers' caches)",
-                       "per_layer_us": ms * 1e3 / LAYERS},
+            "config": {"workload": f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers",
+                       "parallelism": f"dp{ws}", "layers": layers, "tokens_per_step_per_gpu": T,
+                       "num_splits": md.num_splits, "l2": l2_note,
+                       "per_layer_us": ms * 1e3 / layers},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
-                         "kernel": "hca_attention_kernel (decode)", "launch_us": attn_us,
+                         "kernel": "hca_decode_tc_kernel" + (" + hca_attention_combine_kernel" if md.num_splits > 1 else ""),
+                         "launch_us": attn_us,
                          "algorithmic_bytes": algo},
             "cpu_baseline": cpu,
             "e2e": {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
