@@ -34,6 +34,10 @@ extern "C" {
 #define HCA_E_UNSUPPORTED (-2) /* shape not instantiated in this build */
 #define HCA_E_CUDA (-3)        /* CUDA launch error */
 #define HCA_E_WORKSPACE (-4)   /* workspace too small */
+#define HCA_E_TOO_LARGE (-5)   /* needs more than HCA_NOALLOC_WORKSPACE_BYTES of split-K scratch */
+
+/* Size of the static split-K scratch of hca_sparse_decode_noalloc (16 MiB). */
+#define HCA_NOALLOC_WORKSPACE_BYTES (16ll * 1024 * 1024)
 
 const char* hca_status_string(int status);
 /* Library ABI version (major * 100 + minor). */
@@ -210,6 +214,34 @@ int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_stride_head
                       const int32_t* group_starts, int32_t num_groups, int32_t max_group_tokens,
                       float softmax_scale, const float* attn_sink, int32_t num_splits,
                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* hca_sparse_decode for callers that cannot allocate device memory: a
+ * runtime that owns every allocation itself (its caching allocator must not
+ * be bypassed, or its memory budget is fixed before serving starts) or that
+ * calls from a context where cudaMalloc is not allowed, and so cannot supply
+ * `workspace`.  No counterpart in the reference (FlashMLA's decode takes its
+ * split buffers from the caller).  Same arguments and results as
+ * hca_sparse_decode without workspace / workspace_bytes; the split-K partials
+ * go to a static device array of HCA_NOALLOC_WORKSPACE_BYTES that every GPU
+ * loading this library holds until exit, and a call whose
+ * hca_sparse_decode_workspace_bytes exceeds it returns HCA_E_TOO_LARGE.  No
+ * memory is allocated.  The first call on a device looks up the array's
+ * device address with that device current; make that first call before any
+ * stream capture.  All calls on a GPU share the array: calls whose kernels
+ * overlap on the GPU race, so order them on one stream.  Nothing in the array
+ * needs clearing between calls (each call writes every partial it merges). */
+int hca_sparse_decode_noalloc(void* out, int64_t out_stride_tok, int64_t out_stride_head, float* lse,
+                              const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                              int32_t num_tokens, int32_t num_heads, int32_t head_dim,
+                              int32_t rope_dim, const uint8_t* swa_cache, int32_t swa_page_size,
+                              int64_t swa_page_stride_bytes, const int32_t* swa_indices,
+                              int64_t swa_indices_stride, const int32_t* swa_lens,
+                              const uint8_t* comp_cache, int32_t comp_page_size,
+                              int64_t comp_page_stride_bytes, const int32_t* comp_indices,
+                              int64_t comp_indices_stride, const int32_t* comp_lens,
+                              const int32_t* group_starts, int32_t num_groups,
+                              int32_t max_group_tokens, float softmax_scale,
+                              const float* attn_sink, int32_t num_splits, void* stream);
 
 /* Replaces the chunked gather + flash_mla_sparse_fwd of
  * DeepseekV4FlashMLASparseImpl._forward_prefill

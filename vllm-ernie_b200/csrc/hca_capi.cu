@@ -8,6 +8,7 @@ extern "C" const char* hca_status_string(int status) {
     case HCA_E_UNSUPPORTED: return "shape not instantiated in this build";
     case HCA_E_CUDA: return "CUDA launch error";
     case HCA_E_WORKSPACE: return "workspace too small";
+    case HCA_E_TOO_LARGE: return "needs more split-K scratch than HCA_NOALLOC_WORKSPACE_BYTES";
     default: return "unknown status";
   }
 }
