@@ -86,8 +86,12 @@ def _tp(group) -> tuple[int, int]:
     return dist.get_world_size(group), dist.get_rank(group)
 
 
-def _check_attn_tp(config: Any, tp_size: int) -> None:
-    """TP must divide ``o_groups`` and the head counts (``E/nvidia/attention.py:111-118``)."""
+def _check_attn_tp(config: Any, tp_size: int | None = None) -> None:
+    """TP must divide ``o_groups`` and the head counts (``E/nvidia/attention.py:111-118``).
+    ``tp_size`` defaults to the world size of the default process group (1
+    when none is initialised), the tensor-parallel group of a TP-only run."""
+    if tp_size is None:
+        tp_size = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
     for name in ("o_groups", "num_attention_heads", "hybrid_mla_num_attention_heads"):
         if getattr(config, name) % tp_size:
             raise ValueError(
@@ -105,6 +109,9 @@ class VHAPostMix(nn.Module):
         local = num_heads // self.tp_size
         self.U = nn.Parameter(torch.zeros(local, rank), requires_grad=False)
         self.V = nn.Parameter(torch.zeros(local, rank), requires_grad=False)
+        # checkpoint loaders call param.weight_loader(param, full_tensor)
+        self.U.weight_loader = self.load_local_heads
+        self.V.weight_loader = self.load_local_heads
         if self.tp_size == 1:
             self.register_buffer("m", torch.eye(num_heads), persistent=False)
 

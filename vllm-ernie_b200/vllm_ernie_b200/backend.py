@@ -85,10 +85,12 @@ def get_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int, head
     return (num_blocks, block_size, head_size)
 
 
-def packed_block_stride_alignment(head_dim: int, mla_kv_lora_rank: int, mla_qk_rope_head_dim: int) -> int:
-    """Byte alignment shared by every layer's page
-    (``E/nvidia/attention.py:561-571``)."""
-    return math.lcm(512, head_dim * 2, (mla_kv_lora_rank + mla_qk_rope_head_dim) * 2)
+def packed_block_stride_alignment(vllm_config) -> int:
+    """Byte alignment shared by the pages of every layer in the hybrid KV
+    group (HCA, DSA and indexer), read from
+    ``vllm_config.model_config.hf_config`` (``E/nvidia/attention.py:561-571``)."""
+    cfg = vllm_config.model_config.hf_config
+    return math.lcm(512, cfg.head_dim * 2, (cfg.mla_kv_lora_rank + cfg.mla_qk_rope_head_dim) * 2)
 
 
 # ---------------------------------------------------------------------------
