@@ -305,7 +305,7 @@ def main():
     outs = [None] * layers
 
     def step():
-        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=md.num_splits, buffers=bufs)
+        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs)
         for l in range(layers):
             outs[l] = decode_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin,
                                    q_buf=q_buf, o_buf=o_buf)
@@ -313,7 +313,8 @@ def main():
     # metadata: token->req, 2 slot maps, compressed slot map (fill + map),
     # window indices, C128A indices; per layer: insert, state save, compress,
     # attention (+ split-K combine), VHA/inverse-RoPE/FP8
-    launches_per_step = 7 + layers * (5 + (1 if md.num_splits > 1 else 0))
+    combine = md.schedule is not None or md.num_splits > 1
+    launches_per_step = 7 + (1 if md.schedule is not None else 0) + layers * (5 + (1 if combine else 0))
     step()  # warm (allocations, workspace)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
@@ -354,7 +355,8 @@ def main():
             ops.sparse_decode(qs[l], caches[l].swa, dims.swa_page, md.swa_indices, md.swa_lens, caches[l].comp,
                               dims.comp_page, md.comp_indices, md.comp_lens, dims.head_dim ** -0.5,
                               weights[l].attn_sink, out=o_buf, group_starts=md.group_starts,
-                              max_group_tokens=md.max_group_tokens, num_splits=md.num_splits)
+                              max_group_tokens=md.max_group_tokens, num_splits=md.num_splits,
+                              schedule=md.schedule, max_items=md.max_items)
 
     attn_all()
     torch.cuda.synchronize()
@@ -431,11 +433,13 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers",
                        "parallelism": f"dp{ws}", "layers": layers, "tokens_per_step_per_gpu": T,
-                       "num_splits": md.num_splits, "l2": l2_note,
+                       "split_k": (f"balanced work list, {md.max_items} CTAs" if md.schedule is not None
+                                   else f"{md.num_splits} uniform splits per request"),
+                       "l2": l2_note,
                        "per_layer_us": ms * 1e3 / layers},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
-                         "kernel": "hca_decode_tc_kernel" + (" + hca_attention_combine_kernel" if md.num_splits > 1 else ""),
+                         "kernel": "hca_decode_tc_kernel" + (" + hca_attention_combine_kernel" if combine else ""),
                          "launch_us": attn_us,
                          "algorithmic_bytes": algo},
             "cpu_baseline": cpu,

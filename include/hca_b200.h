@@ -215,6 +215,41 @@ int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_stride_head
                       float softmax_scale, const float* attn_sink, int32_t num_splits,
                       void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Decode work list, built once per step on the device (replaces FlashMLA's
+ * get_mla_metadata -> tile_scheduler_metadata / num_splits, called at
+ * V/models/deepseek_v4/nvidia/flashmla.py:210-302 and
+ * V/v1/attention/backends/mla/flashmla_sparse.py:565-687).  Group g's union
+ * rows (window of its first token + tail of its last token + the last
+ * token's compressed rows) make c_g chunks of 64; the smallest per-CTA chunk
+ * budget whose CTA count fits max_items (at most 16 CTAs per group, at least
+ * one) is chosen, so the longest CTA of one wave is as short as possible.
+ * schedule: int32[hca_decode_schedule_ints(num_groups, max_items)], 16-byte
+ * aligned; max_items >= num_groups (one wave = the SM count).  group_starts
+ * as for hca_sparse_decode (NULL: one token per group, num_groups = tokens);
+ * comp_lens NULL = no compressed rows.  Valid for every layer of the step. */
+int64_t hca_decode_schedule_ints(int32_t num_groups, int32_t max_items);
+int hca_decode_schedule(int32_t* schedule, int32_t max_items, const int32_t* group_starts,
+                        int32_t num_groups, int32_t num_tokens, const int32_t* swa_lens,
+                        const int32_t* comp_lens, void* stream);
+
+/* hca_sparse_decode over a work list from hca_decode_schedule (same
+ * max_items) instead of uniform splits.  Workspace:
+ * hca_sparse_decode_workspace_bytes(1, max_group_tokens, num_heads, head_dim,
+ * max_items) bytes (one partial slot per work item). */
+int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                                float* lse, const void* q, int64_t q_stride_tok,
+                                int64_t q_stride_head, int32_t num_tokens, int32_t num_heads,
+                                int32_t head_dim, int32_t rope_dim, const uint8_t* swa_cache,
+                                int32_t swa_page_size, int64_t swa_page_stride_bytes,
+                                const int32_t* swa_indices, int64_t swa_indices_stride,
+                                const int32_t* swa_lens, const uint8_t* comp_cache,
+                                int32_t comp_page_size, int64_t comp_page_stride_bytes,
+                                const int32_t* comp_indices, int64_t comp_indices_stride,
+                                const int32_t* comp_lens, const int32_t* group_starts,
+                                int32_t num_groups, int32_t max_group_tokens, float softmax_scale,
+                                const float* attn_sink, const int32_t* schedule, int32_t max_items,
+                                void* workspace, int64_t workspace_bytes, void* stream);
+
 /* hca_sparse_decode for callers that cannot allocate device memory: a
  * runtime that owns every allocation itself (its caching allocator must not
  * be bypassed, or its memory budget is fixed before serving starts) or that

@@ -32,7 +32,8 @@ def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_R
     assert rel <= max_rel, (err.max(), rel)
 
 
-def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True):
+def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148):
+    """``splits=None``: the balanced work list for ``sm_count`` CTAs."""
     from vllm_ernie_b200 import ops
     from vllm_ernie_b200.decode import build_decode_metadata
     from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
@@ -41,7 +42,9 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
     maxc = 1024
     b = make_decode_batch(ctx, q_per_seq, dims, DEV, seed=seed, max_model_len=maxc * 128)
     caches = alloc_layer_caches(b, seed=seed + 1)
-    md = build_decode_metadata(b, maxc, num_splits=splits)
+    md = build_decode_metadata(b, maxc, num_splits=splits, sm_count=sm_count)
+    if splits is None:
+        check_schedule(md)
     # index tables vs the oracle builders (bit-exact)
     qsl, sl = b.query_start_loc.cpu().numpy(), b.seq_lens.cpu().numpy()
     t2r = M.token_to_req_indices(qsl)
@@ -72,7 +75,7 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
                             caches.comp if comp else None, 2, md.comp_indices if comp else None,
                             md.comp_lens if comp else None, 128 ** -0.5, sink,
                             group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,
-                            num_splits=md.num_splits)
+                            num_splits=md.num_splits, schedule=md.schedule, max_items=md.max_items)
     ref = A.sparse_decode(q.float().cpu().numpy(), caches.swa.cpu().numpy(), 64, idx, lens,
                           caches.comp.cpu().numpy() if comp else None, 2, gd if comp else None,
                           dl if comp else None, 128 ** -0.5,
@@ -82,12 +85,46 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
     return out
 
 
-@pytest.mark.parametrize("splits", [1, 3])
+def check_schedule(md):
+    """The device work list equals this plain restatement of its rule: the
+    smallest per-CTA chunk budget t (at most 16 CTAs per group) with
+    sum_g max(1, ceil(c_g / t)) <= max_items; group g gets that many CTAs over
+    even chunk ranges, numbered group by group; the rest are idle."""
+    gs = md.group_starts.cpu().numpy()
+    wl = md.swa_lens.cpu().numpy()
+    cl = md.comp_lens.cpu().numpy()
+    c = []
+    for g in range(len(gs) - 1):
+        t0, t1 = gs[g], gs[g + 1]
+        if wl[t0] <= 0:
+            c.append(0)
+            continue
+        rows = wl[t0] + min(t1 - t0 - 1, wl[t1 - 1]) + max(cl[t1 - 1], 0)
+        c.append(-(-rows // 64))
+    maxc = max(c + [1])
+    t = max(1, -(-maxc // 16))
+    while sum(max(1, -(-x // t)) for x in c) > md.max_items:
+        t += 1
+    items, groups = [], []
+    for g, x in enumerate(c):
+        s = max(1, -(-x // t))
+        groups.append((len(items), s))
+        items += [(g, k, k * x // s, (k + 1) * x // s) for k in range(s)]
+    items += [(-1, 0, 0, 0)] * (md.max_items - len(items))
+    got = md.schedule.cpu().numpy()
+    n = md.max_items
+    assert np.array_equal(got[: 4 * n].reshape(n, 4)[:, 0], np.array([i[0] for i in items]))
+    live = [i for i in items if i[0] >= 0]
+    assert np.array_equal(got[: 4 * len(live)].reshape(-1, 4), np.array(live))
+    assert np.array_equal(got[4 * n:].reshape(-1, 2), np.array(groups))
+
+
+@pytest.mark.parametrize("splits", [1, 3, None])
 @pytest.mark.parametrize("q_per_seq", [1, 3])
 def test_decode_mixed_contexts(q_per_seq, splits):
     # short (< window), boundary-crossing, and long contexts
     ctx = [0, 5, 126, 127, 128, 254, 1000, 9000, 40000, 130000]
-    _decode_case(ctx, q_per_seq, 64, splits, seed=11 + q_per_seq + splits)
+    _decode_case(ctx, q_per_seq, 64, splits, seed=11 + q_per_seq + (splits or 7))
 
 
 def test_decode_config2_shape_sample():
@@ -96,6 +133,21 @@ def test_decode_config2_shape_sample():
     rng = np.random.default_rng(0)
     ctx = rng.integers(4096, 131072, size=8).tolist()
     _decode_case(ctx, 3, 64, 4, seed=3)
+
+
+def test_decode_config2_shape_scheduled():
+    """The bench's balanced work list on 64 config-2 requests: multi-CTA
+    groups, single-CTA groups and idle CTAs in one launch."""
+    rng = np.random.default_rng(1)
+    ctx = rng.integers(4096, 131072, size=64).tolist()
+    _decode_case(ctx, 3, 64, None, seed=4)
+
+
+@pytest.mark.parametrize("sm_count", [3, 13, 40])
+def test_decode_schedule_small_waves(sm_count):
+    # few CTAs for many rows: budgets above the 16-split cap, groups with one CTA
+    _decode_case([5, 126, 700, 4000, 9000, 33000, 60000, 131000][: max(1, min(8, sm_count))], 3, 64, None,
+                 seed=17 + sm_count, sm_count=sm_count)
 
 
 @pytest.mark.parametrize("sink_mode", ["neginf", "none"])

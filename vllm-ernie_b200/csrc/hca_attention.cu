@@ -92,9 +92,14 @@ struct AttnParams {
   const float* sink;
   // split-K
   int num_splits;
-  float* ws_o;      // [groups][splits][rows][D]
-  float* ws_ml;     // [groups][splits][rows][2]
+  float* ws_o;      // [groups][splits][rows][D], or [items][rows][D] with a schedule
+  float* ws_ml;     // [groups][splits][rows][2], or [items][rows][2] with a schedule
   int max_rows;     // query rows per group slot in the workspace
+  // decode work list (nullptr: num_splits uniform splits per group):
+  // sched[4 * i .. 4 * i + 3] = {group, split, chunk begin, chunk end} of CTA
+  // i (group -1: idle), then per group {first item, items}
+  const int32_t* sched;
+  int sched_items;
 };
 
 // Resolved description of one group.
@@ -495,10 +500,17 @@ __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnPa
   const int H = P.num_heads;
   const int rows_q = G.ntok * H;
   if (rows_q > P.max_rows) return;
-  const int S = P.num_splits;
+  // the group's partials: S consecutive workspace slots from gbase
+  int S = P.num_splits;
+  int64_t first = static_cast<int64_t>(gidx) * S;
+  if (!kPrefill && P.sched) {
+    first = P.sched[4 * P.sched_items + 2 * gidx];
+    S = P.sched[4 * P.sched_items + 2 * gidx + 1];
+    if (S <= 1) return;  // its only CTA wrote the output itself
+  }
   const int r0 = blockIdx.y * 16;
   if (r0 >= rows_q) return;
-  const int64_t gbase = static_cast<int64_t>(gidx) * S * P.max_rows;
+  const int64_t gbase = first * P.max_rows;
   // weights per (row, split): one warp per 2 rows
   if (threadIdx.x < 16 * 16) {
     const int rr = threadIdx.x >> 4, sp = threadIdx.x & 15;
@@ -640,7 +652,24 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
 
-  const int gidx = blockIdx.y, split = blockIdx.x;
+  // this CTA's work: a (group, chunk range) from the schedule, or split
+  // blockIdx.x of group blockIdx.y; `item` numbers its partial in the workspace
+  int gidx, c_begin, c_end;
+  int64_t item;
+  bool single;  // the group has no other CTA: write the final output directly
+  if (P.sched) {
+    const int4 it = reinterpret_cast<const int4*>(P.sched)[blockIdx.x];
+    if (it.x < 0) return;
+    gidx = it.x;
+    c_begin = it.z;
+    c_end = it.w;
+    item = blockIdx.x;
+    single = P.sched[4 * P.sched_items + 2 * gidx + 1] == 1;
+  } else {
+    gidx = blockIdx.y;
+    item = static_cast<int64_t>(gidx) * P.num_splits + blockIdx.x;
+    single = P.num_splits == 1;
+  }
   Group G;
   if (!resolve_group<false>(P, gidx, G)) return;
   const int H = P.num_heads;
@@ -649,8 +678,13 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   const int ntiles = (rows_q + 127) / 128;
   const int n_u = G.n_win + G.n_comp;
   const int nchunks = (n_u + kCh - 1) / kCh;
-  const int c_begin = static_cast<int>((static_cast<int64_t>(split) * nchunks) / P.num_splits);
-  const int c_end = static_cast<int>((static_cast<int64_t>(split + 1) * nchunks) / P.num_splits);
+  if (!P.sched) {
+    const int split = blockIdx.x;
+    c_begin = static_cast<int>((static_cast<int64_t>(split) * nchunks) / P.num_splits);
+    c_end = static_cast<int>((static_cast<int64_t>(split + 1) * nchunks) / P.num_splits);
+  }
+  if (c_end > nchunks) c_end = nchunks;
+  if (c_begin > c_end) c_begin = c_end;
   const int n = c_end - c_begin;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -1052,7 +1086,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
       if (!ok) report(err, misc + 1, 8);
       // ---- epilogue: normalise (single split) or write the partial ----
       const bool have_o = ok && n > 0 && l > 0.0f;
-      if (P.num_splits == 1) {
+      if (single) {
         const float sink2 = (P.sink && row_valid) ? P.sink[head] * kLog2e : -INFINITY;
         const float inv = have_o ? 1.0f / (l + exp2f(sink2 - m_used)) : 0.0f;
         __nv_bfloat16* orow = P.out + (G.t0 + tok) * P.o_st + head * P.o_sh;
@@ -1076,7 +1110,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
         if (P.lse && row_valid)
           P.lse[(G.t0 + tok) * H + head] = have_o ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
       } else {
-        const int64_t rr = (static_cast<int64_t>(gidx) * P.num_splits + split) * P.max_rows + (row_valid ? r : 0);
+        const int64_t rr = item * P.max_rows + (row_valid ? r : 0);
 #pragma unroll 1
         for (int q4 = 0; q4 < kD / 32; ++q4) {
           uint32_t o[32];
@@ -1106,6 +1140,114 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+// ============================================================================
+// Decode work list (one CTA, kSchedThreads threads).  Group g has c_g chunks
+// of 64 union rows (the decode kernel's own count).  The smallest per-CTA
+// chunk budget t with sum_g max(1, ceil(c_g / t)) <= max_items and at most
+// kSchedMaxSplits CTAs per group is found by bisection; group g then gets
+// s_g = max(1, ceil(c_g / t)) CTAs over even chunk ranges, numbered group by
+// group.  With max_items = one wave of CTAs this minimises the longest CTA.
+// ============================================================================
+constexpr int kSchedThreads = 1024;
+constexpr int kSchedMaxGroups = 8192;
+constexpr int kSchedMaxSplits = 16;
+
+__device__ __forceinline__ int sched_chunks(const int32_t* group_starts, const int32_t* swa_lens,
+                                            const int32_t* comp_lens, int g) {
+  const int t0 = group_starts ? group_starts[g] : g;
+  const int t1 = group_starts ? group_starts[g + 1] : g + 1;
+  const int len0 = swa_lens[t0];
+  if (len0 <= 0) return 0;  // padding group: one CTA writes its zeros
+  const int len_last = swa_lens[t1 - 1];
+  const int extra = min(t1 - t0 - 1, len_last);
+  const int n_comp = comp_lens ? max(comp_lens[t1 - 1], 0) : 0;
+  return (len0 + extra + n_comp + tcd::kCh - 1) / tcd::kCh;
+}
+
+__device__ __forceinline__ int block_sum(int v, int* red) {
+  __syncthreads();
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int s = 0;
+  for (int w = 0; w < kSchedThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+__global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
+    int32_t* sched, int max_items, const int32_t* group_starts, int num_groups, const int32_t* swa_lens,
+    const int32_t* comp_lens) {
+  __shared__ int c_s[kSchedMaxGroups];
+  __shared__ int red[kSchedThreads / 32];
+  int maxc = 1;
+  for (int g = threadIdx.x; g < num_groups; g += kSchedThreads) {
+    c_s[g] = sched_chunks(group_starts, swa_lens, comp_lens, g);
+    maxc = max(maxc, c_s[g]);
+  }
+  for (int o = 16; o > 0; o >>= 1) maxc = max(maxc, __shfl_xor_sync(0xffffffffu, maxc, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = maxc;
+  __syncthreads();
+  for (int w = 0; w < kSchedThreads / 32; ++w) maxc = max(maxc, red[w]);
+  // bisection on the budget t in [lo, hi]; t = hi = maxc always fits
+  // (num_groups <= max_items is checked on the host)
+  int lo = max(1, (maxc + kSchedMaxSplits - 1) / kSchedMaxSplits), hi = max(lo, maxc);
+  while (lo < hi) {
+    const int t = (lo + hi) >> 1;
+    int cnt = 0;
+    for (int g = threadIdx.x; g < num_groups; g += kSchedThreads) cnt += max(1, (c_s[g] + t - 1) / t);
+    if (block_sum(cnt, red) <= max_items)
+      hi = t;
+    else
+      lo = t + 1;
+  }
+  const int t = lo;
+  // exclusive prefix sum of s_g: each thread owns a contiguous run of groups
+  const int per = (num_groups + kSchedThreads - 1) / kSchedThreads;
+  const int g0 = threadIdx.x * per, g1 = min(num_groups, g0 + per);
+  int local = 0;
+  for (int g = g0; g < g1; ++g) local += max(1, (c_s[g] + t - 1) / t);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;  // inclusive scan within the warp, then over warp totals
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = red[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    red[lane] = w;
+  }
+  __syncthreads();
+  int first = incl - local + (warp > 0 ? red[warp - 1] : 0);
+  const int total = red[kSchedThreads / 32 - 1];
+  int32_t* groups = sched + 4 * static_cast<int64_t>(max_items);
+  for (int g = g0; g < g1; ++g) {
+    const int c = c_s[g];
+    const int sg = max(1, (c + t - 1) / t);
+    for (int k = 0; k < sg; ++k) {
+      int4 it;
+      it.x = g;
+      it.y = k;
+      it.z = static_cast<int>((static_cast<int64_t>(k) * c) / sg);
+      it.w = static_cast<int>((static_cast<int64_t>(k + 1) * c) / sg);
+      reinterpret_cast<int4*>(sched)[first + k] = it;
+    }
+    groups[2 * g] = first;
+    groups[2 * g + 1] = sg;
+    first += sg;
+  }
+  // idle slots past the last item
+  for (int i = total + threadIdx.x; i < max_items; i += kSchedThreads)
+    reinterpret_cast<int4*>(sched)[i] = make_int4(-1, 0, 0, 0);
 }
 
 int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
@@ -1161,7 +1303,7 @@ static int launch_attention(const AttnParams& P, int num_groups, int group_token
   return HCA_LAUNCH_STATUS();
 }
 
-extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_stride_head,
+static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_stride_head,
                                  float* lse, const void* q, int64_t q_stride_tok,
                                  int64_t q_stride_head, int32_t num_tokens, int32_t num_heads,
                                  int32_t head_dim, int32_t rope_dim, const uint8_t* swa_cache,
@@ -1173,13 +1315,20 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
                                  const int32_t* comp_lens, const int32_t* group_starts,
                                  int32_t num_groups, int32_t max_group_tokens,
                                  float softmax_scale, const float* attn_sink, int32_t num_splits,
+                                 const int32_t* schedule, int32_t max_items,
                                  void* workspace, int64_t workspace_bytes, void* stream) {
   if (!group_starts) {
     num_groups = num_tokens;
     max_group_tokens = 1;
   }
-  HCA_CHECK_ARG(num_tokens >= 0 && num_groups >= 0 && num_splits >= 1 && num_splits <= 16 &&
-                swa_page_size > 0);
+  HCA_CHECK_ARG(num_tokens >= 0 && num_groups >= 0 && swa_page_size > 0);
+  if (schedule) {
+    HCA_CHECK_ARG(max_items >= num_groups && max_items >= 1 && num_groups <= kSchedMaxGroups &&
+                  reinterpret_cast<uintptr_t>(schedule) % 16 == 0);
+    num_splits = 1;
+  } else {
+    HCA_CHECK_ARG(num_splits >= 1 && num_splits <= 16);
+  }
   if (head_dim != 128 || rope_dim != 64 || num_heads < 1 || max_group_tokens < 1 || max_group_tokens > 30 ||
       max_group_tokens * num_heads > tcd::kMaxRows)
     return HCA_E_UNSUPPORTED;
@@ -1220,12 +1369,17 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
   P.sink = attn_sink;
   P.num_splits = num_splits;
   P.max_rows = max_group_tokens * num_heads;
-  if (num_splits > 1) {
-    const int64_t need = hca_sparse_decode_workspace_bytes(num_groups, max_group_tokens, num_heads,
-                                                           head_dim, num_splits);
+  P.sched = schedule;
+  P.sched_items = schedule ? max_items : 0;
+  // partial slots: groups x splits, or one per work-list item
+  const int32_t slot_groups = schedule ? 1 : num_groups;
+  const int32_t slot_splits = schedule ? max_items : num_splits;
+  if (slot_splits > 1) {
+    const int64_t need = hca_sparse_decode_workspace_bytes(slot_groups, max_group_tokens, num_heads,
+                                                           head_dim, slot_splits);
     if (!workspace || workspace_bytes < need) return HCA_E_WORKSPACE;
     const int64_t rows = static_cast<int64_t>(max_group_tokens) * num_heads;
-    const int64_t o = align_up(static_cast<int64_t>(num_groups) * num_splits * rows * head_dim * 4, 256);
+    const int64_t o = align_up(static_cast<int64_t>(slot_groups) * slot_splits * rows * head_dim * 4, 256);
     const int64_t ml = align_up(static_cast<int64_t>(num_groups) * num_splits * rows * 2 * 4, 256);
     (void)ml;
     char* w = static_cast<char*>(workspace);
@@ -1242,10 +1396,80 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
   }
   int* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
-  hca_decode_tc_kernel<<<dim3(num_splits, num_groups), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
-  if (num_splits > 1)
+  if (schedule)
+    hca_decode_tc_kernel<<<dim3(max_items, 1), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
+  else
+    hca_decode_tc_kernel<<<dim3(num_splits, num_groups), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
+  if (slot_splits > 1)
     hca_attention_combine_kernel<128, false><<<dim3(num_groups, (P.max_rows + 15) / 16), 256, 0, s>>>(P);
   return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                                 float* lse, const void* q, int64_t q_stride_tok,
+                                 int64_t q_stride_head, int32_t num_tokens, int32_t num_heads,
+                                 int32_t head_dim, int32_t rope_dim, const uint8_t* swa_cache,
+                                 int32_t swa_page_size, int64_t swa_page_stride_bytes,
+                                 const int32_t* swa_indices, int64_t swa_indices_stride,
+                                 const int32_t* swa_lens, const uint8_t* comp_cache,
+                                 int32_t comp_page_size, int64_t comp_page_stride_bytes,
+                                 const int32_t* comp_indices, int64_t comp_indices_stride,
+                                 const int32_t* comp_lens, const int32_t* group_starts,
+                                 int32_t num_groups, int32_t max_group_tokens,
+                                 float softmax_scale, const float* attn_sink, int32_t num_splits,
+                                 void* workspace, int64_t workspace_bytes, void* stream) {
+  return sparse_decode_impl(out, out_stride_tok, out_stride_head, lse, q, q_stride_tok, q_stride_head, num_tokens,
+                            num_heads, head_dim, rope_dim, swa_cache, swa_page_size, swa_page_stride_bytes,
+                            swa_indices, swa_indices_stride, swa_lens, comp_cache, comp_page_size,
+                            comp_page_stride_bytes, comp_indices, comp_indices_stride, comp_lens, group_starts,
+                            num_groups, max_group_tokens, softmax_scale, attn_sink, num_splits, nullptr, 0,
+                            workspace, workspace_bytes, stream);
+}
+
+extern "C" int64_t hca_decode_schedule_ints(int32_t num_groups, int32_t max_items) {
+  if (num_groups < 0 || max_items < num_groups || max_items < 1 || num_groups > kSchedMaxGroups) return -1;
+  return 4 * static_cast<int64_t>(max_items) + 2 * static_cast<int64_t>(num_groups);
+}
+
+extern "C" int hca_decode_schedule(int32_t* schedule, int32_t max_items, const int32_t* group_starts,
+                                   int32_t num_groups, int32_t num_tokens, const int32_t* swa_lens,
+                                   const int32_t* comp_lens, void* stream) {
+  HCA_CHECK_ARG(hca_decode_schedule_ints(num_groups, max_items) > 0);
+  HCA_CHECK_ARG(num_tokens >= 0 && (group_starts || num_groups == num_tokens));
+  HCA_CHECK_ARG(schedule && reinterpret_cast<uintptr_t>(schedule) % 16 == 0);
+  if (num_groups == 0) {
+    // every CTA idle
+    hca_decode_schedule_kernel<<<1, kSchedThreads, 0, as_stream(stream)>>>(schedule, max_items, group_starts, 0,
+                                                                           swa_lens, comp_lens);
+    return HCA_LAUNCH_STATUS();
+  }
+  HCA_CHECK_ARG(swa_lens);
+  hca_decode_schedule_kernel<<<1, kSchedThreads, 0, as_stream(stream)>>>(schedule, max_items, group_starts,
+                                                                         num_groups, swa_lens, comp_lens);
+  return HCA_LAUNCH_STATUS();
+}
+
+extern "C" int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                                           float* lse, const void* q, int64_t q_stride_tok,
+                                           int64_t q_stride_head, int32_t num_tokens, int32_t num_heads,
+                                           int32_t head_dim, int32_t rope_dim, const uint8_t* swa_cache,
+                                           int32_t swa_page_size, int64_t swa_page_stride_bytes,
+                                           const int32_t* swa_indices, int64_t swa_indices_stride,
+                                           const int32_t* swa_lens, const uint8_t* comp_cache,
+                                           int32_t comp_page_size, int64_t comp_page_stride_bytes,
+                                           const int32_t* comp_indices, int64_t comp_indices_stride,
+                                           const int32_t* comp_lens, const int32_t* group_starts,
+                                           int32_t num_groups, int32_t max_group_tokens,
+                                           float softmax_scale, const float* attn_sink,
+                                           const int32_t* schedule, int32_t max_items,
+                                           void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!schedule) return HCA_E_INVALID;
+  return sparse_decode_impl(out, out_stride_tok, out_stride_head, lse, q, q_stride_tok, q_stride_head, num_tokens,
+                            num_heads, head_dim, rope_dim, swa_cache, swa_page_size, swa_page_stride_bytes,
+                            swa_indices, swa_indices_stride, swa_lens, comp_cache, comp_page_size,
+                            comp_page_stride_bytes, comp_indices, comp_indices_stride, comp_lens, group_starts,
+                            num_groups, max_group_tokens, softmax_scale, attn_sink, 1, schedule, max_items,
+                            workspace, workspace_bytes, stream);
 }
 
 extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out_stride_head,

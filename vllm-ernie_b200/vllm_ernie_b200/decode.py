@@ -37,6 +37,8 @@ class DecodeMetadata:
     group_starts: torch.Tensor
     max_group_tokens: int
     num_splits: int
+    schedule: torch.Tensor | None = None  # balanced work list (None: uniform num_splits)
+    max_items: int = 0
 
 
 def choose_num_splits(num_groups: int, sm_count: int = SM_COUNT_B200) -> int:
@@ -49,9 +51,11 @@ def choose_num_splits(num_groups: int, sm_count: int = SM_COUNT_B200) -> int:
 
 
 def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: int | None = None,
-                          buffers: dict | None = None) -> DecodeMetadata:
+                          buffers: dict | None = None, sm_count: int = SM_COUNT_B200) -> DecodeMetadata:
     """All per-step index tables, on the device, through the library's
-    builders (bit-exact with the reference's)."""
+    builders (bit-exact with the reference's).  ``num_splits=None`` builds the
+    balanced work list for one wave of ``sm_count`` CTAs; an integer forces
+    that many uniform splits per group."""
     d = batch.dims
     dev = batch.device
     T = batch.num_tokens
@@ -89,9 +93,15 @@ def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: i
         gs = torch.tensor(starts, dtype=torch.int32, device=dev)
     else:
         gs = qsl
-    ns = num_splits if num_splits is not None else choose_num_splits(gs.numel() - 1)
+    ngroups = gs.numel() - 1
+    if num_splits is not None:
+        return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
+                              cidx, clens, gs, max_g, num_splits)
+    items = max(sm_count, ngroups)
+    sched = ops.decode_schedule(gs, T, swa_lens, clens, items, out=buf.get("schedule"))
+    buf["schedule"] = sched
     return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
-                          cidx, clens, gs, max_g, ns)
+                          cidx, clens, gs, max_g, 1, sched, items)
 
 
 @dataclass
@@ -137,7 +147,8 @@ def decode_layer(batch: DecodeBatch, md: DecodeMetadata, caches: LayerCaches, w:
     o = ops.sparse_decode(q, caches.swa, d.swa_page, md.swa_indices, md.swa_lens, caches.comp,
                           d.comp_page, md.comp_indices, md.comp_lens, d.head_dim ** -0.5, w.attn_sink,
                           out=o_buf, group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,
-                          num_splits=md.num_splits, rope_dim=d.rope_dim)
+                          num_splits=md.num_splits, rope_dim=d.rope_dim, schedule=md.schedule,
+                          max_items=md.max_items)
     if not quantize:
         return ops.vha_inv_rope(o, w.vha_mix, batch.positions, cos_sin, d.rope_dim)
     return ops.vha_inv_rope_fp8_quant(o, w.vha_mix, batch.positions, cos_sin, d.n_groups, d.nope,

@@ -230,16 +230,36 @@ class DecodeWorkspace:
 _WS = DecodeWorkspace()
 
 
+def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_items: int, out=None):
+    """Per-step decode work list (the role of FlashMLA's ``get_mla_metadata``
+    tile-scheduler metadata): ``int32[hca_decode_schedule_ints]``, valid for
+    every layer of the step.  ``max_items`` = one wave of CTAs (the SM count,
+    at least the number of groups)."""
+    _check_cuda(swa_lens)
+    num_groups = num_tokens if group_starts is None else group_starts.numel() - 1
+    n = lib().hca_decode_schedule_ints(num_groups, max_items)
+    if n <= 0:
+        raise ValueError(f"decode schedule: max_items={max_items} must cover num_groups={num_groups}")
+    if out is None or out.numel() != n:
+        out = torch.empty(n, dtype=torch.int32, device=swa_lens.device)
+    call("hca_decode_schedule", _p(out), max_items, _p(group_starts), num_groups, num_tokens, _p(swa_lens),
+         _p(comp_lens), _s())
+    return out
+
+
 def sparse_decode(q, swa_cache, swa_block_size: int, swa_indices, swa_lens, comp_cache,
                   comp_block_size: int, comp_indices, comp_lens, softmax_scale: float, attn_sink,
                   out=None, group_starts=None, max_group_tokens: int = 1, num_splits: int = 1,
-                  lse=None, rope_dim: int = 64, workspace: DecodeWorkspace | None = None):
+                  lse=None, rope_dim: int = 64, workspace: DecodeWorkspace | None = None,
+                  schedule=None, max_items: int = 0):
     """Replacement of ``flash_mla_with_kvcache`` for the HCA decode call
     (``V/models/deepseek_v4/nvidia/flashmla.py:286-302``).  ``q`` is
     ``[T, H, D]`` bf16; ``swa_indices``/``comp_indices`` are the builders'
     ``[T, W]`` / ``[T, C]`` int32 tables (any extra middle dim of size 1 is
     accepted); ``group_starts`` groups consecutive-position tokens of one
-    request."""
+    request.  With ``schedule`` (from ``decode_schedule``, same
+    ``max_items``) the CTAs follow its balanced work list and ``num_splits``
+    is unused; otherwise every group gets ``num_splits`` even splits."""
     _check_cuda(q, swa_cache, swa_indices, swa_lens)
     t, h, d = q.shape
     if out is None:
@@ -249,15 +269,20 @@ def sparse_decode(q, swa_cache, swa_block_size: int, swa_indices, swa_lens, comp
     num_groups = t if group_starts is None else group_starts.numel() - 1
     ws = None
     nbytes = 0
-    if num_splits > 1:
-        nbytes = lib().hca_sparse_decode_workspace_bytes(num_groups, max_group_tokens, h, d, num_splits)
+    slots = (1, max_items) if schedule is not None else (num_groups, num_splits)
+    if slots[1] > 1:
+        nbytes = lib().hca_sparse_decode_workspace_bytes(slots[0], max_group_tokens, h, d, slots[1])
         ws = (workspace or _WS).get(nbytes, q.device)
-    call("hca_sparse_decode", _p(out), out.stride(0), out.stride(1), _p(lse), _p(q), q.stride(0),
-         q.stride(1), t, h, d, rope_dim, _p(swa_cache), swa_block_size, swa_cache.stride(0), _p(si),
-         si.stride(0), _p(swa_lens), _p(comp_cache), comp_block_size,
-         comp_cache.stride(0) if comp_cache is not None else 0, _p(ci),
-         ci.stride(0) if ci is not None else 0, _p(comp_lens), _p(group_starts), num_groups,
-         max_group_tokens, softmax_scale, _p(attn_sink), num_splits, _p(ws), nbytes, _s())
+    common = (_p(out), out.stride(0), out.stride(1), _p(lse), _p(q), q.stride(0),
+              q.stride(1), t, h, d, rope_dim, _p(swa_cache), swa_block_size, swa_cache.stride(0), _p(si),
+              si.stride(0), _p(swa_lens), _p(comp_cache), comp_block_size,
+              comp_cache.stride(0) if comp_cache is not None else 0, _p(ci),
+              ci.stride(0) if ci is not None else 0, _p(comp_lens), _p(group_starts), num_groups,
+              max_group_tokens, softmax_scale, _p(attn_sink))
+    if schedule is not None:
+        call("hca_sparse_decode_scheduled", *common, _p(schedule), max_items, _p(ws), nbytes, _s())
+    else:
+        call("hca_sparse_decode", *common, num_splits, _p(ws), nbytes, _s())
     return out
 
 
