@@ -314,7 +314,9 @@ def main():
     # window indices, C128A indices; per layer: insert, state save, compress,
     # attention (+ split-K combine), VHA/inverse-RoPE/FP8
     combine = md.schedule is not None or md.num_splits > 1
-    launches_per_step = 7 + (1 if md.schedule is not None else 0) + layers * (5 + (1 if combine else 0))
+    # scheduled: the split merge is fused into the VHA/quant launch
+    per_layer = 5 if (md.schedule is not None or md.num_splits == 1) else 6
+    launches_per_step = 7 + (1 if md.schedule is not None else 0) + layers * per_layer
     step()  # warm (allocations, workspace)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()

@@ -250,6 +250,31 @@ int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, int64_t out_s
                                 const float* attn_sink, const int32_t* schedule, int32_t max_items,
                                 void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Decode attention fused with the output stage: the scheduled
+ * hca_sparse_decode, whose split partials are merged per token by a second
+ * launch that also applies the VHA head mix, the inverse RoPE and the FP8
+ * quant of wo_a's input (hca_vha_inv_rope_fp8_quant's outputs and layout),
+ * so O never round-trips through memory in bf16.  Replaces the
+ * flash_mla_with_kvcache decode call followed by the plugin's fused
+ * VHA + inverse RoPE + FP8 quant (V/models/deepseek_v4/nvidia/flashmla.py:210-302;
+ * E/nvidia/attention.py:166-285, 471-539).  O is rounded to bf16 before the
+ * mix, as in the unfused path.  D = 128, H % 16 == 0, H <= 64.  Workspace:
+ * hca_sparse_decode_vha_workspace_bytes(max_items, max_group_tokens,
+ * num_heads, head_dim) bytes. */
+int64_t hca_sparse_decode_vha_workspace_bytes(int32_t max_items, int32_t max_group_tokens,
+                                              int32_t num_heads, int32_t head_dim);
+int hca_sparse_decode_vha_fp8_quant(
+    uint8_t* out, int32_t* scale, const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+    int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t rope_dim,
+    const uint8_t* swa_cache, int32_t swa_page_size, int64_t swa_page_stride_bytes,
+    const int32_t* swa_indices, int64_t swa_indices_stride, const int32_t* swa_lens,
+    const uint8_t* comp_cache, int32_t comp_page_size, int64_t comp_page_stride_bytes,
+    const int32_t* comp_indices, int64_t comp_indices_stride, const int32_t* comp_lens,
+    const int32_t* group_starts, int32_t num_groups, int32_t max_group_tokens,
+    float softmax_scale, const float* attn_sink, const int32_t* schedule, int32_t max_items,
+    const void* mix, const int64_t* positions, const float* cos_sin, int64_t cos_sin_stride,
+    int32_t n_groups, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* hca_sparse_decode for callers that cannot allocate device memory: a
  * runtime that owns every allocation itself (its caching allocator must not
  * be bypassed, or its memory budget is fixed before serving starts) or that

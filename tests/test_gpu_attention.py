@@ -260,3 +260,48 @@ def test_decode_layer_hot_path_matches_oracle():
     mix = w.vha_mix.float().cpu().numpy()
     y_ref = O.inv_rope_fp8_quant(np.einsum("hg,tgd->thd", mix, bf16_round(o)), pos, cs, 8, 64, quant=False)
     check_close(y.float().cpu().numpy(), y_ref)
+
+
+def _dequant(data, scale):
+    """e4m3 [T, G, HPG*D] x UE8M0 [T, G, HPG] -> fp32 [T, H, D]."""
+    t, g, w = data.shape
+    hpg = scale.shape[2]
+    x = data.float().view(t, g, hpg, w // hpg)
+    e = (scale.to(torch.int64) & 0xFF).float() - 127.0
+    return (x * torch.exp2(e)[..., None]).reshape(t, g * hpg, w // hpg)
+
+
+def test_decode_fused_vha_quant_matches_unfused():
+    """Scheduled attention fused with the VHA mix + inverse RoPE + FP8 quant
+    equals attention followed by hca_vha_inv_rope_fp8_quant: e4m3 bytes agree
+    except where O's bf16 rounding flips (at most one e4m3 step)."""
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200.decode import build_decode_metadata, random_layer_weights
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dims = HCADims(heads=64)
+    rng = np.random.default_rng(5)
+    ctx = [0, 3, 130] + rng.integers(4096, 131000, size=29).tolist()
+    b = make_decode_batch(ctx, 3, dims, DEV, seed=41, max_model_len=1024 * 128)
+    caches = alloc_layer_caches(b, seed=42)
+    w = random_layer_weights(dims, DEV, seed=43)
+    for sm_count in (148, 40):
+        md = build_decode_metadata(b, 1024, sm_count=sm_count)
+        g = torch.Generator(device=DEV).manual_seed(44)
+        q = torch.randn((b.num_tokens, 64, 128), generator=g, device=DEV).to(torch.bfloat16)
+        cs = rope_cos_sin_cache(1024 * 128 + 8, 64, dims.rope_theta, DEV)
+        args = (q, caches.swa, 64, md.swa_indices, md.swa_lens, caches.comp, 2, md.comp_indices, md.comp_lens,
+                128 ** -0.5, w.attn_sink)
+        o = ops.sparse_decode(*args, group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,
+                              schedule=md.schedule, max_items=md.max_items)
+        d_ref, s_ref = ops.vha_inv_rope_fp8_quant(o, w.vha_mix, b.positions, cs, 8, 64, 64)
+        d_got, s_got = ops.sparse_decode_vha_fp8_quant(*args, md.group_starts, md.max_group_tokens, md.schedule,
+                                                       md.max_items, w.vha_mix, b.positions, cs, 8)
+        torch.cuda.synchronize()
+        assert ops.device_error() == 0
+        same = (d_ref.view(torch.uint8) == d_got.view(torch.uint8)).float().mean().item()
+        assert same > 0.99, same
+        assert (s_ref == s_got).float().mean().item() > 0.99
+        a, r = _dequant(d_got, s_got), _dequant(d_ref, s_ref)
+        assert torch.isfinite(a).all()
+        assert ((a - r).abs() <= 0.07 * torch.maximum(a.abs(), r.abs()) + 1e-6).all()

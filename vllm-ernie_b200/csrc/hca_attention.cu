@@ -100,6 +100,9 @@ struct AttnParams {
   // i (group -1: idle), then per group {first item, items}
   const int32_t* sched;
   int sched_items;
+  // every CTA writes its partial, even a group's only CTA (the merge happens
+  // in the fused combine + VHA kernel)
+  int force_partials;
 };
 
 // Resolved description of one group.
@@ -490,6 +493,7 @@ __global__ void __launch_bounds__(NW * 32, 1) hca_attention_kernel(const AttnPar
 // S partials weighted by 2^(m_s - m), then applies the sink and writes bf16.
 template <int D, bool kPrefill>
 __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnParams P) {
+  pdl_wait_and_release();
   constexpr int kSegs = D / 8;
   static_assert(16 * kSegs <= 256 * 4, "one pass per CTA");
   __shared__ float w_s[16][16 + 1];
@@ -647,6 +651,7 @@ __device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
 }  // namespace tcd
 
 __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const AttnParams P, int* err) {
+  pdl_wait_and_release();
   using namespace tcd;
   using namespace tc;
   extern __shared__ uint8_t smem_dyn[];
@@ -670,6 +675,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     item = static_cast<int64_t>(gidx) * P.num_splits + blockIdx.x;
     single = P.num_splits == 1;
   }
+  if (P.force_partials) single = false;
   Group G;
   if (!resolve_group<false>(P, gidx, G)) return;
   const int H = P.num_heads;
@@ -1250,6 +1256,223 @@ __global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
     reinterpret_cast<int4*>(sched)[i] = make_int4(-1, 0, 0, 0);
 }
 
+// ============================================================================
+// Fused split-K merge + VHA head mix + inverse RoPE + FP8 quant (decode).
+// One CTA (512 threads) per token, padded to a multiple of 4 tokens.
+//   merge: thread (head h = tid / 8, 16-dim segment tid % 8) sums the
+//          group's partials weighted by 2^(m_s - m), applies the sink and
+//          rounds O to bf16 in shared memory (the combine kernel's math);
+//   mix:   warp w < 8: heads 16 (w % 4) .. +15, dims 64 (w / 4) .. +63 of
+//          y = mix @ O (mma.sync m16n8k16 bf16, fp32 accumulate);
+//   out:   inverse GPT-J RoPE on the RoPE dims, per-head amax over the two
+//          dim halves, UE8M0 scale, e4m3 bytes in wo_a's input layout.
+// ============================================================================
+struct VhaOut {
+  uint8_t* out;          // [n_groups][tokens][hpg * D] e4m3
+  int32_t* scale;        // [n_groups * hpg][aligned tokens] UE8M0 exponent bytes
+  const __nv_bfloat16* mix;  // [H][H] bf16, I + V U^T
+  const int64_t* positions;
+  const float* cos_sin;
+  int64_t cs_stride;
+  int num_tokens, aligned_t, n_groups, num_groups;
+};
+
+__global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const AttnParams P, const VhaOut V) {
+  pdl_wait_and_release();
+  constexpr int D = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = D + 8;
+  constexpr int kMaxSplits = 16;
+  __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
+  __shared__ __align__(16) __nv_bfloat16 o_s[kMaxH * kOStride];
+  __shared__ float cs_s[64];
+  __shared__ float amax_s[2][kMaxH];
+  const int H = P.num_heads;
+  const int hpg = H / V.n_groups;
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (t >= V.num_tokens) {
+    for (int h = threadIdx.x; h < H; h += blockDim.x) V.scale[static_cast<int64_t>(h) * V.aligned_t + t] = 0;
+    return;
+  }
+  // start the loads the merge does not wait for: the mix and this token's cos / sin
+  for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
+    const int r = i / (H / 8), c8 = i % (H / 8);
+    *reinterpret_cast<uint4*>(&mix_s[r * kMixStride + c8 * 8]) =
+        *reinterpret_cast<const uint4*>(V.mix + static_cast<int64_t>(r) * H + c8 * 8);
+  }
+  if (threadIdx.x < P.rope_dim) cs_s[threadIdx.x] = V.cos_sin[V.positions[t] * V.cs_stride + threadIdx.x];
+  // the token's group: every warp finds it on its own (ballot over groups
+  // whose start, end and schedule entry are loaded together), so no block
+  // barrier waits on it.  S = 0 (O = 0) if no group holds the token.
+  int first = 0, S = 0, t0 = t;
+  const int32_t* gt = P.sched ? P.sched + 4 * P.sched_items : nullptr;
+  if (!P.group_starts) {
+    first = gt ? gt[2 * t] : t * P.num_splits;
+    S = gt ? gt[2 * t + 1] : P.num_splits;
+  } else {
+    for (int base = 0; base < V.num_groups; base += 128) {
+      int a[4], f[4], sc[4];
+      bool hit[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int g = base + k * 32 + lane;
+        hit[k] = false;
+        a[k] = f[k] = sc[k] = 0;
+        if (g < V.num_groups) {
+          a[k] = P.group_starts[g];
+          const int b = P.group_starts[g + 1];
+          f[k] = gt ? gt[2 * g] : g * P.num_splits;
+          sc[k] = gt ? gt[2 * g + 1] : P.num_splits;
+          hit[k] = a[k] <= t && t < b;
+        }
+      }
+      bool found = false;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const unsigned m = __ballot_sync(0xffffffffu, hit[k]);
+        if (m && !found) {
+          const int src = __ffs(m) - 1;
+          first = __shfl_sync(0xffffffffu, f[k], src);
+          S = __shfl_sync(0xffffffffu, sc[k], src);
+          t0 = __shfl_sync(0xffffffffu, a[k], src);
+          found = true;
+        }
+      }
+      if (found) break;
+    }
+  }
+  // a group larger than the workspace rows was skipped by the attention launch
+  if ((t - t0 + 1) * H > P.max_rows || S > kMaxSplits) S = 0;
+  // ---- merge: thread (head h, 16-dim segment) ----
+  {
+    const int h = threadIdx.x >> 3, seg = threadIdx.x & 7;
+    if (h < H) {
+      const int64_t row = static_cast<int64_t>(t - t0) * H + h;
+      float w[kMaxSplits];
+      float mx = -INFINITY, lw = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplits; ++sp) {
+        w[sp] = 0.0f;
+        if (sp < S) {
+          const int64_t i = ((first + sp) * static_cast<int64_t>(P.max_rows) + row) * 2;
+          const float m = __ldcg(P.ws_ml + i), l = __ldcg(P.ws_ml + i + 1);
+          w[sp] = l > 0.0f ? m : -INFINITY;  // the split's max for now; its weight below
+          if (l > 0.0f) mx = fmaxf(mx, m);
+        }
+      }
+      const float base = mx == -INFINITY ? 0.0f : mx;
+      float acc[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxSplits; ++sp) {
+        if (sp < S) {
+          const int64_t slot = (first + sp) * static_cast<int64_t>(P.max_rows) + row;
+          const float l = __ldcg(P.ws_ml + slot * 2 + 1);
+          const float wt = w[sp] == -INFINITY ? 0.0f : exp2f(w[sp] - base);
+          lw += l > 0.0f ? l * wt : 0.0f;
+          const float4* src = reinterpret_cast<const float4*>(P.ws_o + slot * D + seg * 16);
+          float4 v[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[q] = __ldcg(src + q);
+          // an empty split's row was never written: weight 0, value unused
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[4 * q] += wt != 0.0f ? wt * v[q].x : 0.0f;
+            acc[4 * q + 1] += wt != 0.0f ? wt * v[q].y : 0.0f;
+            acc[4 * q + 2] += wt != 0.0f ? wt * v[q].z : 0.0f;
+            acc[4 * q + 3] += wt != 0.0f ? wt * v[q].w : 0.0f;
+          }
+        }
+      }
+      const float sink2 = P.sink ? P.sink[h] * kLog2e : -INFINITY;
+      const float inv = lw > 0.0f ? 1.0f / (lw + exp2f(sink2 - base)) : 0.0f;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        uint4 pk;
+        pk.x = pack_bf16(acc[8 * q] * inv, acc[8 * q + 1] * inv);
+        pk.y = pack_bf16(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
+        pk.z = pack_bf16(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
+        pk.w = pack_bf16(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
+        *reinterpret_cast<uint4*>(&o_s[h * kOStride + seg * 16 + q * 8]) = pk;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- mix ----
+  const int ht = warp & 3, dh = (warp >> 2) & 1;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int h0 = ht * 16 + gq, h1 = h0 + 8;
+  const bool active = warp < 8 && ht * 16 < H;
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  if (active) {
+    for (int kk = 0; kk < H / 16; ++kk) {
+      uint32_t a[4];
+      ldmatrix_x4(a, &mix_s[(ht * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8]);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, &o_s[(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kOStride + dh * 64 + j * 8 +
+                                  (lane >> 4) * 8]);
+        mma16816(acc[j], a, b);
+        mma16816(acc[j + 1], a, b + 2);
+      }
+    }
+    // inverse GPT-J RoPE on the dims >= nope
+    const int nope = D - P.rope_dim;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = dh * 64 + j * 8 + 2 * cq;
+      if (d >= nope) {
+        const int pr = (d - nope) >> 1;
+        const float c = cs_s[pr], sn = cs_s[P.rope_dim / 2 + pr];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float e = acc[j][2 * hh], od = acc[j][2 * hh + 1];
+          acc[j][2 * hh] = e * c + od * sn;
+          acc[j][2 * hh + 1] = od * c - e * sn;
+        }
+      }
+    }
+    float am0 = 0.0f, am1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      am0 = fmaxf(am0, fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])));
+      am1 = fmaxf(am1, fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])));
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
+    }
+    if (cq == 0) {
+      amax_s[dh][h0] = am0;
+      amax_s[dh][h1] = am1;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+  // ---- quantise: one UE8M0 scale per (head, 128 dims) ----
+  const float a0 = fmaxf(amax_s[0][h0], amax_s[1][h0]), a1 = fmaxf(amax_s[0][h1], amax_s[1][h1]);
+  const int e0 = ue8m0_exponent(a0, 1e-10f, false), e1 = ue8m0_exponent(a1, 1e-10f, false);
+  const float i0 = exp2i(-e0), i1 = exp2i(-e1);
+  uint8_t* r0 = V.out + (static_cast<int64_t>(h0 / hpg) * V.num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
+  uint8_t* r1 = V.out + (static_cast<int64_t>(h1 / hpg) * V.num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = dh * 64 + j * 8 + 2 * cq;
+    *reinterpret_cast<uint16_t*>(r0 + d) =
+        static_cast<uint16_t>(to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8));
+    *reinterpret_cast<uint16_t*>(r1 + d) =
+        static_cast<uint16_t>(to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8));
+  }
+  if (dh == 0 && cq == 0) {
+    V.scale[static_cast<int64_t>(h0) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e0));
+    V.scale[static_cast<int64_t>(h1) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e1));
+  }
+}
+
 int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
@@ -1315,8 +1538,9 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
                                  const int32_t* comp_lens, const int32_t* group_starts,
                                  int32_t num_groups, int32_t max_group_tokens,
                                  float softmax_scale, const float* attn_sink, int32_t num_splits,
-                                 const int32_t* schedule, int32_t max_items,
-                                 void* workspace, int64_t workspace_bytes, void* stream) {
+                                 const int32_t* schedule, int32_t max_items, int fused,
+                                 void* workspace, int64_t workspace_bytes, void* stream,
+                                 AttnParams* fused_params = nullptr) {
   if (!group_starts) {
     num_groups = num_tokens;
     max_group_tokens = 1;
@@ -1371,15 +1595,16 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   P.max_rows = max_group_tokens * num_heads;
   P.sched = schedule;
   P.sched_items = schedule ? max_items : 0;
+  P.force_partials = fused;
   // partial slots: groups x splits, or one per work-list item
   const int32_t slot_groups = schedule ? 1 : num_groups;
   const int32_t slot_splits = schedule ? max_items : num_splits;
-  if (slot_splits > 1) {
-    const int64_t need = hca_sparse_decode_workspace_bytes(slot_groups, max_group_tokens, num_heads,
-                                                           head_dim, slot_splits);
-    if (!workspace || workspace_bytes < need) return HCA_E_WORKSPACE;
+  if (slot_splits > 1 || fused) {
     const int64_t rows = static_cast<int64_t>(max_group_tokens) * num_heads;
-    const int64_t o = align_up(static_cast<int64_t>(slot_groups) * slot_splits * rows * head_dim * 4, 256);
+    const int64_t slots = static_cast<int64_t>(slot_groups) * slot_splits;
+    const int64_t o = align_up(slots * rows * head_dim * 4, 256);
+    const int64_t need = o + align_up(slots * rows * 2 * 4, 256);
+    if (!workspace || workspace_bytes < need) return HCA_E_WORKSPACE;
     const int64_t ml = align_up(static_cast<int64_t>(num_groups) * num_splits * rows * 2 * 4, 256);
     (void)ml;
     char* w = static_cast<char*>(workspace);
@@ -1396,12 +1621,16 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   }
   int* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
-  if (schedule)
-    hca_decode_tc_kernel<<<dim3(max_items, 1), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
-  else
-    hca_decode_tc_kernel<<<dim3(num_splits, num_groups), tcd::kThreads, tcd::kSmemBytes, s>>>(P, err);
+  const int lrc = launch_pdl(hca_decode_tc_kernel, schedule ? dim3(max_items, 1) : dim3(num_splits, num_groups),
+                             dim3(tcd::kThreads), tcd::kSmemBytes, s, P, err);
+  if (lrc != HCA_OK) return lrc;
+  if (fused) {
+    *fused_params = P;
+    return HCA_LAUNCH_STATUS();
+  }
   if (slot_splits > 1)
-    hca_attention_combine_kernel<128, false><<<dim3(num_groups, (P.max_rows + 15) / 16), 256, 0, s>>>(P);
+    return launch_pdl(hca_attention_combine_kernel<128, false>, dim3(num_groups, (P.max_rows + 15) / 16), dim3(256),
+                      0, s, P);
   return HCA_LAUNCH_STATUS();
 }
 
@@ -1422,7 +1651,7 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
                             num_heads, head_dim, rope_dim, swa_cache, swa_page_size, swa_page_stride_bytes,
                             swa_indices, swa_indices_stride, swa_lens, comp_cache, comp_page_size,
                             comp_page_stride_bytes, comp_indices, comp_indices_stride, comp_lens, group_starts,
-                            num_groups, max_group_tokens, softmax_scale, attn_sink, num_splits, nullptr, 0,
+                            num_groups, max_group_tokens, softmax_scale, attn_sink, num_splits, nullptr, 0, 0,
                             workspace, workspace_bytes, stream);
 }
 
@@ -1449,6 +1678,58 @@ extern "C" int hca_decode_schedule(int32_t* schedule, int32_t max_items, const i
   return HCA_LAUNCH_STATUS();
 }
 
+extern "C" int64_t hca_sparse_decode_vha_workspace_bytes(int32_t max_items, int32_t max_group_tokens,
+                                                         int32_t num_heads, int32_t head_dim) {
+  if (max_items < 1 || max_group_tokens < 1 || num_heads < 1 || head_dim < 1) return 0;
+  const int64_t slots = max_items, rows = static_cast<int64_t>(max_group_tokens) * num_heads;
+  return align_up(slots * rows * head_dim * 4, 256) + align_up(slots * rows * 2 * 4, 256);
+}
+
+extern "C" int hca_sparse_decode_vha_fp8_quant(
+    uint8_t* out, int32_t* scale, const void* q, int64_t q_stride_tok, int64_t q_stride_head, int32_t num_tokens,
+    int32_t num_heads, int32_t head_dim, int32_t rope_dim, const uint8_t* swa_cache, int32_t swa_page_size,
+    int64_t swa_page_stride_bytes, const int32_t* swa_indices, int64_t swa_indices_stride, const int32_t* swa_lens,
+    const uint8_t* comp_cache, int32_t comp_page_size, int64_t comp_page_stride_bytes, const int32_t* comp_indices,
+    int64_t comp_indices_stride, const int32_t* comp_lens, const int32_t* group_starts, int32_t num_groups,
+    int32_t max_group_tokens, float softmax_scale, const float* attn_sink, const int32_t* schedule,
+    int32_t max_items, const void* mix, const int64_t* positions, const float* cos_sin, int64_t cos_sin_stride,
+    int32_t n_groups, void* workspace, int64_t workspace_bytes, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && n_groups > 0 && num_heads > 0 && num_heads % n_groups == 0);
+  if (head_dim != 128 || rope_dim != 64 || num_heads % 16 || num_heads > 64) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(out && scale && schedule && mix && positions && cos_sin && workspace);
+  HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(mix) % 16 == 0 && reinterpret_cast<uintptr_t>(workspace) % 16 == 0);
+  // the attention launch writes only split partials here; `out` of the
+  // attention stage is unused, so the (aligned) workspace stands in for it
+  AttnParams P{};
+  const int rc = sparse_decode_impl(workspace, 8, 8, nullptr, q, q_stride_tok, q_stride_head, num_tokens, num_heads,
+                                    head_dim, rope_dim, swa_cache, swa_page_size, swa_page_stride_bytes, swa_indices,
+                                    swa_indices_stride, swa_lens, comp_cache, comp_page_size, comp_page_stride_bytes,
+                                    comp_indices, comp_indices_stride, comp_lens, group_starts, num_groups,
+                                    max_group_tokens, softmax_scale, attn_sink, 1, schedule, max_items, 1, workspace,
+                                    workspace_bytes, stream, &P);
+  if (rc != HCA_OK) return rc;
+  VhaOut V;
+  V.out = out;
+  V.scale = scale;
+  V.mix = static_cast<const __nv_bfloat16*>(mix);
+  V.positions = positions;
+  V.cos_sin = cos_sin;
+  V.cs_stride = cos_sin_stride;
+  V.num_tokens = num_tokens;
+  V.aligned_t = (num_tokens + 3) / 4 * 4;
+  V.n_groups = n_groups;
+  V.num_groups = group_starts ? num_groups : num_tokens;
+  static bool carveout_set = false;  // two CTAs per SM: prefer shared memory over L1 (same value every time)
+  if (!carveout_set) {
+    if (cudaFuncSetAttribute(hca_combine_vha_quant_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      return HCA_E_CUDA;
+    carveout_set = true;
+  }
+  return launch_pdl(hca_combine_vha_quant_kernel, dim3(V.aligned_t), dim3(512), 0, as_stream(stream), P, V);
+}
+
 extern "C" int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, int64_t out_stride_head,
                                            float* lse, const void* q, int64_t q_stride_tok,
                                            int64_t q_stride_head, int32_t num_tokens, int32_t num_heads,
@@ -1468,7 +1749,7 @@ extern "C" int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, in
                             num_heads, head_dim, rope_dim, swa_cache, swa_page_size, swa_page_stride_bytes,
                             swa_indices, swa_indices_stride, swa_lens, comp_cache, comp_page_size,
                             comp_page_stride_bytes, comp_indices, comp_indices_stride, comp_lens, group_starts,
-                            num_groups, max_group_tokens, softmax_scale, attn_sink, 1, schedule, max_items,
+                            num_groups, max_group_tokens, softmax_scale, attn_sink, 1, schedule, max_items, 0,
                             workspace, workspace_bytes, stream);
 }
 

@@ -109,6 +109,7 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
                                             const int64_t* slot_mapping,
                                             const int64_t* positions, const float* cos_sin,
                                             int64_t cs_stride, int rope_dim, float eps) {
+  pdl_wait_and_release();
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
@@ -216,6 +217,7 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
                                            const int64_t* positions, const int64_t* slot_mapping,
                                            int block_size, int head_size, int state_width,
                                            int ratio) {
+  pdl_wait_and_release();
   const int64_t t = blockIdx.x;
   const int64_t slot = slot_mapping[t];
   if (slot < 0) return;
@@ -248,6 +250,7 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
     int block_size, const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride,
     uint8_t* kv_cache, const int64_t* kv_slot, int kv_page_size, int64_t kv_page_stride,
     int rope_dim, int ratio) {
+  pdl_wait_and_release();
   constexpr int kGroups = kCompressThreads / D;
   constexpr int kSub = 32;  // tokens per batch of independent loads
   __shared__ float red[32];
@@ -389,17 +392,10 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
   auto* qo = static_cast<__nv_bfloat16*>(q_out);
   auto* qi = static_cast<const __nv_bfloat16*>(q);
   auto* ki = static_cast<const __nv_bfloat16*>(kv);
-  if (head_dim == 128)
-    qnorm_rope_kv_insert_kernel<128><<<grid, 128, 0, as_stream(stream)>>>(
-        qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi, q_stride_tok, q_stride_head,
-        num_heads, ki, kv_stride, swa_cache, page_size, page_stride_bytes, slot_mapping,
-        positions, cos_sin, cos_sin_stride, rope_dim, eps);
-  else
-    qnorm_rope_kv_insert_kernel<512><<<grid, 128, 0, as_stream(stream)>>>(
-        qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi, q_stride_tok, q_stride_head,
-        num_heads, ki, kv_stride, swa_cache, page_size, page_stride_bytes, slot_mapping,
-        positions, cos_sin, cos_sin_stride, rope_dim, eps);
-  return HCA_LAUNCH_STATUS();
+  return launch_pdl(head_dim == 128 ? qnorm_rope_kv_insert_kernel<128> : qnorm_rope_kv_insert_kernel<512>, grid,
+                    dim3(128), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
+                    q_stride_tok, q_stride_head, num_heads, ki, kv_stride, swa_cache, page_size,
+                    page_stride_bytes, slot_mapping, positions, cos_sin, cos_sin_stride, rope_dim, eps);
 }
 
 extern "C" int hca_quantize_insert_k(uint8_t* cache, int32_t page_size, int64_t page_stride_bytes,
@@ -456,10 +452,9 @@ extern "C" int hca_save_partial_states(float* state, int64_t state_stride_block,
                 state_width >= head_size && compress_ratio > 0);
   if (num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(state && kv && score && ape && positions && slot_mapping);
-  save_partial_states_kernel<<<num_tokens, 128, 0, as_stream(stream)>>>(
-      state, state_stride_block, state_stride_tok, kv, kv_stride, score, score_stride, ape,
-      ape_stride, positions, slot_mapping, block_size, head_size, state_width, compress_ratio);
-  return HCA_LAUNCH_STATUS();
+  return launch_pdl(save_partial_states_kernel, dim3(num_tokens), dim3(128), 0, as_stream(stream), state,
+                    state_stride_block, state_stride_tok, kv, kv_stride, score, score_stride, ape, ape_stride,
+                    positions, slot_mapping, block_size, head_size, state_width, compress_ratio);
 }
 
 extern "C" int hca_compress_norm_rope_store(
@@ -476,17 +471,9 @@ extern "C" int hca_compress_norm_rope_store(
   if (num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(state && token_to_req && positions && state_slot_mapping && block_table &&
                 norm_weight && cos_sin && kv_cache && kv_slot_mapping);
-  if (head_dim == 128)
-    compress_kernel<128><<<num_tokens, kCompressThreads, 0, as_stream(stream)>>>(
-        state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
-        state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
-        cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,
-        compress_ratio);
-  else
-    compress_kernel<512><<<num_tokens, kCompressThreads, 0, as_stream(stream)>>>(
-        state, state_stride_block, state_stride_tok, state_width, token_to_req, positions,
-        state_slot_mapping, block_table, bt_stride, block_size, norm_weight, eps, cos_sin,
-        cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size, kv_page_stride_bytes, rope_dim,
-        compress_ratio);
-  return HCA_LAUNCH_STATUS();
+  return launch_pdl(head_dim == 128 ? compress_kernel<128> : compress_kernel<512>, dim3(num_tokens),
+                    dim3(kCompressThreads), 0, as_stream(stream), state, state_stride_block, state_stride_tok,
+                    state_width, token_to_req, positions, state_slot_mapping, block_table, bt_stride, block_size,
+                    norm_weight, eps, cos_sin, cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size,
+                    kv_page_stride_bytes, rope_dim, compress_ratio);
 }

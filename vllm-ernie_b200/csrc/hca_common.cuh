@@ -23,6 +23,35 @@ constexpr int kQuantBlock = 64;  // NoPE quantisation block of the cached rows
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Programmatic dependent launch for the per-layer chain of kernels.  A kernel
+// launched with launch_pdl may be scheduled while the kernel before it on the
+// stream is still running; it first waits (griddepcontrol.wait) until that
+// kernel has completed and its writes are visible -- before any global read
+// and before any early return, so completion stays transitive along the
+// chain -- and then lets its own successor launch (launch_dependents).  The
+// successor only launches once every CTA of this kernel has started, so its
+// waiting CTAs never hold resources this kernel still needs.  Without a
+// programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void pdl_wait_and_release() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? HCA_OK : HCA_E_CUDA;
+}
+
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
 // Geometry of one cached row: N fp8 bytes + R bf16, then N/64 + 1 scale bytes.

@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(256) vha_mma_kernel(uint8_t* out_fp8, int32_t*
                                                       const int64_t* positions, const float* cos_sin,
                                                       int64_t cs_stride, int num_tokens, int aligned_t,
                                                       int num_heads, int n_groups, int rope_dim) {
+  pdl_wait_and_release();
   constexpr int kCk = 128;             // dims per pass
   constexpr int kMaxH = 64;            // heads of one (TP-local) layer
   constexpr int kMixStride = kMaxH + 8;  // padded rows: conflict-free ldmatrix
@@ -308,15 +309,9 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
         reinterpret_cast<uintptr_t>(mix) % 16)
       return HCA_E_UNSUPPORTED;
     const int threads = (num_heads / 16) * 32;
-    if (head_dim == 128)
-      vha_mma_kernel<128, MODE><<<aligned, threads, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh,
-                                                            mp, positions, cos_sin, cs_stride, num_tokens, aligned,
-                                                            num_heads, n_groups, rope_dim);
-    else
-      vha_mma_kernel<512, MODE><<<aligned, threads, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh,
-                                                            mp, positions, cos_sin, cs_stride, num_tokens, aligned,
-                                                            num_heads, n_groups, rope_dim);
-    return HCA_LAUNCH_STATUS();
+    return launch_pdl(head_dim == 128 ? vha_mma_kernel<128, MODE> : vha_mma_kernel<512, MODE>, dim3(aligned),
+                      dim3(threads), 0, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
+                      cos_sin, cs_stride, num_tokens, aligned, num_heads, n_groups, rope_dim);
   }
   if (head_dim == 128)
     vha_out_kernel<128, MODE><<<aligned, 256, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op,

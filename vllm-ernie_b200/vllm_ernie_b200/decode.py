@@ -144,6 +144,12 @@ def decode_layer(batch: DecodeBatch, md: DecodeMetadata, caches: LayerCaches, w:
                                  batch.state_bt, d.state_page, d.head_dim, cos_sin, caches.comp,
                                  md.comp_slot, d.comp_page, d.head_dim, d.rope_dim, d.ratio,
                                  w.comp_norm, d.eps)
+    if quantize and md.schedule is not None:
+        # attention + VHA + inverse RoPE + FP8 quant without the bf16 O round trip
+        return ops.sparse_decode_vha_fp8_quant(
+            q, caches.swa, d.swa_page, md.swa_indices, md.swa_lens, caches.comp, d.comp_page, md.comp_indices,
+            md.comp_lens, d.head_dim ** -0.5, w.attn_sink, md.group_starts, md.max_group_tokens, md.schedule,
+            md.max_items, w.vha_mix, batch.positions, cos_sin, d.n_groups, d.rope_dim)
     o = ops.sparse_decode(q, caches.swa, d.swa_page, md.swa_indices, md.swa_lens, caches.comp,
                           d.comp_page, md.comp_indices, md.comp_lens, d.head_dim ** -0.5, w.attn_sink,
                           out=o_buf, group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,

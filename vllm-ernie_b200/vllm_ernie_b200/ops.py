@@ -331,6 +331,36 @@ def vha_inv_rope_fp8_quant(o, mix, positions, cos_sin_cache, n_groups: int, nope
     return out.transpose(0, 1), scale.permute(2, 0, 1)[:t]
 
 
+def sparse_decode_vha_fp8_quant(q, swa_cache, swa_block_size: int, swa_indices, swa_lens, comp_cache,
+                                comp_block_size: int, comp_indices, comp_lens, softmax_scale: float,
+                                attn_sink, group_starts, max_group_tokens: int, schedule, max_items: int,
+                                mix, positions, cos_sin_cache, n_groups: int, rope_dim: int = 64,
+                                workspace: DecodeWorkspace | None = None):
+    """Decode attention (scheduled) fused with the VHA mix, inverse RoPE and
+    FP8 quant: ``sparse_decode`` followed by ``vha_inv_rope_fp8_quant`` in two
+    launches, without the bf16 O round trip.  Returns the same
+    ``(data [T, G, HPG*D] e4m3, scale [T, G, HPG] int32)`` views."""
+    _check_cuda(q, swa_cache, swa_indices, swa_lens, mix, positions, cos_sin_cache, schedule)
+    t, h, d = q.shape
+    hpg = h // n_groups
+    out = torch.empty((n_groups, t, hpg * d), dtype=FP8, device=q.device)
+    scale = torch.empty((n_groups, hpg, _aligned(t)), dtype=torch.int32, device=q.device)
+    if t == 0:
+        return out.transpose(0, 1), scale.permute(2, 0, 1)[:t]
+    si = swa_indices.reshape(swa_indices.shape[0], -1)
+    ci = comp_indices.reshape(comp_indices.shape[0], -1) if comp_indices is not None else None
+    num_groups = t if group_starts is None else group_starts.numel() - 1
+    nbytes = lib().hca_sparse_decode_vha_workspace_bytes(max_items, max_group_tokens, h, d)
+    ws = (workspace or _WS).get(nbytes, q.device)
+    call("hca_sparse_decode_vha_fp8_quant", _p(out), _p(scale), _p(q), q.stride(0), q.stride(1), t, h, d,
+         rope_dim, _p(swa_cache), swa_block_size, swa_cache.stride(0), _p(si), si.stride(0), _p(swa_lens),
+         _p(comp_cache), comp_block_size, comp_cache.stride(0) if comp_cache is not None else 0, _p(ci),
+         ci.stride(0) if ci is not None else 0, _p(comp_lens), _p(group_starts), num_groups, max_group_tokens,
+         softmax_scale, _p(attn_sink), _p(schedule), max_items, _p(mix), _p(positions), _p(cos_sin_cache),
+         cos_sin_cache.stride(0), n_groups, _p(ws), nbytes, _s())
+    return out.transpose(0, 1), scale.permute(2, 0, 1)[:t]
+
+
 def fused_inv_rope_fp8_quant(o, positions, cos_sin_cache, n_groups: int, heads_per_group: int,
                              nope_dim: int = 448, rope_dim: int = 64):
     """``V/models/deepseek_v4/common/ops/fused_inv_rope_fp8_quant.py:138-193``
