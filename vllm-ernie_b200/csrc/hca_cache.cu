@@ -257,11 +257,23 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
   __shared__ int64_t row_off[512];
   __shared__ float part[3][kGroups][D];
   const int64_t t = blockIdx.x;
-  if (state_slot[t] < 0) return;
-  const int64_t p = positions[t];
-  if ((p + 1) % ratio != 0) return;
+  // the token's scalars in one round trip (independent loads), then the exit
+  // test; most tokens of a decode step are not at a block boundary
+  const int64_t sslot = state_slot[t], p = positions[t], slot = kv_slot[t];
   const int req = t2r[t];
+  if (sslot < 0 || (p + 1) % ratio != 0) return;
   const int c = threadIdx.x % D, grp = threadIdx.x / D;
+  // loads of the epilogue, issued now so they land during the pooling
+  const float nw = norm_w[c];
+  const RowGeom g = row_geom(D, rope_dim);
+  const int nope = g.nope;
+  float co = 1.0f, si = 0.0f;
+  if (c >= nope) {
+    const float* cs = cos_sin + (p / ratio) * ratio * cs_stride;
+    const int pr = (c - nope) >> 1;
+    co = cs[pr];
+    si = cs[rope_dim / 2 + pr];
+  }
   // Row offsets of the `ratio` states (all positions are >= 0 at a boundary).
   for (int i = threadIdx.x; i < ratio; i += kCompressThreads) {
     const int64_t pos = p - ratio + 1 + i;
@@ -315,12 +327,9 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
   }
   const float ss = block_sum(comp * comp, red);
   if (grp != 0) return;  // no barrier below involves the other groups
-  const float normed = comp * rsqrtf(ss / static_cast<float>(D) + eps) * norm_w[c];
-  const int64_t slot = kv_slot[t];
+  const float normed = comp * rsqrtf(ss / static_cast<float>(D) + eps) * nw;
   if (slot < 0) return;  // uniform across the CTA
-  const RowGeom g = row_geom(D, rope_dim);
   const RowPtr dst = row_ptr(kv_cache, slot, kv_page_size, kv_page_stride, g);
-  const int nope = g.nope;
   // NoPE: UE8M0 quant of the bf16 rounding; 64-channel blocks = 2 warps.
   const float qv = bf16_round(normed);
   float amax = warp_max(c < nope ? fabsf(qv) : 0.0f);
@@ -336,10 +345,6 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
     dst.data[c] = to_e4m3(qv * exp2i(-e));
     if ((c % kQuantBlock) == 0) dst.scale[c / kQuantBlock] = encode_ue8m0(e);
   } else {
-    const int64_t cpos = (p / ratio) * ratio;
-    const float* cs = cos_sin + cpos * cs_stride;
-    const int pr = (c - nope) >> 1;
-    const float co = cs[pr], si = cs[rope_dim / 2 + pr];
     const bool even = ((c - nope) & 1) == 0;
     const float r = even ? normed * co - partner * si : normed * co + partner * si;
     reinterpret_cast<uint16_t*>(dst.data + nope)[c - nope] = float_to_bf16_bits(r);
