@@ -1116,25 +1116,45 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
         if (P.lse && row_valid)
           P.lse[(G.t0 + tok) * H + head] = have_o ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
       } else {
+        // The fp32 partial rows are staged in shared memory (the Q and K
+        // tiles are free once the last MMA has completed) as query-ordered
+        // 512-byte rows whose 16-byte chunks are XOR-swizzled by row, so both
+        // the per-thread row writes and the per-warp row reads below are
+        // bank-conflict free; each warp then stores whole rows, one
+        // coalesced 512-byte line group per instruction.
         const int64_t rr = item * P.max_rows + (row_valid ? r : 0);
+        float* stage = reinterpret_cast<float*>(smem + kQOff);  // [rows][128] fp32
+        const bool any_o = ok && n > 0;
 #pragma unroll 1
         for (int q4 = 0; q4 < kD / 32; ++q4) {
           uint32_t o[32];
-          if (ok && n > 0) {
+          if (any_o) {
             tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
             tmem_wait_ld();
           }
           if (row_valid && have_o) {
-            float4* dst = reinterpret_cast<float4*>(P.ws_o + rr * kD + q4 * 32);
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
-                                   __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+            for (int e = 0; e < 8; ++e) {
+              const int j = q4 * 8 + e;  // 16-byte chunk of the row
+              *reinterpret_cast<float4*>(stage + r * kD + ((j ^ (r & 7)) << 2)) =
+                  make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                              __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+            }
           }
         }
         if (row_valid) {
           P.ws_ml[rr * 2] = have_o ? m_used : -INFINITY;
           P.ws_ml[rr * 2 + 1] = have_o ? l : 0.0f;
+        }
+        if (n > 0) {
+          // the active softmax warps (4 per tile) meet here -- the condition is
+          // uniform across the CTA, even when a wait timed out; rows whose sum
+          // is zero carry whatever the stage holds: the merge never reads them
+          asm volatile("bar.sync 2, %0;\n" ::"r"(ntiles * 128) : "memory");
+          for (int row = warp; row < rows_q; row += ntiles * 4) {
+            const float4 v = *reinterpret_cast<const float4*>(stage + row * kD + ((lane ^ (row & 7)) << 2));
+            reinterpret_cast<float4*>(P.ws_o + (item * P.max_rows + row) * kD)[lane] = v;
+          }
         }
       }
     }
