@@ -305,3 +305,11 @@ def test_decode_fused_vha_quant_matches_unfused():
         a, r = _dequant(d_got, s_got), _dequant(d_ref, s_ref)
         assert torch.isfinite(a).all()
         assert ((a - r).abs() <= 0.07 * torch.maximum(a.abs(), r.abs()) + 1e-6).all()
+
+
+@pytest.mark.parametrize("heads", [1, 8])
+@pytest.mark.parametrize("splits", [1, None])
+def test_decode_few_heads(heads, splits):
+    """Tiles with fewer than 16 query rows (some TMEM lane quadrants empty),
+    e.g. 8 heads per GPU under TP=8."""
+    _decode_case([5, 300, 9000, 70000], 3, heads, splits, seed=23 + heads)

@@ -644,6 +644,14 @@ __device__ __forceinline__ int tile_row_to_query(int tile, int rit, int rows_q) 
   return (ln < q && local < R) ? tile * 128 + local : -1;
 }
 
+// Lane quadrants (softmax warps) of M-tile `tile` that hold query rows.
+__device__ __forceinline__ int active_quads(int tile, int rows_q) {
+  const int R = min(128, rows_q - tile * 128);
+  if (R <= 0) return 0;
+  const int q = (R + 3) >> 2;
+  return (R + q - 1) / q;
+}
+
 __device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
   *s_err = 1;
   if (err) atomicOr(err, code);
@@ -682,6 +690,9 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   const int rows_q = G.ntok * H;
   if (rows_q > kMaxRows || rows_q > P.max_rows) return;
   const int ntiles = (rows_q + 127) / 128;
+  // softmax warps with rows: quadrants 0 .. act0 - 1 of tile 0, 0 .. act1 - 1 of tile 1
+  const int act0 = active_quads(0, rows_q), act1 = active_quads(1, rows_q);
+  const int nact = act0 + act1;
   const int n_u = G.n_win + G.n_comp;
   const int nchunks = (n_u + kCh - 1) / kCh;
   if (!P.sched) {
@@ -721,7 +732,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(s_full + b, 1);
-      mbar_init(p_full + b, 4 * ntiles);
+      mbar_init(p_full + b, nact);  // one arrival per softmax warp with rows
       mbar_init(pv_done + b, 1);
     }
     mbar_init(q_full, kQWarps * 32 + kQWarps);  // per-thread cp.async completions + one arrival per warp
@@ -1147,11 +1158,12 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
           P.ws_ml[rr * 2 + 1] = have_o ? l : 0.0f;
         }
         if (n > 0) {
-          // the active softmax warps (4 per tile) meet here -- the condition is
+          // the softmax warps with rows meet here -- the condition is
           // uniform across the CTA, even when a wait timed out; rows whose sum
           // is zero carry whatever the stage holds: the merge never reads them
-          asm volatile("bar.sync 2, %0;\n" ::"r"(ntiles * 128) : "memory");
-          for (int row = warp; row < rows_q; row += ntiles * 4) {
+          asm volatile("bar.sync 2, %0;\n" ::"r"(nact * 32) : "memory");
+          const int aidx = (warp >> 2) == 0 ? (warp & 3) : act0 + (warp & 3);  // index among active warps
+          for (int row = aidx; row < rows_q; row += nact) {
             const float4 v = *reinterpret_cast<const float4*>(stage + row * kD + ((lane ^ (row & 7)) << 2));
             reinterpret_cast<float4*>(P.ws_o + (item * P.max_rows + row) * kD)[lane] = v;
           }
