@@ -165,11 +165,19 @@ def test_decode_grid_has_idle_splits():
 
 
 def test_prefill_matches_oracle():
+    # prefill chunks: (prior context, chunk length)
+    _prefill_case([(0, 300), (1000, 131), (128 * 7, 64)], 64, seed=22)
+
+
+@pytest.mark.parametrize("heads", [16, 64])
+def test_prefill_long_prior_context(heads):
+    # tiles of 16 (H=16) or 4 (H=64) tokens over many chunks of compressed rows
+    _prefill_case([(20000, 70), (128 * 40 - 3, 9), (5, 250)], heads, seed=31 + heads)
+
+
+def _prefill_case(reqs, heads, seed):
     from vllm_ernie_b200 import ops
 
-    heads = 64
-    # prefill chunks: (prior context, chunk length)
-    reqs = [(0, 300), (1000, 131), (128 * 7, 64)]
     q_lens = np.array([c for _, c in reqs])
     qsl = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
     seq = np.array([p + c for p, c in reqs], np.int32)
@@ -190,7 +198,7 @@ def test_prefill_matches_oracle():
     n_comp = k
     from vllm_ernie_b200.cache_layout import page_bytes
 
-    gen = torch.Generator(device=DEV).manual_seed(22)
+    gen = torch.Generator(device=DEV).manual_seed(seed)
     swa = torch.zeros((n_swa, page_bytes(64, 128, 64)), dtype=torch.uint8, device=DEV)
     comp = torch.zeros((n_comp, page_bytes(2, 128, 64)), dtype=torch.uint8, device=DEV)
     for cache, page, npg in ((swa, 64, n_swa), (comp, 2, n_comp)):
@@ -208,6 +216,7 @@ def test_prefill_matches_oracle():
                                  comp.cpu().numpy(), 2, comp_bt, 128, 128, 128 ** -0.5,
                                  sink.cpu().numpy(), 128, 64)
     check_close(out.float().cpu().numpy(), ref)
+    assert ops.device_error() == 0
 
 
 def test_decode_layer_hot_path_matches_oracle():

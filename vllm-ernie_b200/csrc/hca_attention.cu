@@ -658,7 +658,8 @@ __device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
 }
 }  // namespace tcd
 
-__global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const AttnParams P, int* err) {
+template <bool kPrefill>
+__global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(const AttnParams P, int* err) {
   pdl_wait_and_release();
   using namespace tcd;
   using namespace tc;
@@ -666,11 +667,16 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
 
   // this CTA's work: a (group, chunk range) from the schedule, or split
-  // blockIdx.x of group blockIdx.y; `item` numbers its partial in the workspace
-  int gidx, c_begin, c_end;
+  // blockIdx.x of group blockIdx.y; `item` numbers its partial in the workspace.
+  // Prefill: tile blockIdx.x of the requests' tokens, all of its rows.
+  int gidx, c_begin = 0, c_end = 1 << 30;
   int64_t item;
   bool single;  // the group has no other CTA: write the final output directly
-  if (P.sched) {
+  if (kPrefill) {
+    gidx = blockIdx.x;
+    item = gidx;
+    single = true;
+  } else if (P.sched) {
     const int4 it = reinterpret_cast<const int4*>(P.sched)[blockIdx.x];
     if (it.x < 0) return;
     gidx = it.x;
@@ -685,7 +691,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   }
   if (P.force_partials) single = false;
   Group G;
-  if (!resolve_group<false>(P, gidx, G)) return;
+  if (!resolve_group<kPrefill>(P, gidx, G)) return;
   const int H = P.num_heads;
   const int rows_q = G.ntok * H;
   if (rows_q > kMaxRows || rows_q > P.max_rows) return;
@@ -695,7 +701,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
   const int nact = act0 + act1;
   const int n_u = G.n_win + G.n_comp;
   const int nchunks = (n_u + kCh - 1) / kCh;
-  if (!P.sched) {
+  if (!kPrefill && !P.sched) {
     const int split = blockIdx.x;
     c_begin = static_cast<int>((static_cast<int64_t>(split) * nchunks) / P.num_splits);
     c_end = static_cast<int>((static_cast<int64_t>(split + 1) * nchunks) / P.num_splits);
@@ -739,7 +745,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
     misc[1] = 0;
     mbar_fence_init();
   }
-  if (threadIdx.x < G.ntok) {
+  if (!kPrefill && threadIdx.x < G.ntok) {
     tok_len[threadIdx.x] = P.swa_lens[G.t0 + threadIdx.x];
     tok_clen[threadIdx.x] = P.comp_cache ? P.comp_lens[G.t0 + threadIdx.x] : 0;
   }
@@ -790,7 +796,19 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_decode_tc_kernel(const A
       R.slot = -1;
       R.mask = 0;
       R.comp = false;
-      if (lane < kProdRows && u < n_u) {
+      if (kPrefill) {
+        // positions: window row u is position win_start + u, compressed row
+        // u - n_win is entry u - n_win; slots through the block tables
+        if (lane < kProdRows && u < n_u) {
+          bool comp;
+          int64_t slot;
+          uint32_t m;
+          row_source<true>(P, G, u, comp, slot, m);
+          R.slot = slot;
+          R.comp = comp;
+          R.mask = m;
+        }
+      } else if (lane < kProdRows && u < n_u) {
         uint32_t m = 0;
         if (u < G.n_win) {
           R.slot = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
@@ -1646,14 +1664,14 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   cudaStream_t s = as_stream(stream);
   static bool smem_set = false;  // one attribute call per process (same value every time)
   if (!smem_set) {
-    if (cudaFuncSetAttribute(hca_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(hca_tc_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              tcd::kSmemBytes) != cudaSuccess)
       return HCA_E_CUDA;
     smem_set = true;
   }
   int* err = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
-  const int lrc = launch_pdl(hca_decode_tc_kernel, schedule ? dim3(max_items, 1) : dim3(num_splits, num_groups),
+  const int lrc = launch_pdl(hca_tc_attention_kernel<false>, schedule ? dim3(max_items, 1) : dim3(num_splits, num_groups),
                              dim3(tcd::kThreads), tcd::kSmemBytes, s, P, err);
   if (lrc != HCA_OK) return lrc;
   if (fused) {
@@ -1835,6 +1853,29 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
   P.scale_log2 = softmax_scale * kLog2e;
   P.sink = attn_sink;
   P.num_splits = 1;
+  if (head_dim == 128 && rope_dim == 64 && num_heads <= tcd::kMaxRows) {
+    // tcgen05 path: tiles of up to 256 query rows (at most 32 tokens, one
+    // mask bit each), all of a tile's rows in one CTA
+    const int tc_tokens = min(32, tcd::kMaxRows / num_heads);
+    P.group_tokens = tc_tokens;
+    P.max_rows = tc_tokens * num_heads;
+    HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(swa_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(comp_cache) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride_tok % 8 == 0 && q_stride_head % 8 == 0);
+    HCA_CHECK_ARG(out_stride_head % 8 == 0 && out_stride_tok % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    static bool smem_set = false;  // one attribute call per process (same value every time)
+    if (!smem_set) {
+      if (cudaFuncSetAttribute(hca_tc_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               tcd::kSmemBytes) != cudaSuccess)
+        return HCA_E_CUDA;
+      smem_set = true;
+    }
+    int* err = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
+    // tiles never straddle requests: at most tokens / G + requests of them
+    const int num_tiles = num_tokens / tc_tokens + num_reqs;
+    return launch_pdl(hca_tc_attention_kernel<true>, dim3(num_tiles), dim3(tcd::kThreads), tcd::kSmemBytes,
+                      as_stream(stream), P, err);
+  }
   // tiles never straddle requests: at most tokens / G + requests of them
   const int num_tiles = num_tokens / group_tokens + num_reqs;
   return launch_attention<true>(P, num_tiles, group_tokens, as_stream(stream));
