@@ -257,6 +257,142 @@ def run_reference(args, ws, rank):
 
 
 # ---------------------------------------------------------------------------
+# prefill workload (config 3): a supplementary line, not the headline metric
+# ---------------------------------------------------------------------------
+
+PREFILL_SEQS, PREFILL_CHUNK = 8, 8192
+PREFILL_METRIC = "HCA chunked-prefill tokens/s & tensor roofline % (8 x 8192-token chunks, prior 0-120K, fp8 KV)"
+
+
+def prefill_contexts(rank: int) -> np.ndarray:
+    rng = np.random.default_rng(4321 + rank)
+    return 128 * rng.integers(0, 960, size=PREFILL_SEQS, endpoint=True)
+
+
+def prefill_flops(ctx: np.ndarray, heads: int, head_dim: int) -> float:
+    """Attention FLOPs of one layer: sum over query tokens of
+    heads x rows x 4 D, rows = (p + 1) // 128 + min(p + 1, 128)."""
+    tot = 0
+    for c in ctx.tolist():
+        p = np.arange(c, c + PREFILL_CHUNK, dtype=np.int64)
+        tot += int(((p + 1) // 128 + np.minimum(p + 1, 128)).sum())
+    return float(tot) * heads * 4 * head_dim
+
+
+def run_prefill(args, ws, rank, local):
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200.decode import build_prefill_metadata, prefill_layer, random_layer_weights
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dev = torch.device("cuda", local)
+    dims = HCADims(heads=64, head_dim=128, rope_dim=64, n_groups=8)
+    ctx = prefill_contexts(rank)
+    batch = make_decode_batch(ctx.tolist(), PREFILL_CHUNK, dims, dev, seed=rank, max_model_len=CTX_HI)
+    T = batch.num_tokens
+    layers = args.layers if args.layers != LAYERS else 4
+    caches = [alloc_layer_caches(batch, seed=20_000 * rank + l) for l in range(layers)]
+    weights = [random_layer_weights(dims, dev, seed=l) for l in range(layers)]
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    q_raw = [torch.randn((T, dims.heads, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+             for _ in range(layers)]
+    kv = torch.randn((layers, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
+    kv_score = torch.randn((layers, T, 2 * dims.head_dim), generator=g, device=dev)
+    cos_sin = rope_cos_sin_cache(CTX_HI + PREFILL_CHUNK + 8, dims.rope_dim, dims.rope_theta, dev)
+    bufs: dict = {}
+    q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
+    o_buf = torch.empty_like(q_buf)
+
+    def step():
+        m = build_prefill_metadata(batch, buffers=bufs)
+        for l in range(layers):
+            prefill_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin, q_buf=q_buf,
+                          o_buf=o_buf)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(ws)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, ws)
+
+    # the attention launch alone, back to back over the layers
+    md = build_prefill_metadata(batch, buffers=bufs)
+    qs = [ops.fused_qnorm_rope_kv_insert(q_raw[l], kv[l], caches[l].swa, md.swa_slot, batch.positions, cos_sin,
+                                         dims.heads, dims.eps, dims.swa_page, dims.rope_dim) for l in range(layers)]
+
+    def attn_all():
+        for l in range(layers):
+            ops.sparse_prefill(qs[l], batch.query_start_loc, batch.seq_lens, caches[l].swa, dims.swa_page,
+                               batch.swa_bt, caches[l].comp, dims.comp_page, batch.comp_bt, dims.window, dims.ratio,
+                               dims.head_dim ** -0.5, weights[l].attn_sink, out=o_buf, rope_dim=dims.rope_dim)
+
+    attn_all()
+    torch.cuda.synchronize()
+    ag = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        attn_all()
+    torch.cuda.current_stream().wait_stream(s)
+    with torch.cuda.graph(ag):
+        attn_all()
+    ag.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, min(args.steps, 10))
+    e0.record()
+    for _ in range(reps):
+        ag.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    attn_us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
+    flops = prefill_flops(ctx, dims.heads, dims.head_dim)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        peak, src = 1590.0, "fallback"
+    achieved = flops / (attn_us * 1e-6) / 1e12
+    if rank == 0:
+        line = {
+            "metric": PREFILL_METRIC, "value": ws * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"config 3 (8 x 8192-token chunks, prior 128*U[0,960], H=64, D=128, fp8 KV) "
+                                   f"x {layers} HCA layers", "parallelism": f"dp{ws}", "layers": layers,
+                       "tokens_per_step_per_gpu": T, "per_layer_us": ms * 1e3 / layers,
+                       "l2": "inputs larger than L2 (1 GB of Q per layer)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": src,
+                         "kernel": "hca_tc_attention_kernel<prefill>", "launch_us": attn_us,
+                         "algorithmic_flops": flops},
+            "cpu_baseline": None, "e2e": None,
+            "gpu_launches": (4 + 5 * layers) * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph, ag
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 
@@ -269,6 +405,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: the headline metric (config 2); prefill: config 3, a supplementary line")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="HCA layers per step (37 in the model; fewer only for profiler captures)")
     args = ap.parse_args()
@@ -277,6 +415,9 @@ def main():
         run_reference(args, ws, rank)
         if ws > 1:
             torch.distributed.destroy_process_group()
+        return
+    if args.workload == "prefill":
+        run_prefill(args, ws, rank, local)
         return
 
     from vllm_ernie_b200 import ops

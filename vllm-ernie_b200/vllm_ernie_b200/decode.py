@@ -159,3 +159,62 @@ def decode_layer(batch: DecodeBatch, md: DecodeMetadata, caches: LayerCaches, w:
         return ops.vha_inv_rope(o, w.vha_mix, batch.positions, cos_sin, d.rope_dim)
     return ops.vha_inv_rope_fp8_quant(o, w.vha_mix, batch.positions, cos_sin, d.n_groups, d.nope,
                                       d.rope_dim)
+
+
+# ---------------------------------------------------------------------------
+# chunked prefill (the same layer path over a chunk of tokens per request)
+# ---------------------------------------------------------------------------
+
+
+@dataclass
+class PrefillMetadata:
+    num_tokens: int
+    token_to_req: torch.Tensor
+    swa_slot: torch.Tensor
+    state_slot: torch.Tensor
+    comp_slot: torch.Tensor
+
+
+def build_prefill_metadata(batch: DecodeBatch, buffers: dict | None = None) -> PrefillMetadata:
+    """Per-step slot maps of a prefill chunk (the attention reads the caches
+    through the block tables, so no index tables are built)."""
+    d = batch.dims
+    T = batch.num_tokens
+    qsl, sl = batch.query_start_loc, batch.seq_lens
+    buf = buffers if buffers is not None else {}
+
+    def get(name, shape, dtype):
+        t = buf.get(name)
+        if t is None or t.shape != shape:
+            t = torch.empty(shape, dtype=dtype, device=batch.device)
+            buf[name] = t
+        return t
+
+    t2r = ops.token_to_req_indices(qsl, T, out=get("t2r", (T,), torch.int32))
+    swa_slot = ops.slot_mapping(qsl, sl, batch.swa_bt, d.swa_page, T, out=get("swa_slot", (T,), torch.int64))
+    state_slot = ops.slot_mapping(qsl, sl, batch.state_bt, d.state_page, T, out=get("state_slot", (T,), torch.int64))
+    comp_slot = ops.get_compressed_slot_mapping(T, qsl, sl, batch.comp_bt, d.comp_page, d.ratio,
+                                                out=get("comp_slot", (T,), torch.int64))
+    return PrefillMetadata(T, t2r, swa_slot, state_slot, comp_slot)
+
+
+def prefill_layer(batch: DecodeBatch, md: PrefillMetadata, caches: LayerCaches, w: LayerWeights,
+                  q_raw: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor, cos_sin: torch.Tensor,
+                  q_buf: torch.Tensor | None = None, o_buf: torch.Tensor | None = None):
+    """One layer of the chunked-prefill path: Q prep + SWA insert, state save,
+    block compression (every completed 128-block of the chunk), attention
+    straight from the fp8 caches, VHA + inverse RoPE + FP8 quant."""
+    d = batch.dims
+    T = md.num_tokens
+    q = ops.fused_qnorm_rope_kv_insert(q_raw, kv, caches.swa, md.swa_slot, batch.positions, cos_sin,
+                                       d.heads, d.eps, d.swa_page, d.rope_dim, out=q_buf)
+    ops.save_partial_states(kv_score[:, : d.head_dim], kv_score[:, d.head_dim:], w.ape, batch.positions,
+                            caches.state, md.state_slot, d.state_page, d.head_dim, d.ratio)
+    ops.compress_norm_rope_store(caches.state, T, md.token_to_req, batch.positions, md.state_slot,
+                                 batch.state_bt, d.state_page, d.head_dim, cos_sin, caches.comp,
+                                 md.comp_slot, d.comp_page, d.head_dim, d.rope_dim, d.ratio,
+                                 w.comp_norm, d.eps)
+    o = ops.sparse_prefill(q, batch.query_start_loc, batch.seq_lens, caches.swa, d.swa_page, batch.swa_bt,
+                           caches.comp, d.comp_page, batch.comp_bt, d.window, d.ratio, d.head_dim ** -0.5,
+                           w.attn_sink, out=o_buf, rope_dim=d.rope_dim)
+    return ops.vha_inv_rope_fp8_quant(o, w.vha_mix, batch.positions, cos_sin, d.n_groups, d.nope, d.rope_dim)
