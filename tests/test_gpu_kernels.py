@@ -253,10 +253,11 @@ def test_vha_inv_rope_fp8_quant_matches_plugin_kernel(ops):
     assert np.linalg.norm(a - b) / np.linalg.norm(b) < 0.03
 
 
-@pytest.mark.parametrize("head_dim", [128, 512])
-def test_vha_inv_rope_fp8_quant_matches_oracle(ops, head_dim):
-    rng = np.random.default_rng(head_dim + 7)
-    t, h, G, r = 13, 64, 8, 64
+@pytest.mark.parametrize("head_dim,t", [(128, 13), (512, 13), (128, 1501), (512, 1501), (128, 4099)])
+def test_vha_inv_rope_fp8_quant_matches_oracle(ops, head_dim, t):
+    # 1501 / 4099 tokens: several tokens per CTA (double-buffered loads), ragged last CTA
+    rng = np.random.default_rng(head_dim + 7 + t)
+    h, G, r = 64, 8, 64
     o = bf16_round(rng.standard_normal((t, h, head_dim)).astype(np.float32))
     u = rng.standard_normal((h, 16)).astype(np.float32) / 8
     v = rng.standard_normal((h, 16)).astype(np.float32) / 8

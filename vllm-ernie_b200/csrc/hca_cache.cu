@@ -43,13 +43,42 @@ __global__ void qk_rmsnorm_kernel(__nv_bfloat16* q_out, int64_t q_out_stride,
 template <int D>
 struct WarpRow {
   static constexpr int E = D / 32;  // elements per lane
-  static_assert(E % 2 == 0 && E >= 2, "head_dim must be a multiple of 64");
+  static_assert(E % 4 == 0, "head_dim must be a multiple of 128");
   float v[E];
 
   __device__ __forceinline__ void load_bf16(const __nv_bfloat16* row, int lane) {
     const uint16_t* p = reinterpret_cast<const uint16_t*>(row) + lane * E;
+    if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+      // E % 4 == 0 here: 8-byte vector loads
 #pragma unroll
-    for (int i = 0; i < E; ++i) v[i] = bf16_bits_to_float(p[i]);
+      for (int i = 0; i < E; i += 4) {
+        const uint2 w = *reinterpret_cast<const uint2*>(p + i);
+        v[i] = bf16_bits_to_float(static_cast<uint16_t>(w.x & 0xffff));
+        v[i + 1] = bf16_bits_to_float(static_cast<uint16_t>(w.x >> 16));
+        v[i + 2] = bf16_bits_to_float(static_cast<uint16_t>(w.y & 0xffff));
+        v[i + 3] = bf16_bits_to_float(static_cast<uint16_t>(w.y >> 16));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) v[i] = bf16_bits_to_float(p[i]);
+    }
+  }
+
+  // bf16 of every element, 8-byte vector stores when aligned
+  __device__ __forceinline__ void store_bf16(__nv_bfloat16* row, int lane) const {
+    uint16_t* o = reinterpret_cast<uint16_t*>(row) + lane * E;
+    if ((reinterpret_cast<uintptr_t>(o) & 7) == 0) {
+#pragma unroll
+      for (int i = 0; i < E; i += 4) {
+        uint2 w;
+        w.x = static_cast<uint32_t>(float_to_bf16_bits(v[i])) | (static_cast<uint32_t>(float_to_bf16_bits(v[i + 1])) << 16);
+        w.y = static_cast<uint32_t>(float_to_bf16_bits(v[i + 2])) | (static_cast<uint32_t>(float_to_bf16_bits(v[i + 3])) << 16);
+        *reinterpret_cast<uint2*>(o + i) = w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) o[i] = float_to_bf16_bits(v[i]);
+    }
   }
 
   // GPT-J rotation of the pairs that fall in the last R dims.
@@ -126,9 +155,7 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
 #pragma unroll
     for (int i = 0; i < WarpRow<D>::E; ++i) row.v[i] *= rrms;
     row.rope(cs, rope_dim, lane, false);
-    uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * WarpRow<D>::E;
-#pragma unroll
-    for (int i = 0; i < WarpRow<D>::E; ++i) o[i] = float_to_bf16_bits(row.v[i]);
+    row.store_bf16(q_out + t * qo_st + h * qo_sh, lane);
   } else if (h < padded_heads) {
     uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * WarpRow<D>::E;
 #pragma unroll
@@ -233,7 +260,8 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
 }
 
 // ----------------------------------------------------------------------------
-// Block compressor: one 512-thread CTA per boundary token.  Thread (g, c)
+// Block compressor: a 512-thread CTA per 32 tokens pools each of them that
+// completes a block.  Thread (g, c)
 // owns channel c of token group g (512 / D groups split the `ratio` pooled
 // tokens); each thread pools its tokens 32 at a time with independent loads
 // (online softmax per channel), the groups merge in shared memory, then the
@@ -243,25 +271,19 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
 // ----------------------------------------------------------------------------
 constexpr int kCompressThreads = 512;
 
+// Pool, normalise, quantise and store the block completed by token t (the
+// whole CTA; returns with every thread past its last barrier).
 template <int D>
-__global__ void __launch_bounds__(kCompressThreads) compress_kernel(
-    const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
-    const int64_t* positions, const int64_t* state_slot, const int32_t* bt, int64_t bt_stride,
-    int block_size, const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride,
-    uint8_t* kv_cache, const int64_t* kv_slot, int kv_page_size, int64_t kv_page_stride,
-    int rope_dim, int ratio) {
-  pdl_wait_and_release();
+__device__ __forceinline__ void compress_token(
+    int64_t t, const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
+    const int64_t* positions, const int64_t* kv_slot, const int32_t* bt, int64_t bt_stride, int block_size,
+    const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride, uint8_t* kv_cache, int kv_page_size,
+    int64_t kv_page_stride, int rope_dim, int ratio, float* red, int64_t* row_off, float* part_flat) {
   constexpr int kGroups = kCompressThreads / D;
-  constexpr int kSub = 32;  // tokens per batch of independent loads
-  __shared__ float red[32];
-  __shared__ int64_t row_off[512];
-  __shared__ float part[3][kGroups][D];
-  const int64_t t = blockIdx.x;
-  // the token's scalars in one round trip (independent loads), then the exit
-  // test; most tokens of a decode step are not at a block boundary
-  const int64_t sslot = state_slot[t], p = positions[t], slot = kv_slot[t];
+  constexpr int kSub = 32;
+  float(*part)[kGroups][D] = reinterpret_cast<float(*)[kGroups][D]>(part_flat);
+  const int64_t p = positions[t], slot = kv_slot[t];
   const int req = t2r[t];
-  if (sslot < 0 || (p + 1) % ratio != 0) return;
   const int c = threadIdx.x % D, grp = threadIdx.x / D;
   // loads of the epilogue, issued now so they land during the pooling
   const float nw = norm_w[c];
@@ -350,6 +372,47 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
     reinterpret_cast<uint16_t*>(dst.data + nope)[c - nope] = float_to_bf16_bits(r);
   }
   if (c == 0) dst.scale[nope / kQuantBlock] = 0;
+}
+
+
+template <int D>
+__global__ void __launch_bounds__(kCompressThreads) compress_kernel(
+    const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
+    const int64_t* positions, const int64_t* state_slot, const int32_t* bt, int64_t bt_stride,
+    int block_size, const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride,
+    uint8_t* kv_cache, const int64_t* kv_slot, int kv_page_size, int64_t kv_page_stride,
+    int rope_dim, int ratio, int64_t num_tokens) {
+  pdl_wait_and_release();
+  constexpr int kGroups = kCompressThreads / D;
+  constexpr int kSub = 32;  // tokens per batch of independent loads
+  __shared__ float red[32];
+  __shared__ int64_t row_off[512];
+  __shared__ float part[3][kGroups][D];
+  __shared__ unsigned boundary_bits;
+  // This CTA scans tokens 32 * blockIdx.x .. + 31 (one coalesced load of
+  // their positions and state slots) and pools every one that completes a
+  // block; a 32-token run holds at most one boundary per request.
+  const int64_t tbase = static_cast<int64_t>(blockIdx.x) * 32;
+  if (threadIdx.x < 32) {
+    const int64_t tt = tbase + threadIdx.x;
+    bool b = false;
+    if (tt < num_tokens) {
+      const int64_t ss = state_slot[tt], pp = positions[tt];
+      b = ss >= 0 && (pp + 1) % ratio == 0;
+    }
+    const unsigned bits = __ballot_sync(0xffffffffu, b);
+    if (threadIdx.x == 0) boundary_bits = bits;
+  }
+  __syncthreads();
+  unsigned todo = boundary_bits;
+  while (todo) {
+    const int64_t t = tbase + (__ffs(todo) - 1);
+    todo &= todo - 1;
+    compress_token<D>(t, state, s_blk, s_tok, state_width, t2r, positions, kv_slot, bt, bt_stride, block_size,
+                      norm_w, eps, cos_sin, cs_stride, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red,
+                      row_off, &part[0][0][0]);
+    __syncthreads();  // the shared buffers are reused by the next boundary
+  }
 }
 
 }  // namespace
@@ -476,9 +539,9 @@ extern "C" int hca_compress_norm_rope_store(
   if (num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(state && token_to_req && positions && state_slot_mapping && block_table &&
                 norm_weight && cos_sin && kv_cache && kv_slot_mapping);
-  return launch_pdl(head_dim == 128 ? compress_kernel<128> : compress_kernel<512>, dim3(num_tokens),
+  return launch_pdl(head_dim == 128 ? compress_kernel<128> : compress_kernel<512>, dim3((num_tokens + 31) / 32),
                     dim3(kCompressThreads), 0, as_stream(stream), state, state_stride_block, state_stride_tok,
                     state_width, token_to_req, positions, state_slot_mapping, block_table, bt_stride, block_size,
                     norm_weight, eps, cos_sin, cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size,
-                    kv_page_stride_bytes, rope_dim, compress_ratio);
+                    kv_page_stride_bytes, rope_dim, compress_ratio, static_cast<int64_t>(num_tokens));
 }

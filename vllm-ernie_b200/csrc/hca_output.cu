@@ -261,6 +261,156 @@ __global__ void __launch_bounds__(256) vha_mma_kernel(uint8_t* out_fp8, int32_t*
   }
 }
 
+// ----------------------------------------------------------------------------
+// Multi-token VHA mix: a CTA of 8 warps handles `tpc` consecutive tokens with
+// the mix loaded once.  Warp w: heads 16 (w % 4) .. +15, dims 64 (w / 4) ..
+// +63 of each 128-dim chunk.  The O chunk and the cos / sin row of the next
+// (token, chunk) stream in by cp.async (double buffer) while the current one
+// is mixed, rotated back, and quantised per (head, 128 dims) -- the amax of
+// the two dim halves meets in shared memory -- (MODE 0) or stored bf16 (MODE 2).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16,
+                                                         int64_t ob_st, int64_t ob_sh, const __nv_bfloat16* o,
+                                                         int64_t o_st, int64_t o_sh, const __nv_bfloat16* mix,
+                                                         const int64_t* positions, const float* cos_sin,
+                                                         int64_t cs_stride, int num_tokens, int aligned_t,
+                                                         int num_heads, int n_groups, int rope_dim, int tpc) {
+  pdl_wait_and_release();
+  constexpr int kCk = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = kCk + 8, kChunks = D / kCk;
+  __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
+  __shared__ __align__(16) __nv_bfloat16 o_s[2][kMaxH * kOStride];
+  __shared__ __align__(16) float cs_s[2][64];
+  __shared__ float amax_s[2][kMaxH];
+  const int H = num_heads, hpg = H / n_groups, nope = D - rope_dim;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ht = warp & 3, dh = warp >> 2, gq = lane >> 2, cq = lane & 3;
+  const int h0 = ht * 16 + gq, h1 = h0 + 8;
+  const bool active = ht * 16 < H;
+  const int t_begin = blockIdx.x * tpc;
+  const int t_end = min(t_begin + tpc, num_tokens);
+  if (MODE == 0)
+    for (int t = max(t_begin, num_tokens); t < min(t_begin + tpc, aligned_t); ++t)
+      for (int h = threadIdx.x; h < H; h += blockDim.x) scale[static_cast<int64_t>(h) * aligned_t + t] = 0;
+  const int items = max(0, t_end - t_begin) * kChunks;
+  if (items == 0) return;
+  for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
+    const int r = i / (H / 8), c8 = i % (H / 8);
+    cp16(&mix_s[r * kMixStride + c8 * 8], mix + static_cast<int64_t>(r) * H + c8 * 8);
+  }
+  // O chunk + cos / sin row of item k into buffer k & 1
+  auto prefetch = [&](int k) {
+    const int t = t_begin + k / kChunks, ck = k % kChunks;
+    const int b = k & 1;
+    for (int i = threadIdx.x; i < H * (kCk / 8); i += blockDim.x) {
+      const int r = i / (kCk / 8), c8 = i % (kCk / 8);
+      cp16(&o_s[b][r * kOStride + c8 * 8], o + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(r) * o_sh + ck * kCk + c8 * 8);
+    }
+    // cos / sin rows alternate by token (a token's chunks all read its row)
+    if (ck == 0 && threadIdx.x < rope_dim / 4)
+      cp16(&cs_s[(t - t_begin) & 1][threadIdx.x * 4], cos_sin + positions[t] * cs_stride + threadIdx.x * 4);
+  };
+  prefetch(0);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  uint32_t packed0 = 0, packed1 = 0;
+  for (int k = 0; k < items; ++k) {
+    const int t = t_begin + k / kChunks, ck = k % kChunks, b = k & 1;
+    if (k + 1 < items) prefetch(k + 1);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    __syncthreads();
+    float acc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    if (active) {
+      for (int kk = 0; kk < H / 16; ++kk) {
+        uint32_t a[4];
+        ldsm_x4(a, &mix_s[(ht * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8], false);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          uint32_t bq[4];
+          ldsm_x4(bq, &o_s[b][(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kOStride + dh * 64 + j * 8 + (lane >> 4) * 8],
+                  true);
+          mma16816_o(acc[j], a, bq);
+          mma16816_o(acc[j + 1], a, bq + 2);
+        }
+      }
+      const float* cs = cs_s[(t - t_begin) & 1];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = ck * kCk + dh * 64 + j * 8 + 2 * cq;
+        if (d >= nope) {
+          const int pr = (d - nope) >> 1;
+          const float c = cs[pr], sn = cs[rope_dim / 2 + pr];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float e = acc[j][2 * hh], od = acc[j][2 * hh + 1];
+            acc[j][2 * hh] = e * c + od * sn;
+            acc[j][2 * hh + 1] = od * c - e * sn;
+          }
+        }
+      }
+    }
+    if (MODE == 2) {
+      if (active) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int d = ck * kCk + dh * 64 + j * 8 + 2 * cq;
+          *reinterpret_cast<__nv_bfloat162*>(out_bf16 + t * ob_st + h0 * ob_sh + d) = __floats2bfloat162_rn(acc[j][0], acc[j][1]);
+          *reinterpret_cast<__nv_bfloat162*>(out_bf16 + t * ob_st + h1 * ob_sh + d) = __floats2bfloat162_rn(acc[j][2], acc[j][3]);
+        }
+      }
+      __syncthreads();  // buffer b is refilled two items on
+      continue;
+    }
+    float am0 = 0.0f, am1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      am0 = fmaxf(am0, fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])));
+      am1 = fmaxf(am1, fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])));
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
+    }
+    if (active && cq == 0) {
+      amax_s[dh][h0] = am0;
+      amax_s[dh][h1] = am1;
+    }
+    __syncthreads();
+    if (active) {
+      const float a0 = fmaxf(amax_s[0][h0], amax_s[1][h0]), a1 = fmaxf(amax_s[0][h1], amax_s[1][h1]);
+      const int e0 = ue8m0_exponent(a0, 1e-10f, false), e1 = ue8m0_exponent(a1, 1e-10f, false);
+      const float i0 = exp2i(-e0), i1 = exp2i(-e1);
+      uint8_t* r0 = out_fp8 + (static_cast<int64_t>(h0 / hpg) * num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
+      uint8_t* r1 = out_fp8 + (static_cast<int64_t>(h1 / hpg) * num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = ck * kCk + dh * 64 + j * 8 + 2 * cq;
+        *reinterpret_cast<uint16_t*>(r0 + d) =
+            static_cast<uint16_t>(to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8));
+        *reinterpret_cast<uint16_t*>(r1 + d) =
+            static_cast<uint16_t>(to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8));
+      }
+      if (ck == 0) packed0 = packed1 = 0;
+      packed0 |= static_cast<uint32_t>(encode_ue8m0(e0)) << (8 * ck);
+      packed1 |= static_cast<uint32_t>(encode_ue8m0(e1)) << (8 * ck);
+      if (ck == kChunks - 1 && dh == 0 && cq == 0) {
+        scale[(static_cast<int64_t>(h0 / hpg) * hpg + h0 % hpg) * aligned_t + t] = static_cast<int32_t>(packed0);
+        scale[(static_cast<int64_t>(h1 / hpg) * hpg + h1 % hpg) * aligned_t + t] = static_cast<int32_t>(packed1);
+      }
+    }
+    __syncthreads();  // amax_s and buffer b are reused
+  }
+}
+
 // x * sigmoid(gate) -> 1x128 FP8; one CTA of 128 threads per (512-col pack, row).
 __global__ void __launch_bounds__(128) sigmoid_mul_quant_kernel(
     uint8_t* out, int32_t* scale, const __nv_bfloat16* x, int64_t x_stride,
@@ -306,12 +456,15 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
   if (MODE != 1 && mp != nullptr) {
     // head mix on the tensor cores: H % 16 == 0, H <= 64, 16-byte aligned rows
     if (num_heads % 16 || num_heads > 64 || o_sh % 8 || o_st % 8 || reinterpret_cast<uintptr_t>(o) % 16 ||
-        reinterpret_cast<uintptr_t>(mix) % 16)
+        reinterpret_cast<uintptr_t>(mix) % 16 || reinterpret_cast<uintptr_t>(cos_sin) % 16 || cs_stride % 4 ||
+        rope_dim > 64)
       return HCA_E_UNSUPPORTED;
-    const int threads = (num_heads / 16) * 32;
-    return launch_pdl(head_dim == 128 ? vha_mma_kernel<128, MODE> : vha_mma_kernel<512, MODE>, dim3(aligned),
-                      dim3(threads), 0, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
-                      cos_sin, cs_stride, num_tokens, aligned, num_heads, n_groups, rope_dim);
+    // tokens per CTA: the mix is loaded once per CTA; keep >= 2 CTAs per SM busy
+    const int tpc = max(1, min(16, aligned / (2 * 148 * 2)));
+    const int ctas = (aligned + tpc - 1) / tpc;
+    return launch_pdl(head_dim == 128 ? vha_tok_kernel<128, MODE> : vha_tok_kernel<512, MODE>, dim3(ctas),
+                      dim3(256), 0, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
+                      cos_sin, cs_stride, num_tokens, aligned, num_heads, n_groups, rope_dim, tpc);
   }
   if (head_dim == 128)
     vha_out_kernel<128, MODE><<<aligned, 256, 0, s>>>(out_fp8, scale, out_bf16, ob_st, ob_sh, op,
