@@ -1509,14 +1509,15 @@ __global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const Att
   const float i0 = exp2i(-e0), i1 = exp2i(-e1);
   uint8_t* r0 = V.out + (static_cast<int64_t>(h0 / hpg) * V.num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
   uint8_t* r1 = V.out + (static_cast<int64_t>(h1 / hpg) * V.num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+  uint32_t p0[8], p1[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int d = dh * 64 + j * 8 + 2 * cq;
-    *reinterpret_cast<uint16_t*>(r0 + d) =
-        static_cast<uint16_t>(to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8));
-    *reinterpret_cast<uint16_t*>(r1 + d) =
-        static_cast<uint16_t>(to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8));
+    p0[j] = to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8);
+    p1[j] = to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8);
   }
+  // 16 contiguous bytes per lane: one full-sector store instead of eight 2-byte ones
+  *reinterpret_cast<uint4*>(r0 + dh * 64 + 16 * cq) = quad_gather_fp8(p0, cq);
+  *reinterpret_cast<uint4*>(r1 + dh * 64 + 16 * cq) = quad_gather_fp8(p1, cq);
   if (dh == 0 && cq == 0) {
     V.scale[static_cast<int64_t>(h0) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e0));
     V.scale[static_cast<int64_t>(h1) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e1));
@@ -1748,7 +1749,8 @@ extern "C" int hca_sparse_decode_vha_fp8_quant(
   if (head_dim != 128 || rope_dim != 64 || num_heads % 16 || num_heads > 64) return HCA_E_UNSUPPORTED;
   if (num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(out && scale && schedule && mix && positions && cos_sin && workspace);
-  HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(mix) % 16 == 0 && reinterpret_cast<uintptr_t>(workspace) % 16 == 0);
+  HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(mix) % 16 == 0 && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(out) % 16 == 0);
   // the attention launch writes only split partials here; `out` of the
   // attention stage is unused, so the (aligned) workspace stands in for it
   AttnParams P{};

@@ -139,38 +139,68 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
                                             const int64_t* positions, const float* cos_sin,
                                             int64_t cs_stride, int rope_dim, float eps) {
   pdl_wait_and_release();
-  const int lane = threadIdx.x & 31;
+  constexpr int E = WarpRow<D>::E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int64_t t = blockIdx.x;
-  const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
-  if (h > padded_heads) return;
-  WarpRow<D> row;
   const float* cs = cos_sin + positions[t] * cs_stride;
-  if (h < num_heads) {
-    row.load_bf16(q + t * q_st + h * q_sh, lane);
-    float ss = 0.0f;
+  // this lane's RoPE pairs (dims lane * E + 2i, + 1): cos / sin once per warp
+  const int nope = D - rope_dim;
+  float pc[E / 2], ps[E / 2];
 #pragma unroll
-    for (int i = 0; i < WarpRow<D>::E; ++i) ss += row.v[i] * row.v[i];
-    ss = warp_sum(ss);
-    const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+  for (int i = 0; i < E / 2; ++i) {
+    const int d = lane * E + 2 * i;
+    pc[i] = 1.0f;
+    ps[i] = 0.0f;
+    if (d >= nope) {
+      pc[i] = cs[(d - nope) >> 1];
+      ps[i] = cs[rope_dim / 2 + ((d - nope) >> 1)];
+    }
+  }
+  auto rope = [&](WarpRow<D>& r) {
 #pragma unroll
-    for (int i = 0; i < WarpRow<D>::E; ++i) row.v[i] *= rrms;
-    row.rope(cs, rope_dim, lane, false);
-    row.store_bf16(q_out + t * qo_st + h * qo_sh, lane);
-  } else if (h < padded_heads) {
-    uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * WarpRow<D>::E;
+    for (int i = 0; i < E / 2; ++i) rope_pair(r.v[2 * i], r.v[2 * i + 1], pc[i], ps[i]);
+  };
+  // One CTA per token.  Warp w owns query heads w, w + nwarps, ...; their rows
+  // are loaded kBatch at a time before any is used (more bytes in flight).
+  constexpr int kBatch = 4;
+  for (int hb = warp; hb < padded_heads; hb += nwarps * kBatch) {
+    WarpRow<D> rows[kBatch];
 #pragma unroll
-    for (int i = 0; i < WarpRow<D>::E; ++i) o[i] = 0;
-  } else {
+    for (int b = 0; b < kBatch; ++b) {
+      const int h = hb + b * nwarps;
+      if (h < num_heads) rows[b].load_bf16(q + t * q_st + h * q_sh, lane);
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int h = hb + b * nwarps;
+      if (h < num_heads) {
+        WarpRow<D>& row = rows[b];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) ss += row.v[i] * row.v[i];
+        ss = warp_sum(ss);
+        const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+        for (int i = 0; i < E; ++i) row.v[i] *= rrms;
+        rope(row);
+        row.store_bf16(q_out + t * qo_st + h * qo_sh, lane);
+      } else if (h < padded_heads) {
+        uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * E;
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = 0;
+      }
+    }
+  }
+  // the KV row: RoPE, fp8 NoPE quant, insert (the last warp)
+  if (warp == nwarps - 1) {
     const int64_t slot = slot_mapping[t];
     if (slot < 0) return;
+    WarpRow<D> row;
     row.load_bf16(kv + t * kv_stride, lane);
-    float roped[WarpRow<D>::E];
     WarpRow<D> r2 = row;
-    r2.rope(cs, rope_dim, lane, false);
-#pragma unroll
-    for (int i = 0; i < WarpRow<D>::E; ++i) roped[i] = r2.v[i];
+    rope(r2);
     const RowGeom g = row_geom(D, rope_dim);
-    row.store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, roped);
+    row.store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, r2.v);
   }
 }
 
@@ -456,12 +486,11 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
   if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
   if (num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(q_out && q && kv && swa_cache && slot_mapping && positions && cos_sin);
-  dim3 grid(num_tokens, (padded_heads + 1 + 3) / 4);
   auto* qo = static_cast<__nv_bfloat16*>(q_out);
   auto* qi = static_cast<const __nv_bfloat16*>(q);
   auto* ki = static_cast<const __nv_bfloat16*>(kv);
-  return launch_pdl(head_dim == 128 ? qnorm_rope_kv_insert_kernel<128> : qnorm_rope_kv_insert_kernel<512>, grid,
-                    dim3(128), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
+  return launch_pdl(head_dim == 128 ? qnorm_rope_kv_insert_kernel<128> : qnorm_rope_kv_insert_kernel<512>,
+                    dim3(num_tokens), dim3(512), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
                     q_stride_tok, q_stride_head, num_heads, ki, kv_stride, swa_cache, page_size,
                     page_stride_bytes, slot_mapping, positions, cos_sin, cos_sin_stride, rope_dim, eps);
 }

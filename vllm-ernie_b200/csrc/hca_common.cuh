@@ -23,6 +23,33 @@ constexpr int kQuantBlock = 64;  // NoPE quantisation block of the cached rows
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Quad transpose of e4m3 byte pairs from an m16n8 accumulator row: lane cq
+// (0..3) of a 4-lane quad holds the pair for columns 8 j + 2 cq, + 1 of
+// j = 0..7 (pair[j], low 16 bits).  Returns this lane's 16 contiguous bytes,
+// columns 16 cq .. 16 cq + 15 of the quad's 64-column segment, so the row
+// is written with one 16-byte store per lane instead of eight 2-byte ones.
+__device__ __forceinline__ uint4 quad_gather_fp8(const uint32_t pair[8], int cq) {
+  // w[k]: this lane's pairs for the 16 bytes that lane k of the quad stores
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) w[k] = (pair[2 * k] & 0xffffu) | (pair[2 * k + 1] << 16);
+  auto sel = [](const uint32_t* a, int i) { return i == 0 ? a[0] : i == 1 ? a[1] : i == 2 ? a[2] : a[3]; };
+  // round r: send the word for lane cq ^ r, receive lane (cq ^ r)'s word for us
+  uint32_t rec[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) rec[r] = r == 0 ? sel(w, cq) : __shfl_xor_sync(0xffffffffu, sel(w, cq ^ r), r);
+  // got[s] = the word from quad lane s = rec[s ^ cq]
+  uint32_t got[4];
+#pragma unroll
+  for (int s2 = 0; s2 < 4; ++s2) got[s2] = sel(rec, s2 ^ cq);
+  uint4 o;
+  o.x = __byte_perm(got[0], got[1], 0x5410);
+  o.y = __byte_perm(got[2], got[3], 0x5410);
+  o.z = __byte_perm(got[0], got[1], 0x7632);
+  o.w = __byte_perm(got[2], got[3], 0x7632);
+  return o;
+}
+
 // Programmatic dependent launch for the per-layer chain of kernels.  A kernel
 // launched with launch_pdl may be scheduled while the kernel before it on the
 // stream is still running; it first waits (griddepcontrol.wait) until that

@@ -275,6 +275,9 @@ __device__ __forceinline__ void cp16(void* dst, const void* src) {
                : "memory");
 }
 
+constexpr int kVhaStages = 4;
+constexpr int kVhaDynSmem = kVhaStages * 64 * (128 + 8) * 2;
+
 template <int D, int MODE>
 __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16,
                                                          int64_t ob_st, int64_t ob_sh, const __nv_bfloat16* o,
@@ -285,8 +288,10 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
   pdl_wait_and_release();
   constexpr int kCk = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = kCk + 8, kChunks = D / kCk;
   __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
-  __shared__ __align__(16) __nv_bfloat16 o_s[2][kMaxH * kOStride];
-  __shared__ __align__(16) float cs_s[2][64];
+  constexpr int kStages = kVhaStages;  // O chunks in flight: the next three stream in while one is mixed
+  extern __shared__ __align__(16) uint8_t vha_dyn[];
+  auto o_s = reinterpret_cast<__nv_bfloat16(*)[kMaxH * kOStride]>(vha_dyn);  // [kStages][...]
+  __shared__ __align__(16) float cs_s[kStages][64];
   __shared__ float amax_s[2][kMaxH];
   const int H = num_heads, hpg = H / n_groups, nope = D - rope_dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -304,26 +309,30 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
     const int r = i / (H / 8), c8 = i % (H / 8);
     cp16(&mix_s[r * kMixStride + c8 * 8], mix + static_cast<int64_t>(r) * H + c8 * 8);
   }
-  // O chunk + cos / sin row of item k into buffer k & 1
+  // O chunk + cos / sin row of item k into buffer k % kStages
   auto prefetch = [&](int k) {
     const int t = t_begin + k / kChunks, ck = k % kChunks;
-    const int b = k & 1;
+    const int b = k % kStages;
     for (int i = threadIdx.x; i < H * (kCk / 8); i += blockDim.x) {
       const int r = i / (kCk / 8), c8 = i % (kCk / 8);
       cp16(&o_s[b][r * kOStride + c8 * 8], o + static_cast<int64_t>(t) * o_st + static_cast<int64_t>(r) * o_sh + ck * kCk + c8 * 8);
     }
-    // cos / sin rows alternate by token (a token's chunks all read its row)
+    // cos / sin rows rotate by token (a token's chunks all read its row;
+    // at most kStages - 1 items, so fewer tokens, are ahead of the current one)
     if (ck == 0 && threadIdx.x < rope_dim / 4)
-      cp16(&cs_s[(t - t_begin) & 1][threadIdx.x * 4], cos_sin + positions[t] * cs_stride + threadIdx.x * 4);
+      cp16(&cs_s[(t - t_begin) % kStages][threadIdx.x * 4], cos_sin + positions[t] * cs_stride + threadIdx.x * 4);
   };
-  prefetch(0);
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
+#pragma unroll
+  for (int k = 0; k < kStages - 1; ++k) {
+    if (k < items) prefetch(k);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
   uint32_t packed0 = 0, packed1 = 0;
   for (int k = 0; k < items; ++k) {
-    const int t = t_begin + k / kChunks, ck = k % kChunks, b = k & 1;
-    if (k + 1 < items) prefetch(k + 1);
+    const int t = t_begin + k / kChunks, ck = k % kChunks, b = k % kStages;
+    if (k + kStages - 1 < items) prefetch(k + kStages - 1);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
-    asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kStages - 1) : "memory");
     __syncthreads();
     float acc[8][4];
 #pragma unroll
@@ -341,7 +350,7 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
           mma16816_o(acc[j + 1], a, bq + 2);
         }
       }
-      const float* cs = cs_s[(t - t_begin) & 1];
+      const float* cs = cs_s[(t - t_begin) % kStages];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int d = ck * kCk + dh * 64 + j * 8 + 2 * cq;
@@ -366,7 +375,7 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
           *reinterpret_cast<__nv_bfloat162*>(out_bf16 + t * ob_st + h1 * ob_sh + d) = __floats2bfloat162_rn(acc[j][2], acc[j][3]);
         }
       }
-      __syncthreads();  // buffer b is refilled two items on
+      __syncthreads();  // buffer b is refilled kStages items on
       continue;
     }
     float am0 = 0.0f, am1 = 0.0f;
@@ -391,14 +400,16 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
       const float i0 = exp2i(-e0), i1 = exp2i(-e1);
       uint8_t* r0 = out_fp8 + (static_cast<int64_t>(h0 / hpg) * num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
       uint8_t* r1 = out_fp8 + (static_cast<int64_t>(h1 / hpg) * num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+      uint32_t p0[8], p1[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int d = ck * kCk + dh * 64 + j * 8 + 2 * cq;
-        *reinterpret_cast<uint16_t*>(r0 + d) =
-            static_cast<uint16_t>(to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8));
-        *reinterpret_cast<uint16_t*>(r1 + d) =
-            static_cast<uint16_t>(to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8));
+        p0[j] = to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8);
+        p1[j] = to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8);
       }
+      // 16 contiguous bytes per lane: one full-sector store instead of eight 2-byte ones
+      const int dseg = ck * kCk + dh * 64 + 16 * cq;
+      *reinterpret_cast<uint4*>(r0 + dseg) = quad_gather_fp8(p0, cq);
+      *reinterpret_cast<uint4*>(r1 + dseg) = quad_gather_fp8(p1, cq);
       if (ck == 0) packed0 = packed1 = 0;
       packed0 |= static_cast<uint32_t>(encode_ue8m0(e0)) << (8 * ck);
       packed1 |= static_cast<uint32_t>(encode_ue8m0(e1)) << (8 * ck);
@@ -457,13 +468,19 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
     // head mix on the tensor cores: H % 16 == 0, H <= 64, 16-byte aligned rows
     if (num_heads % 16 || num_heads > 64 || o_sh % 8 || o_st % 8 || reinterpret_cast<uintptr_t>(o) % 16 ||
         reinterpret_cast<uintptr_t>(mix) % 16 || reinterpret_cast<uintptr_t>(cos_sin) % 16 || cs_stride % 4 ||
-        rope_dim > 64)
+        rope_dim > 64 || reinterpret_cast<uintptr_t>(out_fp8) % 16)
       return HCA_E_UNSUPPORTED;
     // tokens per CTA: the mix is loaded once per CTA; keep >= 2 CTAs per SM busy
     const int tpc = max(1, min(16, aligned / (2 * 148 * 2)));
     const int ctas = (aligned + tpc - 1) / tpc;
-    return launch_pdl(head_dim == 128 ? vha_tok_kernel<128, MODE> : vha_tok_kernel<512, MODE>, dim3(ctas),
-                      dim3(256), 0, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
+    auto* kfn = head_dim == 128 ? vha_tok_kernel<128, MODE> : vha_tok_kernel<512, MODE>;
+    static bool smem_set[2] = {false, false};  // per head dim (same value every time)
+    if (!smem_set[head_dim == 128]) {
+      if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVhaDynSmem) != cudaSuccess)
+        return HCA_E_CUDA;
+      smem_set[head_dim == 128] = true;
+    }
+    return launch_pdl(kfn, dim3(ctas), dim3(256), kVhaDynSmem, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
                       cos_sin, cs_stride, num_tokens, aligned, num_heads, n_groups, rope_dim, tpc);
   }
   if (head_dim == 128)
