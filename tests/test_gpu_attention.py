@@ -32,14 +32,14 @@ def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_R
     assert rel <= max_rel, (err.max(), rel)
 
 
-def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148):
-    """``splits=None``: the balanced work list for ``sm_count`` CTAs."""
+def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148, maxc=1024):
+    """``splits=None``: the balanced work list for ``sm_count`` CTAs; ``maxc``:
+    compressed-index width (context up to maxc * 128)."""
     from vllm_ernie_b200 import ops
     from vllm_ernie_b200.decode import build_decode_metadata
     from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
 
     dims = HCADims(heads=heads)
-    maxc = 1024
     b = make_decode_batch(ctx, q_per_seq, dims, DEV, seed=seed, max_model_len=maxc * 128)
     caches = alloc_layer_caches(b, seed=seed + 1)
     md = build_decode_metadata(b, maxc, num_splits=splits, sm_count=sm_count)
@@ -322,3 +322,12 @@ def test_decode_few_heads(heads, splits):
     """Tiles with fewer than 16 query rows (some TMEM lane quadrants empty),
     e.g. 8 heads per GPU under TP=8."""
     _decode_case([5, 300, 9000, 70000], 3, heads, splits, seed=23 + heads)
+
+
+@pytest.mark.parametrize("splits", [None, 16])
+def test_decode_million_token_context(splits):
+    """Config 4 geometry: ~1M-token contexts, 8192 compressed entries plus the
+    window per sequence, 3 queries per sequence; the split-K merge spans up to
+    16 CTAs per request."""
+    ctx = [1048573, 1048000, 900001, 1048575 - 128 * 5]
+    _decode_case(ctx, 3, 64, splits, seed=51, maxc=8320)
