@@ -161,6 +161,9 @@ def max_over_ranks(x: float, ws: int) -> float:
 # ---------------------------------------------------------------------------
 
 
+_CPU_FIXTURES: dict = {}
+
+
 def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
     """Oracle (CPU restatement of the reference path) on a bounded sample of
     the config-2 workload: whole requests (3 query tokens each) through one
@@ -173,34 +176,51 @@ def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rng = np.random.default_rng(7)
     ctx = contexts(0)
     heads, d, r = 64, 128, 64
     cos_sin = C.rope_cos_sin_cache(CTX_HI + 8, r, 160000.0)
-    done_tokens, t_total, reqs = 0, 0.0, 0
-    for it in range(100 * len(ctx)):
-        b = it % len(ctx)
+
+    def fixture(b: int):
+        """Request b's inputs and compact caches (built once, reused): SWA
+        pages only for the window, compressor-state pages only for the 128
+        positions a block boundary pools, every compressed entry."""
+        if b in _CPU_FIXTURES:
+            return _CPU_FIXTURES[b]
+        rng = np.random.default_rng(7 + b)
         L = int(ctx[b])
         end = L + Q_PER_SEQ
         ncomp = end // 128 + 1
-        sw_lo = max(L - 127, 0)
-        # this request's caches: contiguous pages
-        swa_pages = (end + 63) // 64
-        swa = np.zeros((swa_pages, C.page_bytes(64, d, r)), np.uint8)
-        live = np.arange(sw_lo, end)
-        C.insert_rows(swa, live, rng.standard_normal((len(live), d)).astype(np.float32), 64, d, r)
+
+        def compact_pages(lo: int, page: int):
+            first, last = lo // page, (end - 1) // page
+            bt = np.zeros((1, (end + page - 1) // page), np.int32)
+            bt[0, first:last + 1] = np.arange(last - first + 1)
+            return bt, last - first + 1
+
+        swa_bt, n_swa = compact_pages(max(L - 127, 0), 64)
+        swa = np.zeros((n_swa, C.page_bytes(64, d, r)), np.uint8)
+        live = np.arange(max(L - 127, 0), L)
+        live_slots = swa_bt[0, live // 64] * 64 + live % 64
+        C.insert_rows(swa, live_slots, rng.standard_normal((len(live), d)).astype(np.float32), 64, d, r)
         comp = np.zeros(((ncomp + 1) // 2 + 1, C.page_bytes(2, d, r)), np.uint8)
         C.insert_rows(comp, np.arange(ncomp), rng.standard_normal((ncomp, d)).astype(np.float32), 2, d, r)
-        state = rng.standard_normal(((end + 7) // 8, 8, 2 * d)).astype(np.float32)
+        comp_bt = np.arange(comp.shape[0], dtype=np.int32)[None]
+        st_bt, n_st = compact_pages(max(L - 128, 0), 8)
+        state = rng.standard_normal((n_st, 8, 2 * d)).astype(np.float32)
         q = rng.standard_normal((Q_PER_SEQ, heads, d)).astype(np.float32)
         kv = rng.standard_normal((Q_PER_SEQ, d)).astype(np.float32)
         ks = rng.standard_normal((Q_PER_SEQ, 2 * d)).astype(np.float32)
+        _CPU_FIXTURES[b] = (L, end, swa, swa_bt, comp, comp_bt, state, st_bt, q, kv, ks)
+        return _CPU_FIXTURES[b]
+
+    done_tokens, t_total, reqs = 0, 0.0, 0
+    wall0 = time.perf_counter()
+    for it in range(100 * len(ctx)):
+        b = it % len(ctx)
+        L, end, swa, swa_bt, comp, comp_bt, state, st_bt, q, kv, ks = fixture(b)
         pos = np.arange(L, end)
         qsl = np.array([0, Q_PER_SEQ], np.int32)
         sl = np.array([end], np.int32)
-        swa_bt = np.arange(swa_pages, dtype=np.int32)[None]
-        comp_bt = np.arange(comp.shape[0], dtype=np.int32)[None]
-        st_bt = np.arange(state.shape[0], dtype=np.int32)[None]
         t0 = time.perf_counter()
         qp = O.q_prep(q, pos, cos_sin, r, 1e-6)
         swa_slot = M.slot_mapping(qsl, sl, swa_bt, 64)
@@ -224,7 +244,8 @@ def cpu_sample_tokens_per_s(seconds_budget: float = 15.0) -> dict:
         t_total += time.perf_counter() - t0
         done_tokens += Q_PER_SEQ
         reqs += 1
-        if t_total > seconds_budget:
+        # bounded in CPU time of the timed ops and in wall time (fixture builds)
+        if t_total > seconds_budget or time.perf_counter() - wall0 > 3 * seconds_budget + 30:
             break
     per_layer_tok_s = done_tokens / t_total
     return {"value": per_layer_tok_s / LAYERS, "unit": UNIT, "cores": threads, "kind": "port",
