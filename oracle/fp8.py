@@ -72,8 +72,10 @@ def bf16_bytes(x: np.ndarray) -> np.ndarray:
 
 def bf16_from_bytes(b: np.ndarray) -> np.ndarray:
     """bf16 raw bytes ``[..., 2 * n]`` to fp32 ``[..., n]``."""
-    t = torch.from_numpy(np.ascontiguousarray(b, dtype=np.uint8))
-    return t.view(torch.bfloat16).to(torch.float32).numpy()
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    if b.size == 0:
+        return np.zeros(b.shape[:-1] + (b.shape[-1] // 2,), np.float32)
+    return torch.from_numpy(b).view(torch.bfloat16).to(torch.float32).numpy()
 
 
 def quantize_blocks(x: np.ndarray, block: int, floor: float, divide: bool):

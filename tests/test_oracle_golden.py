@@ -150,3 +150,22 @@ def test_sigmoid_mul_quant_matches_plugin_kernel(name):
     q, s = O.sigmoid_mul_quant_fp8(g["x"], g["gate"])
     assert np.array_equal(s, g["scale"])
     assert np.array_equal(q, g["fp8"])
+
+
+def test_layer_oracle_emulated_vs_exact():
+    """The whole-layer oracle (config 1, prefill 1024 + 640 from an empty
+    cache): the evaluation with the reference kernels' FP8/UE8M0 and bf16
+    roundings stays close to the all-fp32 one, and both are finite."""
+    import torch
+
+    from oracle.layer import HCALayerOracle, HCAShape, random_weights
+
+    shape = HCAShape()
+    w = random_weights(shape, seed=0)
+    g = torch.Generator().manual_seed(1)
+    h = torch.randn(1664, 2048, generator=g).to(torch.bfloat16).float().numpy()
+    qsl, sl = np.array([0, 1024, 1664]), np.array([1024, 640])
+    em = HCALayerOracle(shape, w, max_len=1152, num_reqs=2, emulate_quant=True).forward(h, qsl, sl)
+    ex = HCALayerOracle(shape, w, max_len=1152, num_reqs=2, emulate_quant=False).forward(h, qsl, sl)
+    assert np.isfinite(em).all() and np.isfinite(ex).all()
+    assert np.linalg.norm(em - ex) / np.linalg.norm(ex) < 5e-2

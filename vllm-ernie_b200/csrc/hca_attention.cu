@@ -660,7 +660,13 @@ __device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
 
 template <bool kPrefill>
 __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(const AttnParams P, int* err) {
-  pdl_wait_and_release();
+  // Everything up to pdl_wait() reads only per-step metadata (schedule,
+  // group starts, lengths, index and block tables), written before any layer
+  // kernel ran, so it overlaps the kernel before this one; Q and the cache
+  // rows, which that kernel may still be writing, are read after the wait.
+  // CTAs that exit early wait first, so this launch completes only after its
+  // predecessor.
+  pdl_release();
   using namespace tcd;
   using namespace tc;
   extern __shared__ uint8_t smem_dyn[];
@@ -678,7 +684,10 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     single = true;
   } else if (P.sched) {
     const int4 it = reinterpret_cast<const int4*>(P.sched)[blockIdx.x];
-    if (it.x < 0) return;
+    if (it.x < 0) {
+      pdl_wait();
+      return;
+    }
     gidx = it.x;
     c_begin = it.z;
     c_end = it.w;
@@ -691,10 +700,13 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
   }
   if (P.force_partials) single = false;
   Group G;
-  if (!resolve_group<kPrefill>(P, gidx, G)) return;
+  if (!resolve_group<kPrefill>(P, gidx, G) || G.ntok * P.num_heads > kMaxRows ||
+      G.ntok * P.num_heads > P.max_rows) {
+    pdl_wait();
+    return;
+  }
   const int H = P.num_heads;
   const int rows_q = G.ntok * H;
-  if (rows_q > kMaxRows || rows_q > P.max_rows) return;
   const int ntiles = (rows_q + 127) / 128;
   // softmax warps with rows: quadrants 0 .. act0 - 1 of tile 0, 0 .. act1 - 1 of tile 1
   const int act0 = active_quads(0, rows_q), act1 = active_quads(1, rows_q);
@@ -754,6 +766,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
   const uint32_t tmem = misc[0];
 
   if (warp < kSoftmaxWarps || warp == kMmaWarp) {
+    pdl_wait();  // Q was written by an earlier kernel of this layer
     // Q rows -> two K-major 128B-swizzled M=128 tiles (rows past rows_q zero),
     // loaded by the softmax and MMA warps while the loader already streams KV.
     // A tile with R < 128 query rows spreads them evenly over the four TMEM
@@ -873,6 +886,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
       rq[i].slot = -1;
       if (i < n) resolve(c_begin + i, rq[i]);
     }
+    pdl_wait();  // the cache rows: the kernel before may still be inserting
 #pragma unroll
     for (int i = 0; i < kStages - 1; ++i) issue(i, rq[i]);
     Resolved rn;  // slots of the next chunk to issue

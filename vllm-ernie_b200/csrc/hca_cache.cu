@@ -160,19 +160,26 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
 #pragma unroll
     for (int i = 0; i < E / 2; ++i) rope_pair(r.v[2 * i], r.v[2 * i + 1], pc[i], ps[i]);
   };
-  // One CTA per token.  Warp w owns query heads w, w + nwarps, ...; their rows
-  // are loaded kBatch at a time before any is used (more bytes in flight).
+  // CTA (t, y) owns rows [y * rpc, (y + 1) * rpc) of token t: the query heads,
+  // the zero padding heads, and row padded_heads = the KV row.  Warp w takes
+  // rows w, w + nwarps, ...; they are loaded kBatch at a time before any is
+  // used (more bytes in flight).
+  const int nrows = padded_heads + 1;
+  const int rpc = (nrows + gridDim.y - 1) / gridDim.y;
+  const int row_lo = blockIdx.y * rpc, row_hi = min(nrows, row_lo + rpc);
   constexpr int kBatch = 4;
-  for (int hb = warp; hb < padded_heads; hb += nwarps * kBatch) {
+  for (int hb = row_lo + warp; hb < row_hi; hb += nwarps * kBatch) {
     WarpRow<D> rows[kBatch];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int h = hb + b * nwarps;
-      if (h < num_heads) rows[b].load_bf16(q + t * q_st + h * q_sh, lane);
+      if (h < row_hi && h < num_heads) rows[b].load_bf16(q + t * q_st + h * q_sh, lane);
+      else if (h < row_hi && h == padded_heads) rows[b].load_bf16(kv + t * kv_stride, lane);
     }
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int h = hb + b * nwarps;
+      if (h >= row_hi) continue;
       if (h < num_heads) {
         WarpRow<D>& row = rows[b];
         float ss = 0.0f;
@@ -188,19 +195,16 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
         uint16_t* o = reinterpret_cast<uint16_t*>(q_out + t * qo_st + h * qo_sh) + lane * E;
 #pragma unroll
         for (int i = 0; i < E; ++i) o[i] = 0;
+      } else {
+        // the KV row: RoPE, fp8 NoPE quant, insert
+        const int64_t slot = slot_mapping[t];
+        if (slot < 0) continue;
+        WarpRow<D> r2 = rows[b];
+        rope(r2);
+        const RowGeom g = row_geom(D, rope_dim);
+        rows[b].store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, r2.v);
       }
     }
-  }
-  // the KV row: RoPE, fp8 NoPE quant, insert (the last warp)
-  if (warp == nwarps - 1) {
-    const int64_t slot = slot_mapping[t];
-    if (slot < 0) return;
-    WarpRow<D> row;
-    row.load_bf16(kv + t * kv_stride, lane);
-    WarpRow<D> r2 = row;
-    rope(r2);
-    const RowGeom g = row_geom(D, rope_dim);
-    row.store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, r2.v);
   }
 }
 
@@ -489,8 +493,12 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
   auto* qo = static_cast<__nv_bfloat16*>(q_out);
   auto* qi = static_cast<const __nv_bfloat16*>(q);
   auto* ki = static_cast<const __nv_bfloat16*>(kv);
+  // few tokens (decode): CTAs of 4 warps over 4 rows each (many small CTAs
+  // spread over the SMs); many tokens (prefill): one 16-warp CTA per token
+  const bool few = num_tokens < 4096;
+  const int ysplit = few ? (padded_heads + 1 + 3) / 4 : 1;
   return launch_pdl(head_dim == 128 ? qnorm_rope_kv_insert_kernel<128> : qnorm_rope_kv_insert_kernel<512>,
-                    dim3(num_tokens), dim3(512), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
+                    dim3(num_tokens, ysplit), dim3(few ? 128 : 512), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
                     q_stride_tok, q_stride_head, num_heads, ki, kv_stride, swa_cache, page_size,
                     page_stride_bytes, slot_mapping, positions, cos_sin, cos_sin_stride, rope_dim, eps);
 }

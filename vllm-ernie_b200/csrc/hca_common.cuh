@@ -59,9 +59,11 @@ __device__ __forceinline__ uint4 quad_gather_fp8(const uint32_t pair[8], int cq)
 // successor only launches once every CTA of this kernel has started, so its
 // waiting CTAs never hold resources this kernel still needs.  Without a
 // programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_and_release() {
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  pdl_wait();
+  pdl_release();
 }
 
 template <typename... KArgs, typename... Args>
