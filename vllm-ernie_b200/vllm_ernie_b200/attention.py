@@ -30,7 +30,7 @@ import torch.distributed as dist
 from torch import nn
 
 from . import ops
-from .backend import HCACacheSpec, hca_kv_cache_specs
+from .backend import HCACacheSpec, _sm_count, hca_kv_cache_specs
 from .cache_layout import SWA_BLOCK_SIZE, STATE_BLOCK_SIZE, compressed_page_size
 from .forward_context import get_forward_context
 
@@ -277,11 +277,17 @@ class Ernie5_5HCAAttention(nn.Module):
         ndt, nd = swa.num_decode_tokens, swa.num_decodes
         sink = self.attn_sink[: self.n_local_heads].contiguous()
         if ndt:
+            if c128.decode_schedule is None:
+                # the step's balanced work list: one wave of CTAs over the SMs
+                groups = swa.decode_group_starts.numel() - 1
+                c128.decode_items = max(_sm_count(qp.device), groups)
+                c128.decode_schedule = ops.decode_schedule(swa.decode_group_starts, ndt, swa.decode_swa_lens,
+                                                           c128.c128a_decode_topk_lens, c128.decode_items)
             ops.sparse_decode(qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,
                               self.kv_cache, self.comp_page, c128.c128a_global_decode_topk_indices,
                               c128.c128a_decode_topk_lens, self.scale, sink, out=o[:ndt],
                               group_starts=swa.decode_group_starts, max_group_tokens=swa.decode_max_group_tokens,
-                              num_splits=c128.num_splits, rope_dim=r)
+                              rope_dim=r, schedule=c128.decode_schedule, max_items=c128.decode_items)
         if swa.num_prefills:
             qsl = swa.query_start_loc[nd:] - ndt
             ops.sparse_prefill(qp[ndt:n], qsl, swa.seq_lens[nd:], self.swa_cache, SWA_BLOCK_SIZE,

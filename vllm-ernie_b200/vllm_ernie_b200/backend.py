@@ -170,6 +170,10 @@ class C128AMetadata:
     c128a_decode_topk_lens: torch.Tensor | None = None
     c128a_prefill_topk_indices: torch.Tensor | None = None
     num_splits: int = 1
+    # balanced decode work list of the step (built on first use, shared by
+    # every layer): see ops.decode_schedule
+    decode_schedule: torch.Tensor | None = None
+    decode_items: int = 0
 
 
 @dataclass
