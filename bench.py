@@ -646,7 +646,7 @@ def main():
                        "per_layer_us": ms * 1e3 / layers},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
-                         "kernel": "hca_decode_tc_kernel" + (" + hca_attention_combine_kernel" if combine else ""),
+                         "kernel": "hca_tc_attention_kernel<decode>" + (" + split merge" if combine else ""),
                          "launch_us": attn_us,
                          "algorithmic_bytes": algo},
             "cpu_baseline": cpu,
