@@ -32,14 +32,15 @@ def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_R
     assert rel <= max_rel, (err.max(), rel)
 
 
-def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148, maxc=1024):
+def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148, maxc=1024,
+                 head_dim=128):
     """``splits=None``: the balanced work list for ``sm_count`` CTAs; ``maxc``:
     compressed-index width (context up to maxc * 128)."""
     from vllm_ernie_b200 import ops
     from vllm_ernie_b200.decode import build_decode_metadata
     from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
 
-    dims = HCADims(heads=heads)
+    dims = HCADims(heads=heads, head_dim=head_dim)
     b = make_decode_batch(ctx, q_per_seq, dims, DEV, seed=seed, max_model_len=maxc * 128)
     caches = alloc_layer_caches(b, seed=seed + 1)
     md = build_decode_metadata(b, maxc, num_splits=splits, sm_count=sm_count)
@@ -64,7 +65,7 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
     assert np.array_equal(md.comp_indices.cpu().numpy(), gd)
 
     g = torch.Generator(device=DEV).manual_seed(seed + 2)
-    q = torch.randn((n, heads, 128), generator=g, device=DEV).to(torch.bfloat16)
+    q = torch.randn((n, heads, head_dim), generator=g, device=DEV).to(torch.bfloat16)
     if sink_mode == "random":
         sink = torch.randn(heads, generator=g, device=DEV)
     elif sink_mode == "neginf":
@@ -73,13 +74,13 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
         sink = None
     out = ops.sparse_decode(q, caches.swa, 64, md.swa_indices, md.swa_lens,
                             caches.comp if comp else None, 2, md.comp_indices if comp else None,
-                            md.comp_lens if comp else None, 128 ** -0.5, sink,
+                            md.comp_lens if comp else None, head_dim ** -0.5, sink,
                             group_starts=md.group_starts, max_group_tokens=md.max_group_tokens,
                             num_splits=md.num_splits, schedule=md.schedule, max_items=md.max_items)
     ref = A.sparse_decode(q.float().cpu().numpy(), caches.swa.cpu().numpy(), 64, idx, lens,
                           caches.comp.cpu().numpy() if comp else None, 2, gd if comp else None,
-                          dl if comp else None, 128 ** -0.5,
-                          sink.cpu().numpy() if sink is not None else None, 128, 64)
+                          dl if comp else None, head_dim ** -0.5,
+                          sink.cpu().numpy() if sink is not None else None, head_dim, 64)
     check_close(out.float().cpu().numpy(), ref)
     assert ops.device_error() == 0
     return out
@@ -175,7 +176,7 @@ def test_prefill_long_prior_context(heads):
     _prefill_case([(20000, 70), (128 * 40 - 3, 9), (5, 250)], heads, seed=31 + heads)
 
 
-def _prefill_case(reqs, heads, seed):
+def _prefill_case(reqs, heads, seed, head_dim=128):
     from vllm_ernie_b200 import ops
 
     q_lens = np.array([c for _, c in reqs])
@@ -199,22 +200,22 @@ def _prefill_case(reqs, heads, seed):
     from vllm_ernie_b200.cache_layout import page_bytes
 
     gen = torch.Generator(device=DEV).manual_seed(seed)
-    swa = torch.zeros((n_swa, page_bytes(64, 128, 64)), dtype=torch.uint8, device=DEV)
-    comp = torch.zeros((n_comp, page_bytes(2, 128, 64)), dtype=torch.uint8, device=DEV)
+    swa = torch.zeros((n_swa, page_bytes(64, head_dim, 64)), dtype=torch.uint8, device=DEV)
+    comp = torch.zeros((n_comp, page_bytes(2, head_dim, 64)), dtype=torch.uint8, device=DEV)
     for cache, page, npg in ((swa, 64, n_swa), (comp, 2, n_comp)):
-        rows = torch.randn((npg * page, 128), generator=gen, device=DEV).to(torch.bfloat16)
+        rows = torch.randn((npg * page, head_dim), generator=gen, device=DEV).to(torch.bfloat16)
         ops.quantize_and_insert_k_cache(rows, cache, torch.arange(npg * page, device=DEV), page)
     n = int(qsl[-1])
-    q = torch.randn((n, heads, 128), generator=gen, device=DEV).to(torch.bfloat16)
+    q = torch.randn((n, heads, head_dim), generator=gen, device=DEV).to(torch.bfloat16)
     sink = torch.randn(heads, generator=gen, device=DEV)
     out = ops.sparse_prefill(q, torch.from_numpy(qsl).to(DEV), torch.from_numpy(seq).to(DEV), swa, 64,
                              torch.from_numpy(swa_bt).to(DEV), comp, 2, torch.from_numpy(comp_bt).to(DEV),
-                             128, 128, 128 ** -0.5, sink)
+                             128, 128, head_dim ** -0.5, sink)
     t2r = M.token_to_req_indices(qsl)
     pos = np.concatenate([np.arange(p, p + c) for p, c in reqs])
     ref = A.sparse_prefill_paged(q.float().cpu().numpy(), pos, t2r, swa.cpu().numpy(), 64, swa_bt,
-                                 comp.cpu().numpy(), 2, comp_bt, 128, 128, 128 ** -0.5,
-                                 sink.cpu().numpy(), 128, 64)
+                                 comp.cpu().numpy(), 2, comp_bt, 128, 128, head_dim ** -0.5,
+                                 sink.cpu().numpy(), head_dim, 64)
     check_close(out.float().cpu().numpy(), ref)
     assert ops.device_error() == 0
 
@@ -331,3 +332,31 @@ def test_decode_million_token_context(splits):
     16 CTAs per request."""
     ctx = [1048573, 1048000, 900001, 1048575 - 128 * 5]
     _decode_case(ctx, 3, 64, splits, seed=51, maxc=8320)
+
+
+# ---- head_dim 512 (the model's own head size): CTA-pair kernel ----
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("q_per_seq", [1, 3])
+def test_decode_head_dim_512(q_per_seq, splits):
+    """64 heads x 512: tiles of 2 tokens, so a 3-token group spans two tiles
+    (the second half empty) whose split partials meet in one merge."""
+    ctx = [0, 5, 127, 128, 700, 9000, 40000]
+    _decode_case(ctx, q_per_seq, 64, splits, seed=61 + q_per_seq + splits, maxc=320, head_dim=512)
+
+
+@pytest.mark.parametrize("sink_mode", ["neginf", "none"])
+def test_decode_head_dim_512_16_heads(sink_mode):
+    # 16 heads: all 3 tokens of a request in one 48-row tile; window-only rows
+    _decode_case([3, 200, 2000], 3, 16, 2, seed=67, sink_mode=sink_mode, comp=False, maxc=32, head_dim=512)
+
+
+def test_decode_head_dim_512_long_context():
+    # many compressed rows per tile, split-K over 8 pairs
+    _decode_case([130000, 65000], 3, 64, 8, seed=69, maxc=1024, head_dim=512)
+
+
+@pytest.mark.parametrize("heads", [16, 64])
+def test_prefill_head_dim_512(heads):
+    _prefill_case([(0, 130), (3000, 67), (128 * 9 - 1, 5)], heads, seed=71 + heads, head_dim=512)

@@ -16,6 +16,7 @@
 // tile.  S = Q K^T and O += P V run on the tensor cores (m16n8k16 bf16, fp32
 // accumulate), softmax online in base 2.  Decode splits a group's rows
 // across CTAs (split-K) and the last CTA to finish combines the partials.
+#include "hca_attention.cuh"
 #include "hca_common.cuh"
 #include "hca_tc.cuh"
 
@@ -24,7 +25,6 @@ namespace {
 
 constexpr int kChunk = 64;     // KV rows per pipeline step
 constexpr int kMaxWarps = 12;  // 192 query rows per CTA
-constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, const uint32_t* b) {
   asm volatile(
@@ -48,165 +48,6 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t* r, const void* smem)
                : "r"(a));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Where the rows of a group come from.
-struct AttnParams {
-  // q / out
-  const __nv_bfloat16* q;
-  int64_t q_st, q_sh;
-  __nv_bfloat16* out;
-  int64_t o_st, o_sh;
-  float* lse;
-  int num_heads, rope_dim;
-  // caches
-  const uint8_t* swa_cache;
-  int swa_page;
-  int64_t swa_pstride;
-  const uint8_t* comp_cache;
-  int comp_page;
-  int64_t comp_pstride;
-  // decode: index tables
-  const int32_t* swa_idx;
-  int64_t swa_idx_st;
-  const int32_t* swa_lens;
-  const int32_t* comp_idx;
-  int64_t comp_idx_st;
-  const int32_t* comp_lens;
-  const int32_t* group_starts;  // nullptr: one token per group
-  // prefill: block tables
-  const int32_t* qsl;
-  const int32_t* seq_lens;
-  int num_reqs;
-  const int32_t* swa_bt;
-  int64_t swa_bt_st;
-  const int32_t* comp_bt;
-  int64_t comp_bt_st;
-  int window, ratio;
-  int group_tokens;  // prefill tile size in tokens
-  // softmax
-  float scale_log2;
-  const float* sink;
-  // split-K
-  int num_splits;
-  float* ws_o;      // [groups][splits][rows][D], or [items][rows][D] with a schedule
-  float* ws_ml;     // [groups][splits][rows][2], or [items][rows][2] with a schedule
-  int max_rows;     // query rows per group slot in the workspace
-  // decode work list (nullptr: num_splits uniform splits per group):
-  // sched[4 * i .. 4 * i + 3] = {group, split, chunk begin, chunk end} of CTA
-  // i (group -1: idle), then per group {first item, items}
-  const int32_t* sched;
-  int sched_items;
-  // every CTA writes its partial, even a group's only CTA (the merge happens
-  // in the fused combine + VHA kernel)
-  int force_partials;
-};
-
-// Resolved description of one group.
-struct Group {
-  int t0, ntok;        // first token, tokens
-  int n_win, n_comp;   // union rows: window then compressed
-  // decode (index tables)
-  int len0, len_last, first_tok, last_tok;
-  // prefill (block tables)
-  int req;
-  int64_t p0;          // position of token t0
-  int64_t win_start;   // position of union window row 0
-};
-
-template <bool kPrefill>
-__device__ __forceinline__ bool resolve_group(const AttnParams& P, int gidx, Group& G) {
-  if (!kPrefill) {
-    int t0, t1;
-    if (P.group_starts) {
-      t0 = P.group_starts[gidx];
-      t1 = P.group_starts[gidx + 1];
-    } else {
-      t0 = gidx;
-      t1 = gidx + 1;
-    }
-    G.t0 = t0;
-    G.ntok = t1 - t0;
-    G.first_tok = t0;
-    G.last_tok = t1 - 1;
-    G.len0 = P.swa_lens[t0];
-    G.len_last = P.swa_lens[t1 - 1];
-    if (G.len0 <= 0) {  // padding group
-      G.n_win = 0;
-      G.n_comp = 0;
-      return true;
-    }
-    int extra = G.ntok - 1;
-    if (extra > G.len_last) extra = G.len_last;
-    G.n_win = G.len0 + extra;
-    G.n_comp = P.comp_cache ? P.comp_lens[t1 - 1] : 0;
-    if (G.n_comp < 0) G.n_comp = 0;
-    return true;
-  }
-  // prefill: tile gidx -> (request, first token) by walking the requests
-  int tile = gidx;
-  for (int r = 0; r < P.num_reqs; ++r) {
-    const int qs = P.qsl[r], qe = P.qsl[r + 1];
-    const int ntiles = (qe - qs + P.group_tokens - 1) / P.group_tokens;
-    if (tile < ntiles) {
-      G.req = r;
-      G.t0 = qs + tile * P.group_tokens;
-      G.ntok = min(P.group_tokens, qe - G.t0);
-      G.p0 = static_cast<int64_t>(P.seq_lens[r]) - (qe - qs) + (G.t0 - qs);
-      const int64_t plast = G.p0 + G.ntok - 1;
-      G.win_start = G.p0 - P.window + 1 > 0 ? G.p0 - P.window + 1 : 0;
-      G.n_win = static_cast<int>(plast + 1 - G.win_start);
-      G.n_comp = P.comp_cache ? static_cast<int>((plast + 1) / P.ratio) : 0;
-      return true;
-    }
-    tile -= ntiles;
-  }
-  return false;
-}
-
-// Source slot of union row u and the bitmask of group tokens that attend it.
-template <bool kPrefill>
-__device__ __forceinline__ void row_source(const AttnParams& P, const Group& G, int u,
-                                           bool& is_comp, int64_t& slot, uint32_t& mask) {
-  mask = 0;
-  slot = -1;
-  is_comp = u >= G.n_win;
-  if (!kPrefill) {
-    if (!is_comp) {
-      slot = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
-                        : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
-      for (int k = 0; k < G.ntok; ++k) {
-        const int lk = P.swa_lens[G.t0 + k];
-        if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) mask |= 1u << k;
-      }
-    } else {
-      const int i = u - G.n_win;
-      slot = P.comp_idx[G.last_tok * P.comp_idx_st + i];
-      for (int k = 0; k < G.ntok; ++k)
-        if (i < P.comp_lens[G.t0 + k]) mask |= 1u << k;
-    }
-    if (slot < 0) mask = 0;
-    return;
-  }
-  if (!is_comp) {
-    const int64_t pos = G.win_start + u;
-    slot = static_cast<int64_t>(P.swa_bt[G.req * P.swa_bt_st + pos / P.swa_page]) * P.swa_page +
-           pos % P.swa_page;
-    for (int k = 0; k < G.ntok; ++k) {
-      const int64_t pk = G.p0 + k;
-      if (pos <= pk && pos > pk - P.window) mask |= 1u << k;
-    }
-  } else {
-    const int i = u - G.n_win;
-    slot = static_cast<int64_t>(P.comp_bt[G.req * P.comp_bt_st + i / P.comp_page]) * P.comp_page +
-           i % P.comp_page;
-    for (int k = 0; k < G.ntok; ++k)
-      if (i < (G.p0 + k + 1) / P.ratio) mask |= 1u << k;
-  }
-}
 
 template <int D, int NOPE, int NW, bool kPrefill>
 __global__ void __launch_bounds__(NW * 32, 1) hca_attention_kernel(const AttnParams P) {
@@ -1618,9 +1459,16 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   } else {
     HCA_CHECK_ARG(num_splits >= 1 && num_splits <= 16);
   }
-  if (head_dim != 128 || rope_dim != 64 || num_heads < 1 || max_group_tokens < 1 || max_group_tokens > 30 ||
-      max_group_tokens * num_heads > tcd::kMaxRows)
+  // head_dim 512 runs on CTA pairs (uniform splits, unfused output)
+  const bool wide = head_dim == 512;
+  if (wide) {
+    if (rope_dim != 64 || schedule || fused || num_heads < 1 || num_heads > 128 || max_group_tokens < 1 ||
+        max_group_tokens > 30)
+      return HCA_E_UNSUPPORTED;
+  } else if (head_dim != 128 || rope_dim != 64 || num_heads < 1 || max_group_tokens < 1 || max_group_tokens > 30 ||
+             max_group_tokens * num_heads > tcd::kMaxRows) {
     return HCA_E_UNSUPPORTED;
+  }
   if (num_tokens == 0 || num_groups == 0) return HCA_OK;
   HCA_CHECK_ARG(out && q && swa_cache && swa_indices && swa_lens);
   HCA_CHECK_ARG(!comp_cache || (comp_indices && comp_lens && comp_page_size > 0));
@@ -1677,6 +1525,15 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
     P.ws_ml = reinterpret_cast<float*>(w + o);
   }
   cudaStream_t s = as_stream(stream);
+  int* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
+  if (wide) {
+    P.group_tokens = wide_tile_tokens(num_heads);
+    const int wrc = launch_wide_attention(P, false, num_groups, max_group_tokens, err, s);
+    if (wrc != HCA_OK || num_splits == 1) return wrc;
+    return launch_pdl(hca_attention_combine_kernel<512, false>, dim3(num_groups, (P.max_rows + 15) / 16), dim3(256),
+                      0, s, P);
+  }
   static bool smem_set = false;  // one attribute call per process (same value every time)
   if (!smem_set) {
     if (cudaFuncSetAttribute(hca_tc_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1684,8 +1541,6 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
       return HCA_E_CUDA;
     smem_set = true;
   }
-  int* err = nullptr;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
   const int lrc = launch_pdl(hca_tc_attention_kernel<false>, schedule ? dim3(max_items, 1) : dim3(num_splits, num_groups),
                              dim3(tcd::kThreads), tcd::kSmemBytes, s, P, err);
   if (lrc != HCA_OK) return lrc;
@@ -1833,9 +1688,13 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
                                   const float* attn_sink, void* stream) {
   HCA_CHECK_ARG(num_reqs >= 0 && num_tokens >= 0 && swa_page_size > 0 && window > 0 &&
                 compress_ratio > 0);
-  const int group_tokens = num_heads > 0 ? (kMaxWarps * 16) / num_heads : 0;
-  if (group_tokens < 1 || !attn_shape_ok(num_heads, head_dim, rope_dim, group_tokens))
+  const bool wide = head_dim == 512;
+  const int group_tokens = num_heads > 0 ? (wide ? wide_tile_tokens(num_heads) : (kMaxWarps * 16) / num_heads) : 0;
+  if (wide) {
+    if (rope_dim != 64 || num_heads < 1 || num_heads > 128) return HCA_E_UNSUPPORTED;
+  } else if (group_tokens < 1 || !attn_shape_ok(num_heads, head_dim, rope_dim, group_tokens)) {
     return HCA_E_UNSUPPORTED;
+  }
   if (num_reqs == 0 || num_tokens == 0) return HCA_OK;
   HCA_CHECK_ARG(out && q && query_start_loc && seq_lens && swa_cache && swa_block_table);
   HCA_CHECK_ARG(!comp_cache || (comp_block_table && comp_page_size > 0));
@@ -1869,6 +1728,16 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
   P.scale_log2 = softmax_scale * kLog2e;
   P.sink = attn_sink;
   P.num_splits = 1;
+  if (wide) {
+    // CTA pairs over tiles of 128 / H tokens, all of a tile's rows
+    HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(swa_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(comp_cache) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride_tok % 8 == 0 && q_stride_head % 8 == 0);
+    HCA_CHECK_ARG(out_stride_head % 8 == 0 && out_stride_tok % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0);
+    int* err = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
+    const int num_tiles = num_tokens / group_tokens + num_reqs;
+    return launch_wide_attention(P, true, num_tiles, 0, err, as_stream(stream));
+  }
   if (head_dim == 128 && rope_dim == 64 && num_heads <= tcd::kMaxRows) {
     // tcgen05 path: tiles of up to 256 query rows (at most 32 tokens, one
     // mask bit each), all of a tile's rows in one CTA

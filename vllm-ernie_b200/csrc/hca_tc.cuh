@@ -91,6 +91,63 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return true;
 }
 
+// ------------------------------------------------------- 2-CTA clusters
+// Rank of this CTA in its cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+
+// Shared-memory address of the same location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+
+// 16-byte store into a cluster CTA's shared memory (address from mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Arrive on a cluster CTA's mbarrier (address from mapa_shared), releasing
+// this thread's earlier shared-memory accesses at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(remote_bar) : "memory");
+}
+
+// try_wait on a local mbarrier whose arrivals come from another CTA of the
+// cluster: acquire at cluster scope, so that CTA's released stores are seen.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait_cluster(bar, parity))
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+
+// Every thread of every CTA of the cluster meets here (all threads of each
+// warp execute it together); earlier shared-memory accesses are released to,
+// and acquired from, the whole cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
 // --------------------------------------------------------- bulk async copy
 // One contiguous global -> shared copy completing `bytes` on `bar`
 // (16-byte aligned addresses, size a multiple of 16).  No multicast.
@@ -106,6 +163,11 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
 // 16-byte global -> shared copy through L2 (LSU path, no TMA).
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
+}
+
+// 8-byte global -> shared copy (both addresses 8-byte aligned).
+__device__ __forceinline__ void cp_async8(void* dst_smem, const void* src_gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");
 }
 
 // Close the current group of this thread's cp.async copies.
