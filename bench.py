@@ -40,7 +40,6 @@ CTX_LO, CTX_HI = 4096, 131072
 MAX_COMPRESSED = 1024  # ceil(131072 / 128) rounded to 128
 METRIC = "HCA attn tokens/s & HBM roofline % (decode, 128K ctx, fp8 KV) at 1/2/4/8 B200"
 UNIT = "tokens/s"
-ROW_BYTES_ALGO = 64 + 2 * 64 + 64 // 64  # N + 2R + N/64 at D=128
 
 
 def peaks() -> tuple[float, str]:
@@ -57,12 +56,18 @@ def contexts(rank: int) -> np.ndarray:
     return rng.integers(CTX_LO, CTX_HI - Q_PER_SEQ, size=BATCH, endpoint=True)
 
 
+def row_bytes_algo(head_dim: int, rope_dim: int = 64) -> int:
+    """Bytes of one cached row: N e4m3 + 2R bf16 + N/64 scales (N = D - R)."""
+    nope = head_dim - rope_dim
+    return nope + 2 * rope_dim + nope // 64
+
+
 def algorithmic_bytes(ctx: np.ndarray, heads: int, head_dim: int) -> int:
     """Unique KV rows read + Q read + O write of one attention launch."""
     last = ctx + Q_PER_SEQ - 1
     rows = (last + 1) // 128 + np.minimum(last + 1, 128 + Q_PER_SEQ - 1)
     t = len(ctx) * Q_PER_SEQ
-    return int(rows.sum()) * ROW_BYTES_ALGO + 2 * t * heads * head_dim * 2
+    return int(rows.sum()) * row_bytes_algo(head_dim) + 2 * t * heads * head_dim * 2
 
 
 class ClockSampler:
@@ -473,6 +478,9 @@ def main():
                     help="decode: the headline metric (config 2); prefill: config 3, a supplementary line")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="HCA layers per step (37 in the model; fewer only for profiler captures)")
+    ap.add_argument("--head-dim", type=int, default=128, choices=[128, 512],
+                    help="128: config 2 (the headline); 512: the same decode at the model's own head size, "
+                         "a supplementary line")
     args = ap.parse_args()
     ws, rank, local = setup_dist(cpu_only=args.impl == "reference")
     if args.impl == "reference":
@@ -490,7 +498,8 @@ def main():
                                            rope_cos_sin_cache)
 
     dev = torch.device("cuda", local)
-    dims = HCADims(heads=64, head_dim=128, rope_dim=64, n_groups=8)
+    dims = HCADims(heads=64, head_dim=args.head_dim, rope_dim=64, n_groups=8)
+    wide = args.head_dim == 512
     ctx = contexts(rank)
     batch = make_decode_batch(ctx.tolist(), Q_PER_SEQ, dims, dev, seed=rank, max_model_len=CTX_HI)
     T = batch.num_tokens
@@ -519,8 +528,8 @@ def main():
     # window indices, C128A indices; per layer: insert, state save, compress,
     # attention (+ split-K combine), VHA/inverse-RoPE/FP8
     combine = md.schedule is not None or md.num_splits > 1
-    # scheduled: the split merge is fused into the VHA/quant launch
-    per_layer = 5 if (md.schedule is not None or md.num_splits == 1) else 6
+    # scheduled at head_dim 128: the split merge is fused into the VHA/quant launch
+    per_layer = 5 if ((md.schedule is not None and not wide) or md.num_splits == 1) else 6
     launches_per_step = 7 + (1 if md.schedule is not None else 0) + layers * per_layer
     step()  # warm (allocations, workspace)
     torch.cuda.synchronize()
@@ -588,7 +597,7 @@ def main():
     achieved = algo / (attn_us * 1e-6) / 1e9
     traffic = None
     prof = os.path.join(ROOT, "profiles", "decode_attention_traffic.json")
-    if os.path.exists(prof):
+    if os.path.exists(prof) and not wide:
         try:
             with open(prof) as f:
                 traffic = json.load(f).get("bytes_per_launch")
@@ -629,7 +638,7 @@ def main():
                if cache_bytes > 126e6 else f"caches {cache_bytes / 1e6:.0f} MB fit in L2 (profiling case only)")
 
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not wide:
         sys.path.insert(0, ROOT)
         cpu = cpu_sample_tokens_per_s(15.0)
 
@@ -638,7 +647,10 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers",
+            "config": {"workload": (f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers"
+                                    if not wide else
+                                    f"config 2 requests at the model's head_dim (64 req x 3 q, ctx U[4K,128K], "
+                                    f"H=64, D=512, fp8 KV) x {layers} HCA layers"),
                        "parallelism": f"dp{ws}", "layers": layers, "tokens_per_step_per_gpu": T,
                        "split_k": (f"balanced work list, {md.max_items} CTAs" if md.schedule is not None
                                    else f"{md.num_splits} uniform splits per request"),
@@ -646,7 +658,8 @@ def main():
                        "per_layer_us": ms * 1e3 / layers},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
-                         "kernel": "hca_tc_attention_kernel<decode>" + (" + split merge" if combine else ""),
+                         "kernel": ("hca_wide_attention_kernel<decode> (CTA pairs)" if wide
+                                    else "hca_tc_attention_kernel<decode>") + (" + split merge" if combine else ""),
                          "launch_us": attn_us,
                          "algorithmic_bytes": algo},
             "cpu_baseline": cpu,

@@ -7,6 +7,8 @@ vs the oracle's fp64 evaluation on the same cached rows must have
 checked bit-exactly against the oracle's builders first.
 """
 
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -33,9 +35,10 @@ def check_close(got: np.ndarray, ref: np.ndarray, max_abs=MAX_ABS, max_rel=MAX_R
 
 
 def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=True, sm_count=148, maxc=1024,
-                 head_dim=128):
+                 head_dim=128, whole_groups=False):
     """``splits=None``: the balanced work list for ``sm_count`` CTAs; ``maxc``:
-    compressed-index width (context up to maxc * 128)."""
+    compressed-index width (context up to maxc * 128); ``whole_groups``: one
+    group per request however many rows it has (uniform splits only)."""
     from vllm_ernie_b200 import ops
     from vllm_ernie_b200.decode import build_decode_metadata
     from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
@@ -46,6 +49,8 @@ def _decode_case(ctx, q_per_seq, heads, splits, seed, sink_mode="random", comp=T
     md = build_decode_metadata(b, maxc, num_splits=splits, sm_count=sm_count)
     if splits is None:
         check_schedule(md)
+    if whole_groups:
+        md = dataclasses.replace(md, group_starts=b.query_start_loc, max_group_tokens=q_per_seq)
     # index tables vs the oracle builders (bit-exact)
     qsl, sl = b.query_start_loc.cpu().numpy(), b.seq_lens.cpu().numpy()
     t2r = M.token_to_req_indices(qsl)
@@ -337,13 +342,21 @@ def test_decode_million_token_context(splits):
 # ---- head_dim 512 (the model's own head size): CTA-pair kernel ----
 
 
-@pytest.mark.parametrize("splits", [1, 3])
+@pytest.mark.parametrize("splits", [1, 3, None])
 @pytest.mark.parametrize("q_per_seq", [1, 3])
 def test_decode_head_dim_512(q_per_seq, splits):
-    """64 heads x 512: tiles of 2 tokens, so a 3-token group spans two tiles
-    (the second half empty) whose split partials meet in one merge."""
+    """64 heads x 512: groups of at most 2 tokens (one 128-row tile of a CTA
+    pair); None = the balanced work list."""
     ctx = [0, 5, 127, 128, 700, 9000, 40000]
-    _decode_case(ctx, q_per_seq, 64, splits, seed=61 + q_per_seq + splits, maxc=320, head_dim=512)
+    _decode_case(ctx, q_per_seq, 64, splits, seed=61 + q_per_seq + (splits or 5), maxc=320, head_dim=512)
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+def test_decode_head_dim_512_whole_groups(splits):
+    """A 3-token group of 64 heads (192 rows) spans two pair tiles, whose
+    partials (or outputs) land in the group's rows."""
+    ctx = [0, 5, 127, 128, 700, 9000, 40000]
+    _decode_case(ctx, 3, 64, splits, seed=81 + splits, maxc=320, head_dim=512, whole_groups=True)
 
 
 @pytest.mark.parametrize("sink_mode", ["neginf", "none"])

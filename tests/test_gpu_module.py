@@ -1,8 +1,9 @@
 """The drop-in module on the GPU: ``Ernie5_5HCAAttention.forward`` through the
 backend's metadata builders and the forward context, against the whole-layer
-CPU oracle (config 1: hidden 2048, 16 heads x 128, prefill of 1024 and 640
-tokens from an empty cache, then an ECHO/MTP decode step of 3 tokens per
-request on the caches the prefill wrote).
+CPU oracle (config 1: hidden 2048, 16 heads x 128, and the same with the
+model's head_dim 512; prefill of 1024 and 640 tokens from an empty cache, then
+an ECHO/MTP decode step of 3 tokens per request on the caches the prefill
+wrote).
 
 Tolerance: the layer output (after wo_b) against the oracle's emulated
 evaluation (the FP8/UE8M0 cache and bf16 roundings of the reference kernels)
@@ -46,24 +47,28 @@ def _metadata(layer, swa_bt, comp_bt, st_bt, qsl, seq_lens, positions, spec_toke
                                        positions=pos_d, max_seq_len=int(max(seq_lens)))
 
     cm_swa, cm_comp, cm_st = common(swa_bt, 64), common(comp_bt, 256), common(st_bt, 8)
-    swa = SWAMetadataBuilder(128, 4096, layer.n_local_heads, num_speculative_tokens=spec_tokens, device=DEV).build(0, cm_swa)
+    swa = SWAMetadataBuilder(128, 4096, layer.n_local_heads, num_speculative_tokens=spec_tokens, device=DEV,
+                             head_dim=layer.head_dim).build(0, cm_swa)
     c128 = C128AMetadataBuilder(layer.max_model_len, 4096, num_speculative_tokens=spec_tokens, device=DEV).build(
         0, cm_comp, cm_swa.slot_mapping)
     comp = CompressorMetadataBuilder(4096, device=DEV).build(0, cm_st)
     return HCAStepMetadata(swa, c128, comp).as_forward_context([PREFIX]), pos_d
 
 
-def test_module_forward_prefill_then_decode_matches_layer_oracle():
+@pytest.mark.parametrize("head_dim", [128, 512])
+def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim):
+    """head_dim 128 is config 1; 512 is the model's own head size (the CTA-pair
+    attention kernel, head_dim-512 cache rows, compressor and output path)."""
     from vllm_ernie_b200 import attention as A
     from vllm_ernie_b200.cache_layout import page_bytes
     from vllm_ernie_b200.forward_context import set_forward_context
 
-    shape = HCAShape()
+    shape = HCAShape(head_dim=head_dim)
     weights = random_weights(shape, seed=0)
     max_len = 1152
     oracle = HCALayerOracle(shape, weights, max_len=max_len, num_reqs=2, emulate_quant=True)
 
-    cfg = A.Ernie5_5HCAConfig(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, head_dim=128,
+    cfg = A.Ernie5_5HCAConfig(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, head_dim=head_dim,
                               q_lora_rank=512, qk_rope_head_dim=64, o_groups=4, o_lora_rank=64,
                               hybrid_mla_num_attention_heads=16, num_nextn_predict_layers=0,
                               compress_rope_theta=shape.rope_theta)
@@ -73,14 +78,16 @@ def test_module_forward_prefill_then_decode_matches_layer_oracle():
     assert loaded == set(weights)
     layer.process_weights_after_loading()
     # the oracle's page numbering (contiguous pages per request); the page
-    # strides are the engine's: the compressed cache's 388-byte pages padded
-    # to the 576-byte alignment every HCA cache spec uses
+    # strides are the engine's: the compressed cache's pages (388 bytes at
+    # head_dim 128, 1168 at 512) padded to the 576-byte alignment every HCA
+    # cache spec uses
     cache_spec = layer.get_kv_cache_spec()
     swa = torch.zeros(oracle.swa_cache.shape, dtype=torch.uint8, device=DEV)
     comp = torch.zeros((oracle.comp_cache.shape[0], cache_spec["compressed"].page_size_bytes), dtype=torch.uint8,
                        device=DEV)
     state = torch.zeros(oracle.state.shape, dtype=torch.float32, device=DEV)
-    assert swa.shape[1] == page_bytes(64, 128, 64) and comp.shape[1] == 576
+    assert swa.shape[1] == page_bytes(64, head_dim, 64) and comp.shape[1] % 576 == 0
+    assert comp.shape[1] >= page_bytes(2, head_dim, 64)
     layer.bind_kv_cache(swa, comp, state)
 
     g = torch.Generator().manual_seed(1)

@@ -1462,8 +1462,9 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   // head_dim 512 runs on CTA pairs (uniform splits, unfused output)
   const bool wide = head_dim == 512;
   if (wide) {
-    if (rope_dim != 64 || schedule || fused || num_heads < 1 || num_heads > 128 || max_group_tokens < 1 ||
-        max_group_tokens > 30)
+    // with the work list, every group fits one pair's tile
+    if (rope_dim != 64 || fused || num_heads < 1 || num_heads > 128 || max_group_tokens < 1 ||
+        max_group_tokens > 30 || (schedule && max_group_tokens > wide_tile_tokens(num_heads)))
       return HCA_E_UNSUPPORTED;
   } else if (head_dim != 128 || rope_dim != 64 || num_heads < 1 || max_group_tokens < 1 || max_group_tokens > 30 ||
              max_group_tokens * num_heads > tcd::kMaxRows) {
@@ -1530,7 +1531,7 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   if (wide) {
     P.group_tokens = wide_tile_tokens(num_heads);
     const int wrc = launch_wide_attention(P, false, num_groups, max_group_tokens, err, s);
-    if (wrc != HCA_OK || num_splits == 1) return wrc;
+    if (wrc != HCA_OK || slot_splits == 1) return wrc;
     return launch_pdl(hca_attention_combine_kernel<512, false>, dim3(num_groups, (P.max_rows + 15) / 16), dim3(256),
                       0, s, P);
   }

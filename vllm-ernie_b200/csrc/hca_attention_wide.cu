@@ -26,9 +26,10 @@
 // Work: decode -- split s of tile k of group g, a tile being up to 128 / H
 // consecutive tokens of the group (their union of rows, per-token masks);
 // the split partials go to the group's workspace rows (tile k at row
-// k * tokens_per_tile * H) for the head_dim-512 split merge.  Prefill -- one
-// pair per tile of tokens, rows from the block tables, output written
-// directly.
+// k * tokens_per_tile * H) for the head_dim-512 split merge.  With the
+// balanced work list, groups hold at most one tile and pair i runs item i.
+// Prefill -- one pair per tile of tokens, rows from the block tables, output
+// written directly.
 #include "hca_attention.cuh"
 #include "hca_common.cuh"
 #include "hca_tc.cuh"
@@ -121,6 +122,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
   Group G;
   if (kPrefill) {
     if (!resolve_group<true>(P, work, G)) return;
+  } else if (P.sched) {
+    // balanced work list over groups of at most one tile of tokens
+    const int4 it = reinterpret_cast<const int4*>(P.sched)[work];
+    if (it.x < 0) return;
+    int t0, t1;
+    group_tokens(P, it.x, t0, t1);
+    if (t1 - t0 > P.group_tokens || (t1 - t0) * H > P.max_rows) return;
+    resolve_tokens(P, t0, t1, G);
+    item = work;
+    single = P.sched[4 * P.sched_items + 2 * it.x + 1] == 1;
+    c_begin = it.z;
+    c_end = it.w;
   } else {
     const int split = work % P.num_splits;
     const int gt = work / P.num_splits;
@@ -639,9 +652,10 @@ int launch_wide_attention(const AttnParams& P, bool prefill, int num_groups, int
       return HCA_E_CUDA;
     smem_set[prefill] = true;
   }
-  const int tiles_per_group = prefill ? 1 : (max_group_tokens + P.group_tokens - 1) / P.group_tokens;
+  const int tiles_per_group = prefill || P.sched ? 1 : (max_group_tokens + P.group_tokens - 1) / P.group_tokens;
   const int64_t pairs = prefill ? static_cast<int64_t>(num_groups)
-                                : static_cast<int64_t>(num_groups) * tiles_per_group * P.num_splits;
+                        : P.sched ? static_cast<int64_t>(P.sched_items)
+                                  : static_cast<int64_t>(num_groups) * tiles_per_group * P.num_splits;
   if (pairs <= 0) return HCA_OK;
   if (2 * pairs > 0x7fffffff) return HCA_E_INVALID;
   kernel<<<dim3(static_cast<unsigned>(2 * pairs)), dim3(kThreads), kSmemBytes, s>>>(P, tiles_per_group, err);

@@ -280,7 +280,9 @@ class Ernie5_5HCAAttention(nn.Module):
             if c128.decode_schedule is None:
                 # the step's balanced work list: one wave of CTAs over the SMs
                 groups = swa.decode_group_starts.numel() - 1
-                c128.decode_items = max(_sm_count(qp.device), groups)
+                # (a CTA per SM; a CTA pair per two SMs at head_dim 512)
+                sms = _sm_count(qp.device)
+                c128.decode_items = max(sms if d == 128 else sms // 2, groups)
                 c128.decode_schedule = ops.decode_schedule(swa.decode_group_starts, ndt, swa.decode_swa_lens,
                                                            c128.c128a_decode_topk_lens, c128.decode_items)
             ops.sparse_decode(qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,

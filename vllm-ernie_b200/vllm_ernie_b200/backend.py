@@ -192,6 +192,12 @@ class CompressorMetadata:
 # ---------------------------------------------------------------------------
 
 
+def decode_group_rows(head_dim: int) -> int:
+    """Query rows (tokens x heads) one decode group may hold: two M=128 tiles
+    of one CTA at head_dim 128, one tile of a CTA pair at head_dim 512."""
+    return 256 if head_dim == 128 else 128
+
+
 def _decode_groups(qsl_cpu: list[int], num_decodes: int, max_tokens: int, device) -> torch.Tensor:
     starts: list[int] = []
     for r in range(num_decodes):
@@ -206,8 +212,9 @@ class SWAMetadataBuilder:
     reorder_batch_threshold = 1
 
     def __init__(self, window_size: int, max_num_batched_tokens: int, num_heads: int,
-                 num_speculative_tokens: int = 0, device="cuda"):
+                 num_speculative_tokens: int = 0, device="cuda", head_dim: int = 128):
         self.window_size = window_size
+        self.head_dim = head_dim
         self.block_size = SWA_BLOCK_SIZE
         self.decode_threshold = self.reorder_batch_threshold + num_speculative_tokens
         self.num_heads = num_heads
@@ -239,7 +246,7 @@ class SWAMetadataBuilder:
             md.prefill_gather_lens = ops.compute_prefill_gather_lens(cm.seq_lens, cm.query_start_loc, npf, nd,
                                                                      self.window_size)
         if ndt > 0:
-            max_g = max(1, 256 // self.num_heads)
+            max_g = max(1, decode_group_rows(self.head_dim) // self.num_heads)
             md.decode_max_group_tokens = min(max_g, self.decode_threshold)
             md.decode_group_starts = _decode_groups(cm.query_start_loc_cpu.tolist(), nd,
                                                     md.decode_max_group_tokens, self.device)

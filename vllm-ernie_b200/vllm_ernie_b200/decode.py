@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import torch
 
 from . import ops
+from .backend import decode_group_rows
 from .synthetic import DecodeBatch, HCADims, LayerCaches
 
 SM_COUNT_B200 = 148
@@ -85,19 +86,25 @@ def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: i
     pre = get("comp_prefill", (1, max_compressed), torch.int32)
     ops.build_c128a_topk_metadata(batch.positions, d.ratio, T, t2r, batch.comp_bt, d.comp_page,
                                   swa_slot, cidx, clens, pre, max_compressed)
-    max_g = max(1, min(batch.q_per_seq, 256 // d.heads))
+    max_g = max(1, min(batch.q_per_seq, decode_group_rows(d.head_dim) // d.heads))
     if max_g < batch.q_per_seq:
-        # split each request's tokens into sub-groups of max_g tokens
-        starts = [t for r in range(batch.num_reqs) for t in
-                  range(r * batch.q_per_seq, (r + 1) * batch.q_per_seq, max_g)] + [T]
-        gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+        # split each request's tokens into sub-groups of max_g tokens (a fixed
+        # table for the batch shape: built once, so steps stay graph-capturable)
+        key = ("group_starts", batch.num_reqs, batch.q_per_seq, max_g)
+        gs = buf.get(key)
+        if gs is None:
+            starts = [t for r in range(batch.num_reqs) for t in
+                      range(r * batch.q_per_seq, (r + 1) * batch.q_per_seq, max_g)] + [T]
+            gs = torch.tensor(starts, dtype=torch.int32, device=dev)
+            buf[key] = gs
     else:
         gs = qsl
     ngroups = gs.numel() - 1
     if num_splits is not None:
         return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
                               cidx, clens, gs, max_g, num_splits)
-    items = max(sm_count, ngroups)
+    # one wave: a CTA per SM, or a CTA pair per two SMs at head_dim 512
+    items = max(sm_count if d.head_dim == 128 else sm_count // 2, ngroups)
     sched = ops.decode_schedule(gs, T, swa_lens, clens, items, out=buf.get("schedule"))
     buf["schedule"] = sched
     return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
@@ -144,7 +151,7 @@ def decode_layer(batch: DecodeBatch, md: DecodeMetadata, caches: LayerCaches, w:
                                  batch.state_bt, d.state_page, d.head_dim, cos_sin, caches.comp,
                                  md.comp_slot, d.comp_page, d.head_dim, d.rope_dim, d.ratio,
                                  w.comp_norm, d.eps)
-    if quantize and md.schedule is not None:
+    if quantize and md.schedule is not None and d.head_dim == 128:
         # attention + VHA + inverse RoPE + FP8 quant without the bf16 O round trip
         return ops.sparse_decode_vha_fp8_quant(
             q, caches.swa, d.swa_page, md.swa_indices, md.swa_lens, caches.comp, d.comp_page, md.comp_indices,
