@@ -525,11 +525,12 @@ def main():
                                    q_buf=q_buf, o_buf=o_buf)
 
     # metadata: token->req, 2 slot maps, compressed slot map (fill + map),
-    # window indices, C128A indices; per layer: insert, state save, compress,
-    # attention (+ split-K combine), VHA/inverse-RoPE/FP8
+    # window indices, C128A indices (+ the work list); per layer: the decode
+    # prep (Q prep, KV insert, state save, compress), attention, then either
+    # the fused split merge + VHA/inverse-RoPE/FP8 (scheduled, head_dim 128) or
+    # the split merge (if any) and VHA/inverse-RoPE/FP8
     combine = md.schedule is not None or md.num_splits > 1
-    # scheduled at head_dim 128: the split merge is fused into the VHA/quant launch
-    per_layer = 5 if ((md.schedule is not None and not wide) or md.num_splits == 1) else 6
+    per_layer = 3 if (md.schedule is not None and not wide) else (4 if combine else 3)
     launches_per_step = 7 + (1 if md.schedule is not None else 0) + layers * per_layer
     step()  # warm (allocations, workspace)
     torch.cuda.synchronize()

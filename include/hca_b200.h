@@ -181,6 +181,32 @@ int hca_compress_norm_rope_store(const float* state, int64_t state_stride_block,
                                  int32_t num_tokens, int32_t head_dim, int32_t rope_dim,
                                  int32_t compress_ratio, void* stream);
 
+/* One launch for a decode step's per-layer cache work: the three calls above
+ * (hca_qnorm_rope_kv_insert, hca_save_partial_states,
+ * hca_compress_norm_rope_store, in that order) fused, with the same output
+ * bytes.  It has no single reference counterpart: it replaces the decode-time
+ * sequence of the `_C` fused q-norm / RoPE / KV insert
+ * (V/models/deepseek_v4/attention.py:497-542), save_partial_states
+ * (V/models/deepseek_v4/common/ops/save_partial_states.py:48-101) and the
+ * block compressor (.../fused_compress_quant_cache.py:112-296).  The batch
+ * must be decode-shaped: tokens [query_start_loc[r], query_start_loc[r + 1])
+ * of request r, query_start_loc[num_reqs] == num_tokens; a request's blocks
+ * are pooled by the CTA that saved its tokens' states.  state_kv / state_score
+ * are the two halves of the compressor's fp32 kv_score. */
+int hca_decode_prep(void* q_out, int64_t q_out_stride_tok, int64_t q_out_stride_head, int32_t padded_heads,
+                    const void* q, int64_t q_stride_tok, int64_t q_stride_head, int32_t num_heads,
+                    const void* kv, int64_t kv_stride, uint8_t* swa_cache, int32_t swa_page_size,
+                    int64_t swa_page_stride_bytes, const int64_t* swa_slot_mapping, const int64_t* positions,
+                    const float* cos_sin, int64_t cos_sin_stride, const float* state_kv, int64_t state_kv_stride,
+                    const float* state_score, int64_t state_score_stride, const float* ape, int64_t ape_stride,
+                    float* state, int64_t state_stride_block, int64_t state_stride_tok, int32_t state_width,
+                    int32_t state_block_size, const int64_t* state_slot_mapping, const int32_t* state_block_table,
+                    int64_t state_bt_stride, const float* norm_weight, uint8_t* comp_cache,
+                    const int64_t* comp_slot_mapping, int32_t comp_page_size, int64_t comp_page_stride_bytes,
+                    const int32_t* query_start_loc, const int32_t* token_to_req, int32_t num_reqs,
+                    int32_t num_tokens, int32_t head_dim, int32_t rope_dim, int32_t compress_ratio, float eps,
+                    void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Sparse attention over [window || compressed] rows                        */
 /* ---------------------------------------------------------------------- */

@@ -292,3 +292,51 @@ def test_unsupported_dims_raise(ops):
     cache = torch.zeros((1, 4096), dtype=torch.uint8, device=DEV)
     with pytest.raises(HcaError):
         ops.quantize_and_insert_k_cache(k, cache, torch.zeros(4, dtype=torch.int64, device=DEV), 8, 32)
+
+
+# --------------------------------------------------------------------------
+# fused decode prep == the three cache ops in sequence (same bytes)
+# --------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("head_dim,heads,padded", [(128, 64, 64), (128, 16, 64), (512, 64, 64)])
+def test_decode_prep_matches_three_ops(ops, head_dim, heads, padded):
+    """q, SWA cache, compressor state and compressed cache after
+    hca_decode_prep equal, byte for byte, those after
+    hca_qnorm_rope_kv_insert + hca_save_partial_states +
+    hca_compress_norm_rope_store on the same inputs.  Contexts put block
+    boundaries on the first, middle and last query token of a request (the
+    pooled states include ones saved in the same launch)."""
+    from vllm_ernie_b200.decode import build_decode_metadata
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dims = HCADims(heads=heads, head_dim=head_dim)
+    ctx = [0, 125, 126, 127, 253, 1022, 5000, 130000 - 2, 77]
+    b = make_decode_batch(ctx, 3, dims, DEV, seed=7, max_model_len=1024 * 128)
+    caches = alloc_layer_caches(b, seed=8)
+    md = build_decode_metadata(b, 1024, num_splits=1)
+    n = b.num_tokens
+    assert (((b.positions + 1) % 128 == 0).sum() >= 4)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    q = torch.randn((n, heads, head_dim), generator=g, device=DEV).to(torch.bfloat16)
+    kv = torch.randn((n, head_dim), generator=g, device=DEV).to(torch.bfloat16)
+    ks = torch.randn((n, 2 * head_dim), generator=g, device=DEV)
+    ape = torch.randn((128, head_dim), generator=g, device=DEV) * 0.1
+    w = 1.0 + 0.05 * torch.randn(head_dim, generator=g, device=DEV)
+    cs = rope_cos_sin_cache(1024 * 128 + 8, 64, dims.rope_theta, DEV)
+    a = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    f = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    qa = ops.fused_qnorm_rope_kv_insert(q, kv, a[0], md.swa_slot, b.positions, cs, padded, 1e-6, 64, 64)
+    ops.save_partial_states(ks[:, :head_dim], ks[:, head_dim:], ape, b.positions, a[1], md.state_slot, 8,
+                            head_dim, 128)
+    ops.compress_norm_rope_store(a[1], n, md.token_to_req, b.positions, md.state_slot, b.state_bt, 8, head_dim, cs,
+                                 a[2], md.comp_slot, 2, head_dim, 64, 128, w, 1e-6)
+    qf = ops.decode_prep(q, kv, ks, ape, b.positions, cs, f[0], md.swa_slot, 64, f[1], md.state_slot, b.state_bt, 8,
+                         f[2], md.comp_slot, 2, w, b.query_start_loc, md.token_to_req, b.num_reqs, padded, 1e-6,
+                         128, 64)
+    torch.cuda.synchronize()
+    assert torch.equal(qa.view(torch.int16), qf.view(torch.int16))
+    for x, y in zip(a, f):
+        assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+    # the launch did write: boundaries produced compressed rows, states moved
+    assert not torch.equal(f[2], caches.comp) and not torch.equal(f[1], caches.state)

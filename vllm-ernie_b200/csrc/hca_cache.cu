@@ -345,8 +345,10 @@ __device__ __forceinline__ void compress_token(
 #pragma unroll
     for (int j = 0; j < kSub; ++j) {
       const int i = b0 + j;
-      sc[j] = i < i1 ? __ldg(state + row_off[i] + state_width + c) : -INFINITY;
-      kv[j] = i < i1 ? __ldg(state + row_off[i] + c) : 0.0f;
+      // coherent (L2) loads: the fused decode prep pools states that its
+      // own CTA saved earlier in the same launch
+      sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
+      kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
     }
     float mb = m;
 #pragma unroll
@@ -446,6 +448,179 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
                       norm_w, eps, cos_sin, cs_stride, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red,
                       row_off, &part[0][0][0]);
     __syncthreads();  // the shared buffers are reused by the next boundary
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Decode prep: the per-layer cache work of a decode step in one launch.
+//   CTAs [0, num_reqs): request r.  Its tokens' KV rows (RoPE, fp8 NoPE
+//     quant, SWA insert) and compressor states are written, then -- after a
+//     block barrier, so the pooling reads the states just saved -- every block
+//     one of its tokens completes is pooled into the compressed cache
+//     (compress_token, the same code as compress_kernel).  A request's
+//     tokens are consecutive positions of that request only, so no other CTA
+//     writes the states it pools.
+//   CTAs [num_reqs, ...): prep_rows<D>() query rows each (head RMSNorm +
+//     RoPE; padding heads written as zeros), 64 / (D / 32) consecutive rows
+//     per warp with all their loads issued first.
+// The arithmetic of every row is the one of qnorm_rope_kv_insert_kernel,
+// save_partial_states_kernel and compress_kernel, so the outputs are the
+// same bytes as those three launches.
+// ----------------------------------------------------------------------------
+template <int D>
+constexpr int prep_rows_per_warp() { return 64 / (D / 32); }  // 16 at D=128, 4 at D=512
+template <int D>
+constexpr int prep_rows() { return (kCompressThreads / 32) * prep_rows_per_warp<D>(); }
+
+struct DecodePrepParams {
+  // queries
+  __nv_bfloat16* q_out;
+  int64_t qo_st, qo_sh;
+  int padded_heads;
+  const __nv_bfloat16* q;
+  int64_t q_st, q_sh;
+  int num_heads;
+  // KV rows -> SWA cache
+  const __nv_bfloat16* kv;
+  int64_t kv_stride;
+  uint8_t* swa_cache;
+  int swa_page;
+  int64_t swa_pstride;
+  const int64_t* swa_slot;
+  // RoPE
+  const int64_t* positions;
+  const float* cos_sin;
+  int64_t cs_stride;
+  int rope_dim;
+  float eps;
+  // compressor states
+  const float* st_kv;
+  int64_t st_kv_stride;
+  const float* st_score;
+  int64_t st_score_stride;
+  const float* ape;
+  int64_t ape_stride;
+  float* state;
+  int64_t s_blk, s_tok;
+  int state_width, state_page;
+  const int64_t* state_slot;
+  const int32_t* state_bt;
+  int64_t state_bt_stride;
+  // compressed cache
+  const float* norm_w;
+  uint8_t* comp_cache;
+  const int64_t* comp_slot;
+  int comp_page;
+  int64_t comp_pstride;
+  int ratio;
+  // batch
+  const int32_t* qsl;
+  const int32_t* t2r;
+  int num_reqs;
+  int64_t num_tokens;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kCompressThreads, 1) decode_prep_kernel(const DecodePrepParams p) {
+  pdl_wait_and_release();
+  constexpr int E = WarpRow<D>::E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kWarps = kCompressThreads / 32;
+  const int nope = D - p.rope_dim;
+  // this lane's RoPE pairs (dims lane * E + 2i, + 1) at position `pos`
+  auto load_cs = [&](int64_t pos, float* pc, float* ps) {
+    const float* cs = p.cos_sin + pos * p.cs_stride;
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) {
+      const int d = lane * E + 2 * i;
+      pc[i] = 1.0f;
+      ps[i] = 0.0f;
+      if (d >= nope) {
+        pc[i] = cs[(d - nope) >> 1];
+        ps[i] = cs[p.rope_dim / 2 + ((d - nope) >> 1)];
+      }
+    }
+  };
+  if (blockIdx.x >= p.num_reqs) {
+    // ---------------------------------------------------------- query rows
+    constexpr int kRpw = prep_rows_per_warp<D>();
+    const int64_t base = static_cast<int64_t>(blockIdx.x - p.num_reqs) * prep_rows<D>() + warp * kRpw;
+    const int64_t nrows = p.num_tokens * p.padded_heads;
+    WarpRow<D> rows[kRpw];
+    int64_t tok[kRpw];
+    int head[kRpw];
+#pragma unroll
+    for (int b = 0; b < kRpw; ++b) {
+      const int64_t row = base + b;
+      tok[b] = row / p.padded_heads;
+      head[b] = static_cast<int>(row - tok[b] * p.padded_heads);
+      if (row < nrows && head[b] < p.num_heads) rows[b].load_bf16(p.q + tok[b] * p.q_st + head[b] * p.q_sh, lane);
+    }
+#pragma unroll
+    for (int b = 0; b < kRpw; ++b) {
+      if (base + b >= nrows) continue;
+      if (head[b] < p.num_heads) {
+        float pc[E / 2], ps[E / 2];
+        load_cs(p.positions[tok[b]], pc, ps);
+        WarpRow<D>& row = rows[b];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) ss += row.v[i] * row.v[i];
+        ss = warp_sum(ss);
+        const float rrms = rsqrtf(ss / static_cast<float>(D) + p.eps);
+#pragma unroll
+        for (int i = 0; i < E; ++i) row.v[i] *= rrms;
+#pragma unroll
+        for (int i = 0; i < E / 2; ++i) rope_pair(row.v[2 * i], row.v[2 * i + 1], pc[i], ps[i]);
+        row.store_bf16(p.q_out + tok[b] * p.qo_st + head[b] * p.qo_sh, lane);
+      } else {
+        uint16_t* o = reinterpret_cast<uint16_t*>(p.q_out + tok[b] * p.qo_st + head[b] * p.qo_sh) + lane * E;
+#pragma unroll
+        for (int i = 0; i < E; ++i) o[i] = 0;
+      }
+    }
+    return;
+  }
+  // ------------------------------------------------------------ request r
+  __shared__ float red[32];
+  __shared__ int64_t row_off[512];
+  __shared__ float part[3][kCompressThreads / D][D];
+  const int r = blockIdx.x;
+  const int t0 = p.qsl[r], t1 = p.qsl[r + 1];
+  const RowGeom g = row_geom(D, p.rope_dim);
+  // KV rows: one warp per token
+  for (int j = warp; j < t1 - t0; j += kWarps) {
+    const int64_t t = t0 + j;
+    const int64_t slot = p.swa_slot[t];
+    if (slot < 0) continue;
+    WarpRow<D> row;
+    row.load_bf16(p.kv + t * p.kv_stride, lane);
+    float pc[E / 2], ps[E / 2];
+    load_cs(p.positions[t], pc, ps);
+    WarpRow<D> r2 = row;
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) rope_pair(r2.v[2 * i], r2.v[2 * i + 1], pc[i], ps[i]);
+    row.store_cache_row(row_ptr(p.swa_cache, slot, p.swa_page, p.swa_pstride, g), p.rope_dim, lane, true, r2.v);
+  }
+  // compressor states: state[slot] = [kv, score + ape[pos % ratio]]
+  for (int i = threadIdx.x; i < (t1 - t0) * D; i += kCompressThreads) {
+    const int64_t t = t0 + i / D;
+    const int c = i % D;
+    const int64_t slot = p.state_slot[t];
+    if (slot < 0) continue;
+    const int64_t blk = slot / p.state_page;
+    float* sb = p.state + blk * p.s_blk + (slot - blk * p.state_page) * p.s_tok;
+    sb[c] = p.st_kv[t * p.st_kv_stride + c];
+    sb[p.state_width + c] = p.st_score[t * p.st_score_stride + c] + p.ape[(p.positions[t] % p.ratio) * p.ape_stride + c];
+  }
+  __syncthreads();  // the states are visible to the whole CTA
+  for (int j = 0; j < t1 - t0; ++j) {
+    const int64_t t = t0 + j;
+    if (p.state_slot[t] < 0 || (p.positions[t] + 1) % p.ratio != 0) continue;  // uniform
+    compress_token<D>(t, p.state, p.s_blk, p.s_tok, p.state_width, p.t2r, p.positions, p.comp_slot, p.state_bt,
+                      p.state_bt_stride, p.state_page, p.norm_w, p.eps, p.cos_sin, p.cs_stride, p.comp_cache,
+                      p.comp_page, p.comp_pstride, p.rope_dim, p.ratio, red, row_off, &part[0][0][0]);
+    __syncthreads();
   }
 }
 
@@ -581,4 +756,74 @@ extern "C" int hca_compress_norm_rope_store(
                     state_width, token_to_req, positions, state_slot_mapping, block_table, bt_stride, block_size,
                     norm_weight, eps, cos_sin, cos_sin_stride, kv_cache, kv_slot_mapping, kv_page_size,
                     kv_page_stride_bytes, rope_dim, compress_ratio, static_cast<int64_t>(num_tokens));
+}
+
+extern "C" int hca_decode_prep(
+    void* q_out, int64_t q_out_stride_tok, int64_t q_out_stride_head, int32_t padded_heads, const void* q,
+    int64_t q_stride_tok, int64_t q_stride_head, int32_t num_heads, const void* kv, int64_t kv_stride,
+    uint8_t* swa_cache, int32_t swa_page_size, int64_t swa_page_stride_bytes, const int64_t* swa_slot_mapping,
+    const int64_t* positions, const float* cos_sin, int64_t cos_sin_stride, const float* state_kv,
+    int64_t state_kv_stride, const float* state_score, int64_t state_score_stride, const float* ape,
+    int64_t ape_stride, float* state, int64_t state_stride_block, int64_t state_stride_tok, int32_t state_width,
+    int32_t state_block_size, const int64_t* state_slot_mapping, const int32_t* state_block_table,
+    int64_t state_bt_stride, const float* norm_weight, uint8_t* comp_cache, const int64_t* comp_slot_mapping,
+    int32_t comp_page_size, int64_t comp_page_stride_bytes, const int32_t* query_start_loc,
+    const int32_t* token_to_req, int32_t num_reqs, int32_t num_tokens, int32_t head_dim, int32_t rope_dim,
+    int32_t compress_ratio, float eps, void* stream) {
+  HCA_CHECK_ARG(num_tokens >= 0 && num_reqs >= 0 && num_heads > 0 && padded_heads >= num_heads &&
+                swa_page_size > 0 && state_block_size > 0 && comp_page_size > 0 && state_width >= head_dim &&
+                compress_ratio > 0 && compress_ratio <= 512);
+  if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
+  if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(q_out && q && kv && swa_cache && swa_slot_mapping && positions && cos_sin && state_kv &&
+                state_score && ape && state && state_slot_mapping && state_block_table && norm_weight && comp_cache &&
+                comp_slot_mapping && query_start_loc && token_to_req && num_reqs > 0);
+  DecodePrepParams p{};
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.qo_st = q_out_stride_tok;
+  p.qo_sh = q_out_stride_head;
+  p.padded_heads = padded_heads;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_st = q_stride_tok;
+  p.q_sh = q_stride_head;
+  p.num_heads = num_heads;
+  p.kv = static_cast<const __nv_bfloat16*>(kv);
+  p.kv_stride = kv_stride;
+  p.swa_cache = swa_cache;
+  p.swa_page = swa_page_size;
+  p.swa_pstride = swa_page_stride_bytes;
+  p.swa_slot = swa_slot_mapping;
+  p.positions = positions;
+  p.cos_sin = cos_sin;
+  p.cs_stride = cos_sin_stride;
+  p.rope_dim = rope_dim;
+  p.eps = eps;
+  p.st_kv = state_kv;
+  p.st_kv_stride = state_kv_stride;
+  p.st_score = state_score;
+  p.st_score_stride = state_score_stride;
+  p.ape = ape;
+  p.ape_stride = ape_stride;
+  p.state = state;
+  p.s_blk = state_stride_block;
+  p.s_tok = state_stride_tok;
+  p.state_width = state_width;
+  p.state_page = state_block_size;
+  p.state_slot = state_slot_mapping;
+  p.state_bt = state_block_table;
+  p.state_bt_stride = state_bt_stride;
+  p.norm_w = norm_weight;
+  p.comp_cache = comp_cache;
+  p.comp_slot = comp_slot_mapping;
+  p.comp_page = comp_page_size;
+  p.comp_pstride = comp_page_stride_bytes;
+  p.ratio = compress_ratio;
+  p.qsl = query_start_loc;
+  p.t2r = token_to_req;
+  p.num_reqs = num_reqs;
+  p.num_tokens = num_tokens;
+  const int rows_per_cta = head_dim == 128 ? prep_rows<128>() : prep_rows<512>();
+  const int64_t q_ctas = (static_cast<int64_t>(num_tokens) * padded_heads + rows_per_cta - 1) / rows_per_cta;
+  return launch_pdl(head_dim == 128 ? decode_prep_kernel<128> : decode_prep_kernel<512>,
+                    dim3(static_cast<unsigned>(num_reqs + q_ctas)), dim3(kCompressThreads), 0, as_stream(stream), p);
 }

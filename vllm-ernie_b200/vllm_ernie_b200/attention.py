@@ -266,14 +266,22 @@ class Ernie5_5HCAAttention(nn.Module):
         c128 = md[self.prefix]
         comp = md[self.compressor.state_cache_prefix]
         n = swa.slot_mapping.shape[0]
-        qp = ops.fused_qnorm_rope_kv_insert(q, kv, self.swa_cache, swa.slot_mapping, positions, self.cos_sin_cache,
-                                            self.padded_heads, self.eps, SWA_BLOCK_SIZE, r)
-        ops.save_partial_states(kv_score[:, :d], kv_score[:, d:], self.compressor.ape, positions,
-                                self.state_cache, comp.slot_mapping, STATE_BLOCK_SIZE, d, self.compress_ratio)
-        ops.compress_norm_rope_store(self.state_cache, n, comp.token_to_req_indices, positions, comp.slot_mapping,
-                                     comp.block_table, STATE_BLOCK_SIZE, d, self.cos_sin_cache, self.kv_cache,
-                                     c128.slot_mapping, self.comp_page, d, r, self.compress_ratio,
-                                     self.compressor.norm.weight, self.eps)
+        if swa.num_prefills == 0:
+            # decode-only step: the three cache ops below in one launch
+            qp = ops.decode_prep(q, kv, kv_score, self.compressor.ape, positions, self.cos_sin_cache,
+                                 self.swa_cache, swa.slot_mapping, SWA_BLOCK_SIZE, self.state_cache, comp.slot_mapping,
+                                 comp.block_table, STATE_BLOCK_SIZE, self.kv_cache, c128.slot_mapping, self.comp_page,
+                                 self.compressor.norm.weight, swa.query_start_loc, comp.token_to_req_indices,
+                                 swa.num_decodes, self.padded_heads, self.eps, self.compress_ratio, r)
+        else:
+            qp = ops.fused_qnorm_rope_kv_insert(q, kv, self.swa_cache, swa.slot_mapping, positions,
+                                                self.cos_sin_cache, self.padded_heads, self.eps, SWA_BLOCK_SIZE, r)
+            ops.save_partial_states(kv_score[:, :d], kv_score[:, d:], self.compressor.ape, positions,
+                                    self.state_cache, comp.slot_mapping, STATE_BLOCK_SIZE, d, self.compress_ratio)
+            ops.compress_norm_rope_store(self.state_cache, n, comp.token_to_req_indices, positions,
+                                         comp.slot_mapping, comp.block_table, STATE_BLOCK_SIZE, d, self.cos_sin_cache,
+                                         self.kv_cache, c128.slot_mapping, self.comp_page, d, r, self.compress_ratio,
+                                         self.compressor.norm.weight, self.eps)
         ndt, nd = swa.num_decode_tokens, swa.num_decodes
         sink = self.attn_sink[: self.n_local_heads].contiguous()
         if ndt:

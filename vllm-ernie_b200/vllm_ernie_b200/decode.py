@@ -142,15 +142,12 @@ def decode_layer(batch: DecodeBatch, md: DecodeMetadata, caches: LayerCaches, w:
     scale [T, G, HPG])`` (``quantize``) or the bf16 ``[T, H, D]`` output of
     VHA + inverse RoPE."""
     d = batch.dims
-    T = md.num_tokens
-    q = ops.fused_qnorm_rope_kv_insert(q_raw, kv, caches.swa, md.swa_slot, batch.positions, cos_sin,
-                                       d.heads, d.eps, d.swa_page, d.rope_dim, out=q_buf)
-    ops.save_partial_states(kv_score[:, : d.head_dim], kv_score[:, d.head_dim:], w.ape, batch.positions,
-                            caches.state, md.state_slot, d.state_page, d.head_dim, d.ratio)
-    ops.compress_norm_rope_store(caches.state, T, md.token_to_req, batch.positions, md.state_slot,
-                                 batch.state_bt, d.state_page, d.head_dim, cos_sin, caches.comp,
-                                 md.comp_slot, d.comp_page, d.head_dim, d.rope_dim, d.ratio,
-                                 w.comp_norm, d.eps)
+    # Q head-norm + RoPE, KV insert, state save and block compression: one
+    # launch (the same bytes as the three ops in sequence)
+    q = ops.decode_prep(q_raw, kv, kv_score, w.ape, batch.positions, cos_sin, caches.swa, md.swa_slot, d.swa_page,
+                        caches.state, md.state_slot, batch.state_bt, d.state_page, caches.comp, md.comp_slot,
+                        d.comp_page, w.comp_norm, batch.query_start_loc, md.token_to_req, batch.num_reqs, d.heads,
+                        d.eps, d.ratio, d.rope_dim, out=q_buf)
     if quantize and md.schedule is not None and d.head_dim == 128:
         # attention + VHA + inverse RoPE + FP8 quant without the bf16 O round trip
         return ops.sparse_decode_vha_fp8_quant(

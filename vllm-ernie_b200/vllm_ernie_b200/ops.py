@@ -198,6 +198,36 @@ def compress_norm_rope_store(state_cache, num_actual: int, token_to_req_indices,
              head_dim, rope_head_dim, compress_ratio, _s())
 
 
+def decode_prep(q, kv, kv_score, ape, positions, cos_sin_cache, swa_kv_cache, swa_slot_mapping,
+                swa_block_size: int, state_cache, state_slot_mapping, state_block_table, state_block_size: int,
+                kv_cache, kv_slot_mapping, kv_block_size: int, rms_norm_weight, query_start_loc,
+                token_to_req_indices, num_reqs: int, padded_heads: int, eps: float, compress_ratio: int,
+                rope_dim: int = 64, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``fused_qnorm_rope_kv_insert`` + ``save_partial_states`` +
+    ``compress_norm_rope_store`` of a decode-shaped batch (request r owns
+    tokens ``query_start_loc[r] .. query_start_loc[r + 1]``) in one launch,
+    with the same output bytes; returns the padded q.  ``kv_score`` is the
+    compressor's fp32 ``[T, 2 D]`` (kv then score)."""
+    _check_cuda(q, kv, kv_score, ape, positions, cos_sin_cache, swa_kv_cache, swa_slot_mapping, state_cache,
+                state_slot_mapping, state_block_table, kv_cache, kv_slot_mapping, rms_norm_weight,
+                query_start_loc, token_to_req_indices)
+    t, h, d = q.shape
+    if out is None:
+        out = torch.empty((t, padded_heads, d), dtype=q.dtype, device=q.device)
+    n = swa_slot_mapping.shape[0]
+    if n:
+        ks, sc = kv_score[:, :d], kv_score[:, d:]
+        call("hca_decode_prep", _p(out), out.stride(0), out.stride(1), padded_heads, _p(q), q.stride(0),
+             q.stride(1), h, _p(kv), kv.stride(0), _p(swa_kv_cache), swa_block_size, swa_kv_cache.stride(0),
+             _p(swa_slot_mapping), _p(positions), _p(cos_sin_cache), cos_sin_cache.stride(0), _p(ks), ks.stride(0),
+             _p(sc), sc.stride(0), _p(ape), ape.stride(0), _p(state_cache), state_cache.stride(0),
+             state_cache.stride(1), d, state_block_size, _p(state_slot_mapping), _p(state_block_table),
+             state_block_table.stride(0), _p(rms_norm_weight), _p(kv_cache), _p(kv_slot_mapping), kv_block_size,
+             kv_cache.stride(0), _p(query_start_loc), _p(token_to_req_indices), num_reqs, n, d, rope_dim,
+             compress_ratio, eps, _s())
+    return out
+
+
 # ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
