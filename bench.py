@@ -478,6 +478,8 @@ def main():
                     help="decode: the headline metric (config 2); prefill: config 3, a supplementary line")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="HCA layers per step (37 in the model; fewer only for profiler captures)")
+    ap.add_argument("--items", type=int, default=0,
+                    help="work-list items per step (0: one wave of CTAs, or of CTA pairs at head_dim 512)")
     ap.add_argument("--head-dim", type=int, default=128, choices=[128, 512],
                     help="128: config 2 (the headline); 512: the same decode at the model's own head size, "
                          "a supplementary line")
@@ -513,13 +515,14 @@ def main():
     cos_sin = rope_cos_sin_cache(CTX_HI + 8, dims.rope_dim, dims.rope_theta, dev)
     bufs: dict = {}
     splits = args.splits or None
-    md = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs)
+    md = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs, max_items=args.items or None)
     q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
     o_buf = torch.empty_like(q_buf)
     outs = [None] * layers
 
     def step():
-        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs)
+        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs,
+                                  max_items=args.items or None)
         for l in range(layers):
             outs[l] = decode_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin,
                                    q_buf=q_buf, o_buf=o_buf)

@@ -803,7 +803,11 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_bf16(128, kCh, false, false);
       const uint32_t idesc_o = umma_idesc_bf16(128, kD, false, true);
-      const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
+      // shared-memory descriptors built once; a K step or buffer moves the
+      // start-address field (bits 0-13, address / 16) by offset / 16
+      const uint64_t dq = umma_desc_sw128(smem_u32(smem + kQOff), 16, 1024);
+      const uint64_t dk = umma_desc_sw128(smem_u32(smem + kKOff), 16, 1024);
+      const uint64_t dv = umma_desc_sw128(smem_u32(smem + kKOff), kKRegion, 1024);
       bool ok = mbar_wait(q_full, 0);
       // Q arrived through cp.async (generic proxy); the MMAs read it through
       // the async proxy
@@ -814,10 +818,9 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
         for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t qa = q_base + t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32;
-            const uint32_t ka = k_base + kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32;
-            umma_ss(tmem + s_col(t, sb), umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(ka, 16, 1024), idesc_s,
-                    kk > 0 ? 1u : 0u);
+            const uint32_t qo = (t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32) >> 4;
+            const uint32_t ko = (kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32) >> 4;
+            umma_ss(tmem + s_col(t, sb), dq + qo, dk + ko, idesc_s, kk > 0 ? 1u : 0u);
           }
         }
         umma_commit(s_full + sb);
@@ -827,38 +830,32 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
         tc_fence_after();
         for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
-          for (int kk = 0; kk < kCh / 16; ++kk) {
-            const uint32_t vb = k_base + kb * kKBuf + kk * 2048;
-            umma_ts(tmem + t * 128, tmem + s_col(t, sb) + kk * 8, umma_desc_sw128(vb, kKRegion, 1024), idesc_o,
+          for (int kk = 0; kk < kCh / 16; ++kk)
+            umma_ts(tmem + t * 128, tmem + s_col(t, sb) + kk * 8, dv + ((kb * kKBuf + kk * 2048) >> 4), idesc_o,
                     (i > 0 || kk > 0) ? 1u : 0u);
-          }
         }
         umma_commit(k_empty + kb);
         umma_commit(pv_done + sb);
       };
-      // Issue S(ns) as soon as its K tile is ready (its TMEM S/P buffer was
-      // last used by chunk ns - 2, whose P.V must already be issued) and
-      // P.V(np) as soon as softmax has written P(np); neither waits for the
-      // other.  Bounded: an error after kWaitLimitNs without progress.
-      int ns = 0, np = 0;
-      uint64_t t_last = global_ns();
-      while (ok && np < n) {
-        bool progressed = false;
-        if (ns < n && ns <= np + 1 && mbar_test(k_full + ns % kKBufs, (ns / kKBufs) & 1)) {
-          issue_s(ns);
-          ++ns;
-          progressed = true;
+      // Issue order S(0), then per chunk S(i + 1) -- as soon as its K tile is
+      // ready, so softmax finds the next S waiting -- and P.V(i) once softmax
+      // has written P(i).  S(i + 1) reuses the TMEM buffer of chunk i - 1,
+      // whose P.V is already issued.  The waits suspend the thread (no
+      // polling that would take issue slots from the softmax warps) and are
+      // bounded: an error after kWaitLimitNs.
+      if (ok && n > 0) {
+        ok = mbar_wait(k_full, 0);
+        if (ok) issue_s(0);
+      }
+      for (int i = 0; ok && i < n; ++i) {
+        if (i + 1 < n) {
+          ok = mbar_wait(k_full + (i + 1) % kKBufs, ((i + 1) / kKBufs) & 1);
+          if (!ok) break;
+          issue_s(i + 1);
         }
-        if (np < ns && mbar_test(p_full + (np & 1), (np >> 1) & 1)) {
-          issue_pv(np);
-          ++np;
-          progressed = true;
-        }
-        if (progressed) {
-          t_last = global_ns();
-        } else {
-          if (global_ns() - t_last > kWaitLimitNs) ok = false;
-        }
+        ok = mbar_wait(p_full + (i & 1), (i >> 1) & 1);
+        if (!ok) break;
+        issue_pv(i);
       }
       if (!ok) report(err, misc + 1, 4);
     }

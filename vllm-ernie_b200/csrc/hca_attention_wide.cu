@@ -385,7 +385,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_bf16(128, kCh, false, false);   // S: M128 N64, K-major
       const uint32_t idesc_o = umma_idesc_bf16(128, kHalf, false, true);  // O: M128 N256, V MN-major
-      const uint32_t q_base = smem_u32(smem + kQOff), k_base = smem_u32(smem + kKOff);
+      // descriptors built once; offsets move the start-address field (/ 16)
+      const uint64_t dq = umma_desc_sw128(smem_u32(smem + kQOff), 16, 1024);
+      const uint64_t dk = umma_desc_sw128(smem_u32(smem + kKOff), 16, 1024);
+      const uint64_t dv = umma_desc_sw128(smem_u32(smem + kKOff), kKRegion, 1024);
       bool ok = mbar_wait(q_full, 0);
       fence_proxy_async_smem();
       auto issue_s = [&](int i) {
@@ -393,10 +396,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kHalf / 16; ++kk) {
-          const uint32_t qa = q_base + (kk >> 2) * kQRegion + (kk & 3) * 32;
-          const uint32_t ka = k_base + kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32;
-          umma_ss(tmem + s_col(sb), umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(ka, 16, 1024), idesc_s,
-                  kk > 0 ? 1u : 0u);
+          const uint32_t qo = ((kk >> 2) * kQRegion + (kk & 3) * 32) >> 4;
+          const uint32_t ko = (kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32) >> 4;
+          umma_ss(tmem + s_col(sb), dq + qo, dk + ko, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(s_full + sb);
       };
@@ -404,33 +406,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
         const int kb = i % kKBufs, sb = i & 1;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kCh / 16; ++kk) {
-          const uint32_t vb = k_base + kb * kKBuf + kk * 2048;
-          umma_ts(tmem, tmem + s_col(sb) + kk * 8, umma_desc_sw128(vb, kKRegion, 1024), idesc_o,
+        for (int kk = 0; kk < kCh / 16; ++kk)
+          umma_ts(tmem, tmem + s_col(sb) + kk * 8, dv + ((kb * kKBuf + kk * 2048) >> 4), idesc_o,
                   (i > 0 || kk > 0) ? 1u : 0u);
-        }
         umma_commit(k_empty + kb);
         umma_commit(pv_done + sb);
       };
-      int ns = 0, np = 0;
-      uint64_t t_last = global_ns();
-      while (ok && np < n) {
-        bool progressed = false;
-        if (ns < n && ns <= np + 1 && mbar_test(k_full + ns % kKBufs, (ns / kKBufs) & 1)) {
-          issue_s(ns);
-          ++ns;
-          progressed = true;
+      // S(0), then per chunk S(i + 1) and P.V(i); suspending, bounded waits
+      if (ok && n > 0) {
+        ok = mbar_wait(k_full, 0);
+        if (ok) issue_s(0);
+      }
+      for (int i = 0; ok && i < n; ++i) {
+        if (i + 1 < n) {
+          ok = mbar_wait(k_full + (i + 1) % kKBufs, ((i + 1) / kKBufs) & 1);
+          if (!ok) break;
+          issue_s(i + 1);
         }
-        if (np < ns && mbar_test(p_full + (np & 1), (np >> 1) & 1)) {
-          issue_pv(np);
-          ++np;
-          progressed = true;
-        }
-        if (progressed) {
-          t_last = global_ns();
-        } else if (global_ns() - t_last > kWaitLimitNs) {
-          ok = false;
-        }
+        ok = mbar_wait(p_full + (i & 1), (i >> 1) & 1);
+        if (!ok) break;
+        issue_pv(i);
       }
       if (!ok) report(err, misc + 1, 4);
     }

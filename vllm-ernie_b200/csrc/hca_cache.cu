@@ -314,7 +314,7 @@ __device__ __forceinline__ void compress_token(
     const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride, uint8_t* kv_cache, int kv_page_size,
     int64_t kv_page_stride, int rope_dim, int ratio, float* red, int64_t* row_off, float* part_flat) {
   constexpr int kGroups = kCompressThreads / D;
-  constexpr int kSub = 32;
+  constexpr int kSub = 16;  // states per batch of independent loads
   float(*part)[kGroups][D] = reinterpret_cast<float(*)[kGroups][D]>(part_flat);
   const int64_t p = positions[t], slot = kv_slot[t];
   const int req = t2r[t];
@@ -420,7 +420,6 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
     int rope_dim, int ratio, int64_t num_tokens) {
   pdl_wait_and_release();
   constexpr int kGroups = kCompressThreads / D;
-  constexpr int kSub = 32;  // tokens per batch of independent loads
   __shared__ float red[32];
   __shared__ int64_t row_off[512];
   __shared__ float part[3][kGroups][D];
@@ -461,14 +460,16 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
 //     tokens are consecutive positions of that request only, so no other CTA
 //     writes the states it pools.
 //   CTAs [num_reqs, ...): prep_rows<D>() query rows each (head RMSNorm +
-//     RoPE; padding heads written as zeros), 64 / (D / 32) consecutive rows
-//     per warp with all their loads issued first.
+//     RoPE; padding heads written as zeros), 16 / (D / 32) consecutive rows
+//     per warp with all their loads issued first.  Two CTAs per SM: the
+//     rows are spread over the SMs (the traffic of one SM, not the DRAM,
+//     bounds a CTA that streams many rows).
 // The arithmetic of every row is the one of qnorm_rope_kv_insert_kernel,
 // save_partial_states_kernel and compress_kernel, so the outputs are the
 // same bytes as those three launches.
 // ----------------------------------------------------------------------------
 template <int D>
-constexpr int prep_rows_per_warp() { return 64 / (D / 32); }  // 16 at D=128, 4 at D=512
+constexpr int prep_rows_per_warp() { return 16 / (D / 32); }  // 4 at D=128, 1 at D=512
 template <int D>
 constexpr int prep_rows() { return (kCompressThreads / 32) * prep_rows_per_warp<D>(); }
 
@@ -521,7 +522,7 @@ struct DecodePrepParams {
 };
 
 template <int D>
-__global__ void __launch_bounds__(kCompressThreads, 1) decode_prep_kernel(const DecodePrepParams p) {
+__global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const DecodePrepParams p) {
   pdl_wait_and_release();
   constexpr int E = WarpRow<D>::E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -544,24 +545,51 @@ __global__ void __launch_bounds__(kCompressThreads, 1) decode_prep_kernel(const 
   if (blockIdx.x >= p.num_reqs) {
     // ---------------------------------------------------------- query rows
     constexpr int kRpw = prep_rows_per_warp<D>();
-    const int64_t base = static_cast<int64_t>(blockIdx.x - p.num_reqs) * prep_rows<D>() + warp * kRpw;
-    const int64_t nrows = p.num_tokens * p.padded_heads;
+    // 32-bit row arithmetic (the host checks num_tokens * padded_heads < 2^31);
+    // one division per warp, then (token, head) stepped row by row
+    const int base = (static_cast<int>(blockIdx.x) - p.num_reqs) * prep_rows<D>() + warp * kRpw;
+    const int nrows = static_cast<int>(p.num_tokens) * p.padded_heads;
+    if (base >= nrows) return;
     WarpRow<D> rows[kRpw];
-    int64_t tok[kRpw];
-    int head[kRpw];
+    int tok[kRpw], head[kRpw];
+    {
+      int t = base / p.padded_heads, h = base - t * p.padded_heads;
 #pragma unroll
-    for (int b = 0; b < kRpw; ++b) {
-      const int64_t row = base + b;
-      tok[b] = row / p.padded_heads;
-      head[b] = static_cast<int>(row - tok[b] * p.padded_heads);
-      if (row < nrows && head[b] < p.num_heads) rows[b].load_bf16(p.q + tok[b] * p.q_st + head[b] * p.q_sh, lane);
+      for (int b = 0; b < kRpw; ++b) {
+        tok[b] = t;
+        head[b] = h;
+        if (++h == p.padded_heads) {
+          h = 0;
+          ++t;
+        }
+      }
     }
+#pragma unroll
+    for (int b = 0; b < kRpw; ++b)
+      if (base + b < nrows && head[b] < p.num_heads)
+        rows[b].load_bf16(p.q + tok[b] * p.q_st + head[b] * p.q_sh, lane);
+    // cos / sin of the first and last token of these rows, loaded before any
+    // store (a store may alias them, so later loads could not be hoisted);
+    // with padded_heads >= kRpw no other token occurs
+    const int tok_a = tok[0], tok_b = (base + kRpw - 1 < nrows ? base + kRpw - 1 : nrows - 1) / p.padded_heads;
+    float ca[E / 2], sa[E / 2], cb[E / 2], sb[E / 2];
+    load_cs(p.positions[tok_a], ca, sa);
+    load_cs(p.positions[tok_b], cb, sb);
 #pragma unroll
     for (int b = 0; b < kRpw; ++b) {
       if (base + b >= nrows) continue;
       if (head[b] < p.num_heads) {
         float pc[E / 2], ps[E / 2];
-        load_cs(p.positions[tok[b]], pc, ps);
+        if (tok[b] == tok_a || tok[b] == tok_b) {
+          const bool first = tok[b] == tok_a;
+#pragma unroll
+          for (int i = 0; i < E / 2; ++i) {
+            pc[i] = first ? ca[i] : cb[i];
+            ps[i] = first ? sa[i] : sb[i];
+          }
+        } else {
+          load_cs(p.positions[tok[b]], pc, ps);
+        }
         WarpRow<D>& row = rows[b];
         float ss = 0.0f;
 #pragma unroll
@@ -604,14 +632,18 @@ __global__ void __launch_bounds__(kCompressThreads, 1) decode_prep_kernel(const 
   }
   // compressor states: state[slot] = [kv, score + ape[pos % ratio]]
   for (int i = threadIdx.x; i < (t1 - t0) * D; i += kCompressThreads) {
-    const int64_t t = t0 + i / D;
+    const int t = t0 + i / D;
     const int c = i % D;
-    const int64_t slot = p.state_slot[t];
-    if (slot < 0) continue;
-    const int64_t blk = slot / p.state_page;
+    const int64_t slot64 = p.state_slot[t];
+    if (slot64 < 0) continue;
+    // 32-bit: a state row is >= 1 KB, so any state cache that fits in device
+    // memory has fewer than 2^31 slots; positions are below the model length
+    const int slot = static_cast<int>(slot64);
+    const int blk = slot / p.state_page;
     float* sb = p.state + blk * p.s_blk + (slot - blk * p.state_page) * p.s_tok;
+    const int pm = static_cast<int>(p.positions[t]) % p.ratio;
     sb[c] = p.st_kv[t * p.st_kv_stride + c];
-    sb[p.state_width + c] = p.st_score[t * p.st_score_stride + c] + p.ape[(p.positions[t] % p.ratio) * p.ape_stride + c];
+    sb[p.state_width + c] = p.st_score[t * p.st_score_stride + c] + p.ape[pm * p.ape_stride + c];
   }
   __syncthreads();  // the states are visible to the whole CTA
   for (int j = 0; j < t1 - t0; ++j) {
@@ -775,6 +807,7 @@ extern "C" int hca_decode_prep(
                 compress_ratio > 0 && compress_ratio <= 512);
   if (!geom_ok(head_dim, rope_dim)) return HCA_E_UNSUPPORTED;
   if (num_tokens == 0) return HCA_OK;
+  HCA_CHECK_ARG(static_cast<int64_t>(num_tokens) * padded_heads < (int64_t(1) << 31));
   HCA_CHECK_ARG(q_out && q && kv && swa_cache && swa_slot_mapping && positions && cos_sin && state_kv &&
                 state_score && ape && state && state_slot_mapping && state_block_table && norm_weight && comp_cache &&
                 comp_slot_mapping && query_start_loc && token_to_req && num_reqs > 0);

@@ -52,11 +52,13 @@ def choose_num_splits(num_groups: int, sm_count: int = SM_COUNT_B200) -> int:
 
 
 def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: int | None = None,
-                          buffers: dict | None = None, sm_count: int = SM_COUNT_B200) -> DecodeMetadata:
+                          buffers: dict | None = None, sm_count: int = SM_COUNT_B200,
+                          max_items: int | None = None) -> DecodeMetadata:
     """All per-step index tables, on the device, through the library's
     builders (bit-exact with the reference's).  ``num_splits=None`` builds the
-    balanced work list for one wave of ``sm_count`` CTAs; an integer forces
-    that many uniform splits per group."""
+    balanced work list for one wave of ``sm_count`` CTAs (``max_items``
+    overrides the item count); an integer forces that many uniform splits per
+    group."""
     d = batch.dims
     dev = batch.device
     T = batch.num_tokens
@@ -104,7 +106,7 @@ def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: i
         return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
                               cidx, clens, gs, max_g, num_splits)
     # one wave: a CTA per SM, or a CTA pair per two SMs at head_dim 512
-    items = max(sm_count if d.head_dim == 128 else sm_count // 2, ngroups)
+    items = max(max_items or (sm_count if d.head_dim == 128 else sm_count // 2), ngroups)
     sched = ops.decode_schedule(gs, T, swa_lens, clens, items, out=buf.get("schedule"))
     buf["schedule"] = sched
     return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
