@@ -1180,22 +1180,29 @@ struct VhaOut {
 };
 
 __global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const AttnParams P, const VhaOut V) {
-  pdl_wait_and_release();
+  // Up to the dependency wait this kernel reads only weights (the mix), the
+  // RoPE table and per-step metadata (positions, groups, work list), none of
+  // which a layer kernel writes, so it overlaps the attention still running
+  // on other SMs; the partials (and every store) come after the wait.
+  pdl_release();
   constexpr int D = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = D + 8;
   constexpr int kMaxSplits = 16;
   __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
   __shared__ __align__(16) __nv_bfloat16 o_s[kMaxH * kOStride];
   __shared__ float cs_s[64];
   __shared__ float amax_s[2][kMaxH];
+  __shared__ float w_s[kMaxH][kMaxSplits];  // split weights 2^(m_split - m)
+  __shared__ float inv_s[kMaxH];            // 1 / (sum l + sink)
   const int H = P.num_heads;
   const int hpg = H / V.n_groups;
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (t >= V.num_tokens) {
+    pdl_wait();
     for (int h = threadIdx.x; h < H; h += blockDim.x) V.scale[static_cast<int64_t>(h) * V.aligned_t + t] = 0;
     return;
   }
-  // start the loads the merge does not wait for: the mix and this token's cos / sin
+  // the mix and this token's cos / sin
   for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
     const int r = i / (H / 8), c8 = i % (H / 8);
     *reinterpret_cast<uint4*>(&mix_s[r * kMixStride + c8 * 8]) =
@@ -1244,50 +1251,72 @@ __global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const Att
   }
   // a group larger than the workspace rows was skipped by the attention launch
   if ((t - t0 + 1) * H > P.max_rows || S > kMaxSplits) S = 0;
-  // ---- merge: thread (head h, 16-dim segment) ----
+  pdl_wait();  // the attention launch has written the partials
+  // ---- merge ----
+  // The first two splits' O rows are requested first; while they are in
+  // flight, thread (head, split) pairs turn every split's (m, l) into its
+  // weight (one max and one sum over the 16 lanes of a head); then thread
+  // (head h, 16-dim segment) adds the splits two at a time.
   {
     const int h = threadIdx.x >> 3, seg = threadIdx.x & 7;
-    if (h < H) {
-      const int64_t row = static_cast<int64_t>(t - t0) * H + h;
-      float w[kMaxSplits];
-      float mx = -INFINITY, lw = 0.0f;
+    const int64_t row0 = static_cast<int64_t>(first) * P.max_rows + static_cast<int64_t>(t - t0) * H;
+    const int64_t o_step = static_cast<int64_t>(P.max_rows) * D / 4;  // float4s between splits
+    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
+    float4 v[2][4];
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplits; ++sp) {
-        w[sp] = 0.0f;
-        if (sp < S) {
-          const int64_t i = ((first + sp) * static_cast<int64_t>(P.max_rows) + row) * 2;
-          const float m = __ldcg(P.ws_ml + i), l = __ldcg(P.ws_ml + i + 1);
-          w[sp] = l > 0.0f ? m : -INFINITY;  // the split's max for now; its weight below
-          if (l > 0.0f) mx = fmaxf(mx, m);
-        }
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        v[k][q] = (h < H && k < S) ? __ldcg(op + k * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = threadIdx.x; i < H * kMaxSplits; i += blockDim.x) {
+      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
+      float m = -INFINITY, l = 0.0f;
+      if (sp < S) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(P.ws_ml + (row0 + static_cast<int64_t>(sp) * P.max_rows + hh) * 2));
+        m = ml.x;
+        l = ml.y;
       }
+      float mx = l > 0.0f ? m : -INFINITY;
+#pragma unroll
+      for (int o = kMaxSplits / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float base = mx == -INFINITY ? 0.0f : mx;
+      // an empty split's row was never written: weight 0
+      const float wt = l > 0.0f ? exp2f(m - base) : 0.0f;
+      float lw = l > 0.0f ? l * wt : 0.0f;
+#pragma unroll
+      for (int o = kMaxSplits / 2; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+      w_s[hh][sp] = wt;
+      if (sp == 0) {
+        const float sink2 = P.sink ? P.sink[hh] * kLog2e : -INFINITY;
+        inv_s[hh] = lw > 0.0f ? 1.0f / (lw + exp2f(sink2 - base)) : 0.0f;
+      }
+    }
+    __syncthreads();
+    if (h < H) {
       float acc[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+      for (int sp = 0; sp < S; sp += 2) {
+        if (sp > 0) {
 #pragma unroll
-      for (int sp = 0; sp < kMaxSplits; ++sp) {
-        if (sp < S) {
-          const int64_t slot = (first + sp) * static_cast<int64_t>(P.max_rows) + row;
-          const float l = __ldcg(P.ws_ml + slot * 2 + 1);
-          const float wt = w[sp] == -INFINITY ? 0.0f : exp2f(w[sp] - base);
-          lw += l > 0.0f ? l * wt : 0.0f;
-          const float4* src = reinterpret_cast<const float4*>(P.ws_o + slot * D + seg * 16);
-          float4 v[4];
+          for (int k = 0; k < 2; ++k)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[q] = __ldcg(src + q);
-          // an empty split's row was never written: weight 0, value unused
+            for (int q = 0; q < 4; ++q)
+              v[k][q] = sp + k < S ? __ldcg(op + (sp + k) * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float wt = sp + k < S ? w_s[h][sp + k] : 0.0f;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            acc[4 * q] += wt != 0.0f ? wt * v[q].x : 0.0f;
-            acc[4 * q + 1] += wt != 0.0f ? wt * v[q].y : 0.0f;
-            acc[4 * q + 2] += wt != 0.0f ? wt * v[q].z : 0.0f;
-            acc[4 * q + 3] += wt != 0.0f ? wt * v[q].w : 0.0f;
+            acc[4 * q] += wt != 0.0f ? wt * v[k][q].x : 0.0f;
+            acc[4 * q + 1] += wt != 0.0f ? wt * v[k][q].y : 0.0f;
+            acc[4 * q + 2] += wt != 0.0f ? wt * v[k][q].z : 0.0f;
+            acc[4 * q + 3] += wt != 0.0f ? wt * v[k][q].w : 0.0f;
           }
         }
       }
-      const float sink2 = P.sink ? P.sink[h] * kLog2e : -INFINITY;
-      const float inv = lw > 0.0f ? 1.0f / (lw + exp2f(sink2 - base)) : 0.0f;
+      const float inv = inv_s[h];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         uint4 pk;

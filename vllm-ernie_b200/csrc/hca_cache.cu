@@ -305,38 +305,63 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
 // ----------------------------------------------------------------------------
 constexpr int kCompressThreads = 512;
 
-// Pool, normalise, quantise and store the block completed by token t (the
-// whole CTA; returns with every thread past its last barrier).
+// Per-thread values of a block's compression that depend only on step
+// metadata and weights (position, destination slot, norm weight, RoPE).
+struct CompressCtx {
+  int64_t p, slot;
+  float nw, co, si;
+};
+
+// First part of the compression of the block completed by token t: the
+// metadata loads, and the state-row offsets of the `ratio` pooled positions
+// into row_off (shared memory; the caller synchronises the CTA before
+// compress_pool reads them).  Reads no state and no layer activation.
 template <int D>
-__device__ __forceinline__ void compress_token(
-    int64_t t, const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
-    const int64_t* positions, const int64_t* kv_slot, const int32_t* bt, int64_t bt_stride, int block_size,
-    const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride, uint8_t* kv_cache, int kv_page_size,
-    int64_t kv_page_stride, int rope_dim, int ratio, float* red, int64_t* row_off, float* part_flat) {
-  constexpr int kGroups = kCompressThreads / D;
-  constexpr int kSub = 16;  // states per batch of independent loads
-  float(*part)[kGroups][D] = reinterpret_cast<float(*)[kGroups][D]>(part_flat);
-  const int64_t p = positions[t], slot = kv_slot[t];
+__device__ __forceinline__ CompressCtx compress_begin(int64_t t, int64_t s_blk, int64_t s_tok, const int32_t* t2r,
+                                                      const int64_t* positions, const int64_t* kv_slot,
+                                                      const int32_t* bt, int64_t bt_stride, int block_size,
+                                                      const float* norm_w, const float* cos_sin, int64_t cs_stride,
+                                                      int rope_dim, int ratio, int64_t* row_off) {
+  CompressCtx x;
+  x.p = positions[t];
+  x.slot = kv_slot[t];
   const int req = t2r[t];
-  const int c = threadIdx.x % D, grp = threadIdx.x / D;
+  const int c = threadIdx.x % D;
   // loads of the epilogue, issued now so they land during the pooling
-  const float nw = norm_w[c];
-  const RowGeom g = row_geom(D, rope_dim);
-  const int nope = g.nope;
-  float co = 1.0f, si = 0.0f;
+  x.nw = norm_w[c];
+  const int nope = D - rope_dim;
+  x.co = 1.0f;
+  x.si = 0.0f;
   if (c >= nope) {
-    const float* cs = cos_sin + (p / ratio) * ratio * cs_stride;
+    const float* cs = cos_sin + (x.p / ratio) * ratio * cs_stride;
     const int pr = (c - nope) >> 1;
-    co = cs[pr];
-    si = cs[rope_dim / 2 + pr];
+    x.co = cs[pr];
+    x.si = cs[rope_dim / 2 + pr];
   }
   // Row offsets of the `ratio` states (all positions are >= 0 at a boundary).
   for (int i = threadIdx.x; i < ratio; i += kCompressThreads) {
-    const int64_t pos = p - ratio + 1 + i;
+    const int64_t pos = x.p - ratio + 1 + i;
     const int64_t blk = bt[req * bt_stride + pos / block_size];
     row_off[i] = blk * s_blk + (pos % block_size) * s_tok;
   }
-  __syncthreads();
+  return x;
+}
+
+// Second part: pool the states, normalise, quantise and store the row (the
+// whole CTA; returns with every thread past its last barrier).
+template <int D>
+__device__ __forceinline__ void compress_pool(const CompressCtx& x, const float* state, int state_width, float eps,
+                                              uint8_t* kv_cache, int kv_page_size, int64_t kv_page_stride,
+                                              int rope_dim, int ratio, float* red, const int64_t* row_off,
+                                              float* part_flat) {
+  constexpr int kGroups = kCompressThreads / D;
+  constexpr int kSub = 16;  // states per batch of independent loads
+  float(*part)[kGroups][D] = reinterpret_cast<float(*)[kGroups][D]>(part_flat);
+  const int c = threadIdx.x % D, grp = threadIdx.x / D;
+  const RowGeom g = row_geom(D, rope_dim);
+  const int nope = g.nope;
+  const float nw = x.nw, co = x.co, si = x.si;
+  const int64_t slot = x.slot;
   const int per = (ratio + kGroups - 1) / kGroups;
   const int i0 = grp * per, i1 = min(ratio, i0 + per);
   float m = -INFINITY, den = 0.0f, acc = 0.0f;
@@ -410,6 +435,20 @@ __device__ __forceinline__ void compress_token(
   if (c == 0) dst.scale[nope / kQuantBlock] = 0;
 }
 
+
+// The whole compression of the block completed by token t.
+template <int D>
+__device__ __forceinline__ void compress_token(
+    int64_t t, const float* state, int64_t s_blk, int64_t s_tok, int state_width, const int32_t* t2r,
+    const int64_t* positions, const int64_t* kv_slot, const int32_t* bt, int64_t bt_stride, int block_size,
+    const float* norm_w, float eps, const float* cos_sin, int64_t cs_stride, uint8_t* kv_cache, int kv_page_size,
+    int64_t kv_page_stride, int rope_dim, int ratio, float* red, int64_t* row_off, float* part_flat) {
+  const CompressCtx x = compress_begin<D>(t, s_blk, s_tok, t2r, positions, kv_slot, bt, bt_stride, block_size, norm_w,
+                                          cos_sin, cs_stride, rope_dim, ratio, row_off);
+  __syncthreads();
+  compress_pool<D>(x, state, state_width, eps, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red, row_off,
+                   part_flat);
+}
 
 template <int D>
 __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
@@ -523,7 +562,10 @@ struct DecodePrepParams {
 
 template <int D>
 __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const DecodePrepParams p) {
-  pdl_wait_and_release();
+  // Reads before pdl_wait() touch only step metadata (positions, slot maps,
+  // block tables), weights and the RoPE table; q, kv and the compressor
+  // inputs (outputs of the layer's projections) and every store come after.
+  pdl_release();
   constexpr int E = WarpRow<D>::E;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   constexpr int kWarps = kCompressThreads / 32;
@@ -549,7 +591,10 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
     // one division per warp, then (token, head) stepped row by row
     const int base = (static_cast<int>(blockIdx.x) - p.num_reqs) * prep_rows<D>() + warp * kRpw;
     const int nrows = static_cast<int>(p.num_tokens) * p.padded_heads;
-    if (base >= nrows) return;
+    if (base >= nrows) {
+      pdl_wait();
+      return;
+    }
     WarpRow<D> rows[kRpw];
     int tok[kRpw], head[kRpw];
     {
@@ -564,10 +609,6 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
         }
       }
     }
-#pragma unroll
-    for (int b = 0; b < kRpw; ++b)
-      if (base + b < nrows && head[b] < p.num_heads)
-        rows[b].load_bf16(p.q + tok[b] * p.q_st + head[b] * p.q_sh, lane);
     // cos / sin of the first and last token of these rows, loaded before any
     // store (a store may alias them, so later loads could not be hoisted);
     // with padded_heads >= kRpw no other token occurs
@@ -575,6 +616,11 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
     float ca[E / 2], sa[E / 2], cb[E / 2], sb[E / 2];
     load_cs(p.positions[tok_a], ca, sa);
     load_cs(p.positions[tok_b], cb, sb);
+    pdl_wait();  // q is an output of the layer's projection
+#pragma unroll
+    for (int b = 0; b < kRpw; ++b)
+      if (base + b < nrows && head[b] < p.num_heads)
+        rows[b].load_bf16(p.q + tok[b] * p.q_st + head[b] * p.q_sh, lane);
 #pragma unroll
     for (int b = 0; b < kRpw; ++b) {
       if (base + b >= nrows) continue;
@@ -616,6 +662,19 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
   const int r = blockIdx.x;
   const int t0 = p.qsl[r], t1 = p.qsl[r + 1];
   const RowGeom g = row_geom(D, p.rope_dim);
+  // The first token that completes a block: its metadata loads and state-row
+  // offsets are done before the wait (the request's CTA is resident early).
+  int jb = -1;
+  for (int j = 0; j < t1 - t0; ++j)
+    if (p.state_slot[t0 + j] >= 0 && (p.positions[t0 + j] + 1) % p.ratio == 0) {
+      jb = j;
+      break;
+    }
+  CompressCtx cx{};
+  if (jb >= 0)
+    cx = compress_begin<D>(t0 + jb, p.s_blk, p.s_tok, p.t2r, p.positions, p.comp_slot, p.state_bt, p.state_bt_stride,
+                           p.state_page, p.norm_w, p.cos_sin, p.cs_stride, p.rope_dim, p.ratio, row_off);
+  pdl_wait();  // kv and the compressor inputs are outputs of the layer's projections
   // KV rows: one warp per token
   for (int j = warp; j < t1 - t0; j += kWarps) {
     const int64_t t = t0 + j;
@@ -645,8 +704,15 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
     sb[c] = p.st_kv[t * p.st_kv_stride + c];
     sb[p.state_width + c] = p.st_score[t * p.st_score_stride + c] + p.ape[pm * p.ape_stride + c];
   }
-  __syncthreads();  // the states are visible to the whole CTA
-  for (int j = 0; j < t1 - t0; ++j) {
+  __syncthreads();  // the states (and row_off) are visible to the whole CTA
+  if (jb >= 0) {
+    compress_pool<D>(cx, p.state, p.state_width, p.eps, p.comp_cache, p.comp_page, p.comp_pstride, p.rope_dim, p.ratio,
+                     red, row_off, &part[0][0][0]);
+    __syncthreads();
+  }
+  // any further block end among the request's tokens (more than `ratio`
+  // tokens per request): metadata and pooling in sequence
+  for (int j = jb + 1; jb >= 0 && j < t1 - t0; ++j) {
     const int64_t t = t0 + j;
     if (p.state_slot[t] < 0 || (p.positions[t] + 1) % p.ratio != 0) continue;  // uniform
     compress_token<D>(t, p.state, p.s_blk, p.s_tok, p.state_width, p.t2r, p.positions, p.comp_slot, p.state_bt,
