@@ -347,15 +347,53 @@ __device__ __forceinline__ CompressCtx compress_begin(int64_t t, int64_t s_blk, 
   return x;
 }
 
-// Second part: pool the states, normalise, quantise and store the row (the
-// whole CTA; returns with every thread past its last barrier).
+constexpr int kPoolBatch = 16;  // pooled states per batch of independent loads
+
+// Batch 0 of this thread's pooled states (channel c of its group's first
+// kPoolBatch positions) into pre[j * kCompressThreads + tid] (score) and
+// pre[(kPoolBatch + j) * kCompressThreads + tid] (kv); row_off must be
+// visible to the CTA.  Each thread reads back only its own entries.
 template <int D>
-__device__ __forceinline__ void compress_pool(const CompressCtx& x, const float* state, int state_width, float eps,
-                                              uint8_t* kv_cache, int kv_page_size, int64_t kv_page_stride,
-                                              int rope_dim, int ratio, float* red, const int64_t* row_off,
-                                              float* part_flat) {
+__device__ __forceinline__ void compress_stage_batch0(const float* state, int state_width, int ratio,
+                                                      const int64_t* row_off, float* pre) {
   constexpr int kGroups = kCompressThreads / D;
-  constexpr int kSub = 16;  // states per batch of independent loads
+  const int c = threadIdx.x % D, grp = threadIdx.x / D;
+  const int per = (ratio + kGroups - 1) / kGroups;
+  const int i0 = grp * per, i1 = min(ratio, i0 + per);
+  float sc[kPoolBatch], kv[kPoolBatch];
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) {
+    const int i = i0 + j;
+    sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
+    kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) {
+    pre[j * kCompressThreads + threadIdx.x] = sc[j];
+    pre[(kPoolBatch + j) * kCompressThreads + threadIdx.x] = kv[j];
+  }
+}
+
+// Pooled positions (counted back from the block's last) that batch 0 of
+// every group leaves out: states saved in the current launch may lie among
+// them without changing that batch.
+template <int D>
+__device__ __forceinline__ int compress_batch0_margin(int ratio) {
+  constexpr int kGroups = kCompressThreads / D;
+  const int per = (ratio + kGroups - 1) / kGroups;
+  return ratio - (kGroups - 1) * per - kPoolBatch;
+}
+
+// Second part: pool the states, normalise, quantise and store the row (the
+// whole CTA; returns with every thread past its last barrier).  `pre`: batch
+// 0 staged by compress_stage_batch0, or nullptr to load it here.
+template <int D>
+__device__ __forceinline__ void compress_pool(const CompressCtx& x, const float* pre, const float* state,
+                                              int state_width, float eps, uint8_t* kv_cache, int kv_page_size,
+                                              int64_t kv_page_stride, int rope_dim, int ratio, float* red,
+                                              const int64_t* row_off, float* part_flat) {
+  constexpr int kGroups = kCompressThreads / D;
+  constexpr int kSub = kPoolBatch;
   float(*part)[kGroups][D] = reinterpret_cast<float(*)[kGroups][D]>(part_flat);
   const int c = threadIdx.x % D, grp = threadIdx.x / D;
   const RowGeom g = row_geom(D, rope_dim);
@@ -367,13 +405,21 @@ __device__ __forceinline__ void compress_pool(const CompressCtx& x, const float*
   float m = -INFINITY, den = 0.0f, acc = 0.0f;
   for (int b0 = i0; b0 < i1; b0 += kSub) {
     float sc[kSub], kv[kSub];
+    if (b0 == i0 && pre) {
 #pragma unroll
-    for (int j = 0; j < kSub; ++j) {
-      const int i = b0 + j;
-      // coherent (L2) loads: the fused decode prep pools states that its
-      // own CTA saved earlier in the same launch
-      sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
-      kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
+      for (int j = 0; j < kSub; ++j) {
+        sc[j] = pre[j * kCompressThreads + threadIdx.x];
+        kv[j] = pre[(kSub + j) * kCompressThreads + threadIdx.x];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSub; ++j) {
+        const int i = b0 + j;
+        // coherent (L2) loads: the fused decode prep pools states that its
+        // own CTA saved earlier in the same launch
+        sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
+        kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
+      }
     }
     float mb = m;
 #pragma unroll
@@ -446,8 +492,8 @@ __device__ __forceinline__ void compress_token(
   const CompressCtx x = compress_begin<D>(t, s_blk, s_tok, t2r, positions, kv_slot, bt, bt_stride, block_size, norm_w,
                                           cos_sin, cs_stride, rope_dim, ratio, row_off);
   __syncthreads();
-  compress_pool<D>(x, state, state_width, eps, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red, row_off,
-                   part_flat);
+  compress_pool<D>(x, nullptr, state, state_width, eps, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red,
+                   row_off, part_flat);
 }
 
 template <int D>
@@ -507,6 +553,8 @@ __global__ void __launch_bounds__(kCompressThreads) compress_kernel(
 // save_partial_states_kernel and compress_kernel, so the outputs are the
 // same bytes as those three launches.
 // ----------------------------------------------------------------------------
+constexpr int kPrepDynSmem = 2 * kPoolBatch * kCompressThreads * 4;  // 64 KB
+
 template <int D>
 constexpr int prep_rows_per_warp() { return 16 / (D / 32); }  // 4 at D=128, 1 at D=512
 template <int D>
@@ -659,6 +707,7 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
   __shared__ float red[32];
   __shared__ int64_t row_off[512];
   __shared__ float part[3][kCompressThreads / D][D];
+  extern __shared__ float pre_s[];  // batch 0 of the pooled states: kPrepDynSmem bytes
   const int r = blockIdx.x;
   const int t0 = p.qsl[r], t1 = p.qsl[r + 1];
   const RowGeom g = row_geom(D, p.rope_dim);
@@ -671,9 +720,20 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
       break;
     }
   CompressCtx cx{};
-  if (jb >= 0)
+  bool staged = false;
+  if (jb >= 0) {
     cx = compress_begin<D>(t0 + jb, p.s_blk, p.s_tok, p.t2r, p.positions, p.comp_slot, p.state_bt, p.state_bt_stride,
                            p.state_page, p.norm_w, p.cos_sin, p.cs_stride, p.rope_dim, p.ratio, row_off);
+    __syncthreads();
+    // Batch 0 of every group holds only states of earlier steps when this
+    // launch's tokens up to the block end fall in the margin (uniform across
+    // the CTA): no kernel of this step writes those, so they are staged in
+    // shared memory before the wait too.
+    if (p.positions[t0 + jb] - p.positions[t0] < compress_batch0_margin<D>(p.ratio)) {
+      compress_stage_batch0<D>(p.state, p.state_width, p.ratio, row_off, pre_s);
+      staged = true;
+    }
+  }
   pdl_wait();  // kv and the compressor inputs are outputs of the layer's projections
   // KV rows: one warp per token
   for (int j = warp; j < t1 - t0; j += kWarps) {
@@ -706,8 +766,8 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
   }
   __syncthreads();  // the states (and row_off) are visible to the whole CTA
   if (jb >= 0) {
-    compress_pool<D>(cx, p.state, p.state_width, p.eps, p.comp_cache, p.comp_page, p.comp_pstride, p.rope_dim, p.ratio,
-                     red, row_off, &part[0][0][0]);
+    compress_pool<D>(cx, staged ? pre_s : nullptr, p.state, p.state_width, p.eps, p.comp_cache, p.comp_page,
+                     p.comp_pstride, p.rope_dim, p.ratio, red, row_off, &part[0][0][0]);
     __syncthreads();
   }
   // any further block end among the request's tokens (more than `ratio`
@@ -923,6 +983,13 @@ extern "C" int hca_decode_prep(
   p.num_tokens = num_tokens;
   const int rows_per_cta = head_dim == 128 ? prep_rows<128>() : prep_rows<512>();
   const int64_t q_ctas = (static_cast<int64_t>(num_tokens) * padded_heads + rows_per_cta - 1) / rows_per_cta;
-  return launch_pdl(head_dim == 128 ? decode_prep_kernel<128> : decode_prep_kernel<512>,
-                    dim3(static_cast<unsigned>(num_reqs + q_ctas)), dim3(kCompressThreads), 0, as_stream(stream), p);
+  auto kernel = head_dim == 128 ? decode_prep_kernel<128> : decode_prep_kernel<512>;
+  static bool smem_set[2] = {false, false};  // one attribute call per kernel and process
+  if (!smem_set[head_dim == 512]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepDynSmem) != cudaSuccess)
+      return HCA_E_CUDA;
+    smem_set[head_dim == 512] = true;
+  }
+  return launch_pdl(kernel, dim3(static_cast<unsigned>(num_reqs + q_ctas)), dim3(kCompressThreads), kPrepDynSmem,
+                    as_stream(stream), p);
 }
