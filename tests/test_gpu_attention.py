@@ -175,9 +175,10 @@ def test_prefill_matches_oracle():
     _prefill_case([(0, 300), (1000, 131), (128 * 7, 64)], 64, seed=22)
 
 
-@pytest.mark.parametrize("heads", [16, 64])
+@pytest.mark.parametrize("heads", [8, 16, 64])
 def test_prefill_long_prior_context(heads):
-    # tiles of 16 (H=16) or 4 (H=64) tokens over many chunks of compressed rows
+    # tiles of 32 (H=8, e.g. 16 heads under TP=2), 16 (H=16) or 4 (H=64)
+    # tokens over many chunks of compressed rows
     _prefill_case([(20000, 70), (128 * 40 - 3, 9), (5, 250)], heads, seed=31 + heads)
 
 
@@ -370,6 +371,7 @@ def test_decode_head_dim_512_long_context():
     _decode_case([130000, 65000], 3, 64, 8, seed=69, maxc=1024, head_dim=512)
 
 
-@pytest.mark.parametrize("heads", [16, 64])
+@pytest.mark.parametrize("heads", [4, 16, 64])
 def test_prefill_head_dim_512(heads):
+    # 4 heads: tiles of 31 tokens (the most a row's token mask holds)
     _prefill_case([(0, 130), (3000, 67), (128 * 9 - 1, 5)], heads, seed=71 + heads, head_dim=512)

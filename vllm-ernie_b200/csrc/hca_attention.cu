@@ -542,7 +542,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
   if (P.force_partials) single = false;
   Group G;
   if (!resolve_group<kPrefill>(P, gidx, G) || G.ntok * P.num_heads > kMaxRows ||
-      G.ntok * P.num_heads > P.max_rows) {
+      G.ntok * P.num_heads > P.max_rows || G.ntok > 31) {  // 31 token mask bits (bit 31: loaded)
     pdl_wait();
     return;
   }
@@ -1716,10 +1716,13 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
   HCA_CHECK_ARG(num_reqs >= 0 && num_tokens >= 0 && swa_page_size > 0 && window > 0 &&
                 compress_ratio > 0);
   const bool wide = head_dim == 512;
+  // head_dim 128 with up to 256 heads runs on the tcgen05 kernel (any head
+  // count); the mma.sync kernel is the fallback for the other shapes
+  const bool tc = head_dim == 128 && rope_dim == 64 && num_heads >= 1 && num_heads <= tcd::kMaxRows;
   const int group_tokens = num_heads > 0 ? (wide ? wide_tile_tokens(num_heads) : (kMaxWarps * 16) / num_heads) : 0;
   if (wide) {
     if (rope_dim != 64 || num_heads < 1 || num_heads > 128) return HCA_E_UNSUPPORTED;
-  } else if (group_tokens < 1 || !attn_shape_ok(num_heads, head_dim, rope_dim, group_tokens)) {
+  } else if (!tc && (group_tokens < 1 || !attn_shape_ok(num_heads, head_dim, rope_dim, group_tokens))) {
     return HCA_E_UNSUPPORTED;
   }
   if (num_reqs == 0 || num_tokens == 0) return HCA_OK;
@@ -1765,10 +1768,11 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
     const int num_tiles = num_tokens / group_tokens + num_reqs;
     return launch_wide_attention(P, true, num_tiles, 0, err, as_stream(stream));
   }
-  if (head_dim == 128 && rope_dim == 64 && num_heads <= tcd::kMaxRows) {
-    // tcgen05 path: tiles of up to 256 query rows (at most 32 tokens, one
-    // mask bit each), all of a tile's rows in one CTA
-    const int tc_tokens = min(32, tcd::kMaxRows / num_heads);
+  if (tc) {
+    // tcgen05 path: tiles of up to 256 query rows, at most 31 tokens (one
+    // mask bit each; bit 31 of a row's mask is its "loaded" flag), all of a
+    // tile's rows in one CTA
+    const int tc_tokens = min(31, tcd::kMaxRows / num_heads);
     P.group_tokens = tc_tokens;
     P.max_rows = tc_tokens * num_heads;
     HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(swa_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(comp_cache) % 16 == 0 &&

@@ -187,7 +187,7 @@ int launch_wide_attention(const AttnParams& P, bool prefill, int num_groups, int
                           cudaStream_t s);
 
 // Query tokens one pair handles at head count H (one M=128 tile of rows, at
-// most 32 tokens for the per-token masks).
-inline int wide_tile_tokens(int num_heads) { return num_heads > 0 ? (128 / num_heads < 32 ? 128 / num_heads : 32) : 0; }
+// most 31 tokens: a row's token mask keeps bit 31 for its "loaded" flag).
+inline int wide_tile_tokens(int num_heads) { return num_heads > 0 ? (128 / num_heads < 31 ? 128 / num_heads : 31) : 0; }
 
 }  // namespace hca

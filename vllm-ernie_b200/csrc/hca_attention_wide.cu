@@ -152,7 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
     c_end = static_cast<int>((static_cast<int64_t>(split + 1) * nch) / P.num_splits);
   }
   const int rows_q = G.ntok * H;  // <= 128: tiles hold at most 128 / H tokens
-  if (rows_q > 128 || G.ntok > 32) return;
+  if (rows_q > 128 || G.ntok > 31) return;  // 31 mask bits per row (bit 31: loaded)
   const int nact = active_quads(rows_q);
   const int n_u = G.n_win + G.n_comp;
   const int nchunks = (n_u + kCh - 1) / kCh;
