@@ -340,3 +340,43 @@ def test_decode_prep_matches_three_ops(ops, head_dim, heads, padded):
         assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
     # the launch did write: boundaries produced compressed rows, states moved
     assert not torch.equal(f[2], caches.comp) and not torch.equal(f[1], caches.state)
+
+
+def test_decode_prep_ragged_requests_match_three_ops(ops):
+    """Requests with 1, 2 or 3 query tokens in one batch (ragged
+    query_start_loc), block ends on their first / last / only token: the
+    fused launch still writes the bytes of the three separate ops."""
+    from vllm_ernie_b200.decode import build_decode_metadata
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dims = HCADims(heads=64, head_dim=128)
+    ctx = [0, 125, 126, 127, 253, 1022, 5000, 77, 383]
+    keep = [1, 3, 2, 1, 3, 2, 3, 1, 1]  # tokens kept per request
+    b = make_decode_batch(ctx, 3, dims, DEV, seed=17, max_model_len=1024 * 128)
+    caches = alloc_layer_caches(b, seed=18)
+    md = build_decode_metadata(b, 1024, num_splits=1)
+    sel = torch.tensor([r * 3 + j for r, k in enumerate(keep) for j in range(k)], device=DEV)
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(keep)]), dtype=torch.int32, device=DEV)
+    t2r = torch.tensor([r for r, k in enumerate(keep) for _ in range(k)], dtype=torch.int32, device=DEV)
+    pos, swa_slot, st_slot, c_slot = (x[sel].contiguous() for x in (b.positions, md.swa_slot, md.state_slot, md.comp_slot))
+    assert int(((pos + 1) % 128 == 0).sum()) >= 3
+    n = sel.numel()
+    g = torch.Generator(device=DEV).manual_seed(19)
+    q = torch.randn((n, 64, 128), generator=g, device=DEV).to(torch.bfloat16)
+    kv = torch.randn((n, 128), generator=g, device=DEV).to(torch.bfloat16)
+    ks = torch.randn((n, 256), generator=g, device=DEV)
+    ape = torch.randn((128, 128), generator=g, device=DEV) * 0.1
+    w = 1.0 + 0.05 * torch.randn(128, generator=g, device=DEV)
+    cs = rope_cos_sin_cache(1024 * 128 + 8, 64, dims.rope_theta, DEV)
+    a = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    f = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    qa = ops.fused_qnorm_rope_kv_insert(q, kv, a[0], swa_slot, pos, cs, 64, 1e-6, 64, 64)
+    ops.save_partial_states(ks[:, :128], ks[:, 128:], ape, pos, a[1], st_slot, 8, 128, 128)
+    ops.compress_norm_rope_store(a[1], n, t2r, pos, st_slot, b.state_bt, 8, 128, cs, a[2], c_slot, 2, 128, 64, 128,
+                                 w, 1e-6)
+    qf = ops.decode_prep(q, kv, ks, ape, pos, cs, f[0], swa_slot, 64, f[1], st_slot, b.state_bt, 8, f[2], c_slot, 2, w,
+                         qsl, t2r, len(keep), 64, 1e-6, 128, 64)
+    torch.cuda.synchronize()
+    assert torch.equal(qa.view(torch.int16), qf.view(torch.int16))
+    for x, y in zip(a, f):
+        assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))

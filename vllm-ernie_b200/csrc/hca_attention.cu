@@ -1268,14 +1268,23 @@ __global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const Att
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         v[k][q] = (h < H && k < S) ? __ldcg(op + k * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = threadIdx.x; i < H * kMaxSplits; i += blockDim.x) {
+    // H * kMaxSplits <= 2 * blockDim.x: both (m, l) loads of a thread are in
+    // flight together
+    float2 mlv[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
       const int hh = i / kMaxSplits, sp = i % kMaxSplits;
-      float m = -INFINITY, l = 0.0f;
-      if (sp < S) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(P.ws_ml + (row0 + static_cast<int64_t>(sp) * P.max_rows + hh) * 2));
-        m = ml.x;
-        l = ml.y;
-      }
+      mlv[k] = (i < H * kMaxSplits && sp < S)
+                   ? __ldcg(reinterpret_cast<const float2*>(P.ws_ml + (row0 + static_cast<int64_t>(sp) * P.max_rows + hh) * 2))
+                   : make_float2(-INFINITY, 0.0f);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (i >= H * kMaxSplits) break;  // uniform per warp: H * kMaxSplits is a multiple of 32
+      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
+      const float m = mlv[k].x, l = mlv[k].y;
       float mx = l > 0.0f ? m : -INFINITY;
 #pragma unroll
       for (int o = kMaxSplits / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
