@@ -412,6 +412,226 @@ __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnPa
 }
 
 // ============================================================================
+// Output path of a decode layer at head_dim 128: split-K merge, VHA mix
+// (I + V U^T over heads, mma.sync), inverse GPT-J RoPE at the query position
+// and the FP8 / UE8M0 quant of wo_a's input, one token per CTA
+// (hca_combine_vha_quant_kernel).
+// ============================================================================
+struct VhaOut {
+  uint8_t* out;          // [n_groups][tokens][hpg * D] e4m3
+  int32_t* scale;        // [n_groups * hpg][aligned tokens] UE8M0 exponent bytes
+  const __nv_bfloat16* mix;  // [H][H] bf16, I + V U^T
+  const int64_t* positions;
+  const float* cos_sin;
+  int64_t cs_stride;
+  int num_tokens, aligned_t, n_groups, num_groups;
+};
+
+namespace vt {
+constexpr int D = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = D + 8, kMaxSplits = 16;
+struct Smem {
+  __nv_bfloat16 mix[kMaxH * kMixStride];
+  __nv_bfloat16 o[kMaxH * kOStride];  // one token's merged rows, bf16
+  float cs[64];                       // the token's cos | sin
+  float amax[2][kMaxH];
+  float w[kMaxH][kMaxSplits];         // split weights 2^(m_split - m)
+  float inv[kMaxH];                   // 1 / (sum l + sink)
+};
+}  // namespace vt
+
+// The mix into shared memory (all threads; a barrier follows before use).
+__device__ __forceinline__ void vha_load_mix(const VhaOut& V, int H, vt::Smem& sm) {
+  for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
+    const int r = i / (H / 8), c8 = i % (H / 8);
+    *reinterpret_cast<uint4*>(&sm.mix[r * vt::kMixStride + c8 * 8]) =
+        *reinterpret_cast<const uint4*>(V.mix + static_cast<int64_t>(r) * H + c8 * 8);
+  }
+}
+
+// Merge token t's S split partials (workspace slots first .. first + S - 1 of
+// the group whose first token is t0) into normalised bf16 rows in sm.o.
+// Whole block; ends with a barrier.  Items (head, 16-dim segment) are spread
+// over the threads; per item the splits are added two at a time, the first
+// pair requested before the split weights are formed.
+__device__ __forceinline__ void vha_merge_token(const AttnParams& P, int t, int t0, int first, int S, vt::Smem& sm) {
+  using namespace vt;
+  const int H = P.num_heads;
+  const int lane = threadIdx.x & 31;
+  (void)lane;
+  const int64_t row0 = static_cast<int64_t>(first) * P.max_rows + static_cast<int64_t>(t - t0) * H;
+  const int64_t o_step = static_cast<int64_t>(P.max_rows) * D / 4;  // float4s between splits
+  const int nitems = H * 8;
+  // the first pair of splits of this thread's first item
+  float4 v[2][4];
+  {
+    const int it = threadIdx.x;
+    const int h = it >> 3, seg = it & 7;
+    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        v[k][q] = (it < nitems && k < S) ? __ldcg(op + k * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // split weights: thread (head, split) pairs, two per thread in flight;
+  // H * kMaxSplits is a multiple of 256, so validity is uniform per warp
+  for (int base = 0; base < H * kMaxSplits; base += 2 * blockDim.x) {
+    float2 mlv[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = base + k * blockDim.x + threadIdx.x;
+      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
+      mlv[k] = (i < H * kMaxSplits && sp < S)
+                   ? __ldcg(reinterpret_cast<const float2*>(P.ws_ml + (row0 + static_cast<int64_t>(sp) * P.max_rows + hh) * 2))
+                   : make_float2(-INFINITY, 0.0f);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = base + k * blockDim.x + threadIdx.x;
+      if (i >= H * kMaxSplits) break;
+      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
+      const float m = mlv[k].x, l = mlv[k].y;
+      float mx = l > 0.0f ? m : -INFINITY;
+#pragma unroll
+      for (int o = kMaxSplits / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float bse = mx == -INFINITY ? 0.0f : mx;
+      // an empty split's row was never written: weight 0
+      const float wt = l > 0.0f ? exp2f(m - bse) : 0.0f;
+      float lw = l > 0.0f ? l * wt : 0.0f;
+#pragma unroll
+      for (int o = kMaxSplits / 2; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+      sm.w[hh][sp] = wt;
+      if (sp == 0) {
+        const float sink2 = P.sink ? P.sink[hh] * kLog2e : -INFINITY;
+        sm.inv[hh] = lw > 0.0f ? 1.0f / (lw + exp2f(sink2 - bse)) : 0.0f;
+      }
+    }
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
+    const int h = it >> 3, seg = it & 7;
+    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
+    float acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
+    for (int sp = 0; sp < S; sp += 2) {
+      if (sp > 0 || it != threadIdx.x) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            v[k][q] = sp + k < S ? __ldcg(op + (sp + k) * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float wt = sp + k < S ? sm.w[h][sp + k] : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[4 * q] += wt != 0.0f ? wt * v[k][q].x : 0.0f;
+          acc[4 * q + 1] += wt != 0.0f ? wt * v[k][q].y : 0.0f;
+          acc[4 * q + 2] += wt != 0.0f ? wt * v[k][q].z : 0.0f;
+          acc[4 * q + 3] += wt != 0.0f ? wt * v[k][q].w : 0.0f;
+        }
+      }
+    }
+    const float inv = sm.inv[h];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      uint4 pk;
+      pk.x = pack_bf16(acc[8 * q] * inv, acc[8 * q + 1] * inv);
+      pk.y = pack_bf16(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
+      pk.z = pack_bf16(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
+      pk.w = pack_bf16(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
+      *reinterpret_cast<uint4*>(&sm.o[h * kOStride + seg * 16 + q * 8]) = pk;
+    }
+  }
+  __syncthreads();
+}
+
+// Mix, inverse RoPE and quantise token t's rows (sm.o, sm.mix and sm.cs
+// ready) and store the e4m3 row and UE8M0 scales.  Warps 0-7 compute (warp
+// = 16 heads x 64 dims); every thread of the block calls it (one barrier).
+__device__ __forceinline__ void vha_mix_quant_token(const AttnParams& P, const VhaOut& V, int t, vt::Smem& sm) {
+  using namespace vt;
+  const int H = P.num_heads;
+  const int hpg = H / V.n_groups;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ht = warp & 3, dh = (warp >> 2) & 1;
+  const int gq = lane >> 2, cq = lane & 3;
+  const int h0 = ht * 16 + gq, h1 = h0 + 8;
+  const bool active = warp < 8 && ht * 16 < H;
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+  if (active) {
+    for (int kk = 0; kk < H / 16; ++kk) {
+      uint32_t a[4];
+      ldmatrix_x4(a, &sm.mix[(ht * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8]);
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b[4];
+        ldmatrix_x4_trans(b, &sm.o[(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kOStride + dh * 64 + j * 8 +
+                                   (lane >> 4) * 8]);
+        mma16816(acc[j], a, b);
+        mma16816(acc[j + 1], a, b + 2);
+      }
+    }
+    // inverse GPT-J RoPE on the dims >= nope
+    const int nope = D - P.rope_dim;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = dh * 64 + j * 8 + 2 * cq;
+      if (d >= nope) {
+        const int pr = (d - nope) >> 1;
+        const float c = sm.cs[pr], sn = sm.cs[P.rope_dim / 2 + pr];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float e = acc[j][2 * hh], od = acc[j][2 * hh + 1];
+          acc[j][2 * hh] = e * c + od * sn;
+          acc[j][2 * hh + 1] = od * c - e * sn;
+        }
+      }
+    }
+    float am0 = 0.0f, am1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      am0 = fmaxf(am0, fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])));
+      am1 = fmaxf(am1, fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])));
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
+    }
+    if (cq == 0) {
+      sm.amax[dh][h0] = am0;
+      sm.amax[dh][h1] = am1;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+  // ---- quantise: one UE8M0 scale per (head, 128 dims) ----
+  const float a0 = fmaxf(sm.amax[0][h0], sm.amax[1][h0]), a1 = fmaxf(sm.amax[0][h1], sm.amax[1][h1]);
+  const int e0 = ue8m0_exponent(a0, 1e-10f, false), e1 = ue8m0_exponent(a1, 1e-10f, false);
+  const float i0 = exp2i(-e0), i1 = exp2i(-e1);
+  uint8_t* r0 = V.out + (static_cast<int64_t>(h0 / hpg) * V.num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
+  uint8_t* r1 = V.out + (static_cast<int64_t>(h1 / hpg) * V.num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
+  uint32_t p0[8], p1[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    p0[j] = to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8);
+    p1[j] = to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8);
+  }
+  // 16 contiguous bytes per lane: one full-sector store instead of eight 2-byte ones
+  *reinterpret_cast<uint4*>(r0 + dh * 64 + 16 * cq) = quad_gather_fp8(p0, cq);
+  *reinterpret_cast<uint4*>(r1 + dh * 64 + 16 * cq) = quad_gather_fp8(p1, cq);
+  if (dh == 0 && cq == 0) {
+    V.scale[static_cast<int64_t>(h0) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e0));
+    V.scale[static_cast<int64_t>(h1) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e1));
+  }
+}
+
+// ============================================================================
 // tcgen05 decode kernel (head_dim 128 = 64 e4m3 NoPE + 64 bf16 RoPE)
 //
 // One CTA per (group, split); up to 256 query rows = two M=128 tiles.
@@ -1169,249 +1389,79 @@ __global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
 //   out:   inverse GPT-J RoPE on the RoPE dims, per-head amax over the two
 //          dim halves, UE8M0 scale, e4m3 bytes in wo_a's input layout.
 // ============================================================================
-struct VhaOut {
-  uint8_t* out;          // [n_groups][tokens][hpg * D] e4m3
-  int32_t* scale;        // [n_groups * hpg][aligned tokens] UE8M0 exponent bytes
-  const __nv_bfloat16* mix;  // [H][H] bf16, I + V U^T
-  const int64_t* positions;
-  const float* cos_sin;
-  int64_t cs_stride;
-  int num_tokens, aligned_t, n_groups, num_groups;
-};
+// Token t's group: its first token t0, first work-list item and item count
+// (S = 0: no group holds it).  Each warp finds it on its own (ballot over
+// groups whose start, end and schedule entry are loaded together), so no
+// block barrier waits on it.
+__device__ __forceinline__ void vha_token_group(const AttnParams& P, const VhaOut& V, int t, int& t0, int& first,
+                                                int& S) {
+  const int lane = threadIdx.x & 31;
+  first = 0;
+  S = 0;
+  t0 = t;
+  const int32_t* gt = P.sched ? P.sched + 4 * P.sched_items : nullptr;
+  if (!P.group_starts) {
+    first = gt ? gt[2 * t] : t * P.num_splits;
+    S = gt ? gt[2 * t + 1] : P.num_splits;
+    return;
+  }
+  for (int base = 0; base < V.num_groups; base += 128) {
+    int a[4], f[4], sc[4];
+    bool hit[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int g = base + k * 32 + lane;
+      hit[k] = false;
+      a[k] = f[k] = sc[k] = 0;
+      if (g < V.num_groups) {
+        a[k] = P.group_starts[g];
+        const int b = P.group_starts[g + 1];
+        f[k] = gt ? gt[2 * g] : g * P.num_splits;
+        sc[k] = gt ? gt[2 * g + 1] : P.num_splits;
+        hit[k] = a[k] <= t && t < b;
+      }
+    }
+    bool found = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const unsigned m = __ballot_sync(0xffffffffu, hit[k]);
+      if (m && !found) {
+        const int src = __ffs(m) - 1;
+        first = __shfl_sync(0xffffffffu, f[k], src);
+        S = __shfl_sync(0xffffffffu, sc[k], src);
+        t0 = __shfl_sync(0xffffffffu, a[k], src);
+        found = true;
+      }
+    }
+    if (found) break;
+  }
+}
 
+// Split-K merge + VHA + inverse RoPE + FP8 quant, one 512-thread CTA per
+// token (two per SM).  Up to the dependency wait this kernel reads only
+// weights (the mix), the RoPE table and per-step metadata (positions, groups,
+// work list), none of which a layer kernel writes, so it overlaps the
+// attention still running on other SMs; the partials (and every store) come
+// after the wait.
 __global__ void __launch_bounds__(512, 2) hca_combine_vha_quant_kernel(const AttnParams P, const VhaOut V) {
-  // Up to the dependency wait this kernel reads only weights (the mix), the
-  // RoPE table and per-step metadata (positions, groups, work list), none of
-  // which a layer kernel writes, so it overlaps the attention still running
-  // on other SMs; the partials (and every store) come after the wait.
   pdl_release();
-  constexpr int D = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = D + 8;
-  constexpr int kMaxSplits = 16;
-  __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
-  __shared__ __align__(16) __nv_bfloat16 o_s[kMaxH * kOStride];
-  __shared__ float cs_s[64];
-  __shared__ float amax_s[2][kMaxH];
-  __shared__ float w_s[kMaxH][kMaxSplits];  // split weights 2^(m_split - m)
-  __shared__ float inv_s[kMaxH];            // 1 / (sum l + sink)
+  __shared__ __align__(16) vt::Smem sm;
   const int H = P.num_heads;
-  const int hpg = H / V.n_groups;
   const int t = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (t >= V.num_tokens) {
     pdl_wait();
     for (int h = threadIdx.x; h < H; h += blockDim.x) V.scale[static_cast<int64_t>(h) * V.aligned_t + t] = 0;
     return;
   }
-  // the mix and this token's cos / sin
-  for (int i = threadIdx.x; i < H * (H / 8); i += blockDim.x) {
-    const int r = i / (H / 8), c8 = i % (H / 8);
-    *reinterpret_cast<uint4*>(&mix_s[r * kMixStride + c8 * 8]) =
-        *reinterpret_cast<const uint4*>(V.mix + static_cast<int64_t>(r) * H + c8 * 8);
-  }
-  if (threadIdx.x < P.rope_dim) cs_s[threadIdx.x] = V.cos_sin[V.positions[t] * V.cs_stride + threadIdx.x];
-  // the token's group: every warp finds it on its own (ballot over groups
-  // whose start, end and schedule entry are loaded together), so no block
-  // barrier waits on it.  S = 0 (O = 0) if no group holds the token.
-  int first = 0, S = 0, t0 = t;
-  const int32_t* gt = P.sched ? P.sched + 4 * P.sched_items : nullptr;
-  if (!P.group_starts) {
-    first = gt ? gt[2 * t] : t * P.num_splits;
-    S = gt ? gt[2 * t + 1] : P.num_splits;
-  } else {
-    for (int base = 0; base < V.num_groups; base += 128) {
-      int a[4], f[4], sc[4];
-      bool hit[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int g = base + k * 32 + lane;
-        hit[k] = false;
-        a[k] = f[k] = sc[k] = 0;
-        if (g < V.num_groups) {
-          a[k] = P.group_starts[g];
-          const int b = P.group_starts[g + 1];
-          f[k] = gt ? gt[2 * g] : g * P.num_splits;
-          sc[k] = gt ? gt[2 * g + 1] : P.num_splits;
-          hit[k] = a[k] <= t && t < b;
-        }
-      }
-      bool found = false;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const unsigned m = __ballot_sync(0xffffffffu, hit[k]);
-        if (m && !found) {
-          const int src = __ffs(m) - 1;
-          first = __shfl_sync(0xffffffffu, f[k], src);
-          S = __shfl_sync(0xffffffffu, sc[k], src);
-          t0 = __shfl_sync(0xffffffffu, a[k], src);
-          found = true;
-        }
-      }
-      if (found) break;
-    }
-  }
+  vha_load_mix(V, H, sm);
+  if (threadIdx.x < P.rope_dim) sm.cs[threadIdx.x] = V.cos_sin[V.positions[t] * V.cs_stride + threadIdx.x];
+  int t0, first, S;
+  vha_token_group(P, V, t, t0, first, S);
   // a group larger than the workspace rows was skipped by the attention launch
-  if ((t - t0 + 1) * H > P.max_rows || S > kMaxSplits) S = 0;
+  if ((t - t0 + 1) * H > P.max_rows || S > vt::kMaxSplits) S = 0;
   pdl_wait();  // the attention launch has written the partials
-  // ---- merge ----
-  // The first two splits' O rows are requested first; while they are in
-  // flight, thread (head, split) pairs turn every split's (m, l) into its
-  // weight (one max and one sum over the 16 lanes of a head); then thread
-  // (head h, 16-dim segment) adds the splits two at a time.
-  {
-    const int h = threadIdx.x >> 3, seg = threadIdx.x & 7;
-    const int64_t row0 = static_cast<int64_t>(first) * P.max_rows + static_cast<int64_t>(t - t0) * H;
-    const int64_t o_step = static_cast<int64_t>(P.max_rows) * D / 4;  // float4s between splits
-    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
-    float4 v[2][4];
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        v[k][q] = (h < H && k < S) ? __ldcg(op + k * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    // H * kMaxSplits <= 2 * blockDim.x: both (m, l) loads of a thread are in
-    // flight together
-    float2 mlv[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = threadIdx.x + k * blockDim.x;
-      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
-      mlv[k] = (i < H * kMaxSplits && sp < S)
-                   ? __ldcg(reinterpret_cast<const float2*>(P.ws_ml + (row0 + static_cast<int64_t>(sp) * P.max_rows + hh) * 2))
-                   : make_float2(-INFINITY, 0.0f);
-    }
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int i = threadIdx.x + k * blockDim.x;
-      if (i >= H * kMaxSplits) break;  // uniform per warp: H * kMaxSplits is a multiple of 32
-      const int hh = i / kMaxSplits, sp = i % kMaxSplits;
-      const float m = mlv[k].x, l = mlv[k].y;
-      float mx = l > 0.0f ? m : -INFINITY;
-#pragma unroll
-      for (int o = kMaxSplits / 2; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float base = mx == -INFINITY ? 0.0f : mx;
-      // an empty split's row was never written: weight 0
-      const float wt = l > 0.0f ? exp2f(m - base) : 0.0f;
-      float lw = l > 0.0f ? l * wt : 0.0f;
-#pragma unroll
-      for (int o = kMaxSplits / 2; o > 0; o >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
-      w_s[hh][sp] = wt;
-      if (sp == 0) {
-        const float sink2 = P.sink ? P.sink[hh] * kLog2e : -INFINITY;
-        inv_s[hh] = lw > 0.0f ? 1.0f / (lw + exp2f(sink2 - base)) : 0.0f;
-      }
-    }
-    __syncthreads();
-    if (h < H) {
-      float acc[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
-      for (int sp = 0; sp < S; sp += 2) {
-        if (sp > 0) {
-#pragma unroll
-          for (int k = 0; k < 2; ++k)
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              v[k][q] = sp + k < S ? __ldcg(op + (sp + k) * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const float wt = sp + k < S ? w_s[h][sp + k] : 0.0f;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc[4 * q] += wt != 0.0f ? wt * v[k][q].x : 0.0f;
-            acc[4 * q + 1] += wt != 0.0f ? wt * v[k][q].y : 0.0f;
-            acc[4 * q + 2] += wt != 0.0f ? wt * v[k][q].z : 0.0f;
-            acc[4 * q + 3] += wt != 0.0f ? wt * v[k][q].w : 0.0f;
-          }
-        }
-      }
-      const float inv = inv_s[h];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        uint4 pk;
-        pk.x = pack_bf16(acc[8 * q] * inv, acc[8 * q + 1] * inv);
-        pk.y = pack_bf16(acc[8 * q + 2] * inv, acc[8 * q + 3] * inv);
-        pk.z = pack_bf16(acc[8 * q + 4] * inv, acc[8 * q + 5] * inv);
-        pk.w = pack_bf16(acc[8 * q + 6] * inv, acc[8 * q + 7] * inv);
-        *reinterpret_cast<uint4*>(&o_s[h * kOStride + seg * 16 + q * 8]) = pk;
-      }
-    }
-  }
-  __syncthreads();
-  // ---- mix ----
-  const int ht = warp & 3, dh = (warp >> 2) & 1;
-  const int gq = lane >> 2, cq = lane & 3;
-  const int h0 = ht * 16 + gq, h1 = h0 + 8;
-  const bool active = warp < 8 && ht * 16 < H;
-  float acc[8][4];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-  if (active) {
-    for (int kk = 0; kk < H / 16; ++kk) {
-      uint32_t a[4];
-      ldmatrix_x4(a, &mix_s[(ht * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8]);
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        uint32_t b[4];
-        ldmatrix_x4_trans(b, &o_s[(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kOStride + dh * 64 + j * 8 +
-                                  (lane >> 4) * 8]);
-        mma16816(acc[j], a, b);
-        mma16816(acc[j + 1], a, b + 2);
-      }
-    }
-    // inverse GPT-J RoPE on the dims >= nope
-    const int nope = D - P.rope_dim;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = dh * 64 + j * 8 + 2 * cq;
-      if (d >= nope) {
-        const int pr = (d - nope) >> 1;
-        const float c = cs_s[pr], sn = cs_s[P.rope_dim / 2 + pr];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float e = acc[j][2 * hh], od = acc[j][2 * hh + 1];
-          acc[j][2 * hh] = e * c + od * sn;
-          acc[j][2 * hh + 1] = od * c - e * sn;
-        }
-      }
-    }
-    float am0 = 0.0f, am1 = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      am0 = fmaxf(am0, fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])));
-      am1 = fmaxf(am1, fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])));
-    }
-#pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
-      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
-    }
-    if (cq == 0) {
-      amax_s[dh][h0] = am0;
-      amax_s[dh][h1] = am1;
-    }
-  }
-  __syncthreads();
-  if (!active) return;
-  // ---- quantise: one UE8M0 scale per (head, 128 dims) ----
-  const float a0 = fmaxf(amax_s[0][h0], amax_s[1][h0]), a1 = fmaxf(amax_s[0][h1], amax_s[1][h1]);
-  const int e0 = ue8m0_exponent(a0, 1e-10f, false), e1 = ue8m0_exponent(a1, 1e-10f, false);
-  const float i0 = exp2i(-e0), i1 = exp2i(-e1);
-  uint8_t* r0 = V.out + (static_cast<int64_t>(h0 / hpg) * V.num_tokens + t) * (hpg * D) + (h0 % hpg) * D;
-  uint8_t* r1 = V.out + (static_cast<int64_t>(h1 / hpg) * V.num_tokens + t) * (hpg * D) + (h1 % hpg) * D;
-  uint32_t p0[8], p1[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    p0[j] = to_e4m3(acc[j][0] * i0) | (to_e4m3(acc[j][1] * i0) << 8);
-    p1[j] = to_e4m3(acc[j][2] * i1) | (to_e4m3(acc[j][3] * i1) << 8);
-  }
-  // 16 contiguous bytes per lane: one full-sector store instead of eight 2-byte ones
-  *reinterpret_cast<uint4*>(r0 + dh * 64 + 16 * cq) = quad_gather_fp8(p0, cq);
-  *reinterpret_cast<uint4*>(r1 + dh * 64 + 16 * cq) = quad_gather_fp8(p1, cq);
-  if (dh == 0 && cq == 0) {
-    V.scale[static_cast<int64_t>(h0) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e0));
-    V.scale[static_cast<int64_t>(h1) * V.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e1));
-  }
+  vha_merge_token(P, t, t0, first, S, sm);
+  vha_mix_quant_token(P, V, t, sm);
 }
 
 int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
@@ -1582,7 +1632,7 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   if (lrc != HCA_OK) return lrc;
   if (fused) {
     *fused_params = P;
-    return HCA_LAUNCH_STATUS();
+    return HCA_OK;
   }
   if (slot_splits > 1)
     return launch_pdl(hca_attention_combine_kernel<128, false>, dim3(num_groups, (P.max_rows + 15) / 16), dim3(256),
