@@ -178,3 +178,34 @@ def test_vha_tp_matches_folded_mix_gloo(num_tokens):
     assert tp_err.mean() <= tp1_err.mean()
     assert tp_err.max() <= tp1_err.max()
     torch.testing.assert_close(tp_out, tp1, atol=0.25, rtol=2e-2)
+
+
+# --------------------------------------------------------------------------- custom-op boundary
+
+
+def test_attention_custom_op_schema_and_fake():
+    """The attention runs as ``torch.ops.hca_b200.hca_attention``: it mutates
+    ``out`` (the schema marks it), has a fake implementation (shape
+    propagation without running), and the layer registers itself by name."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    op = torch.ops.hca_b200.hca_attention
+    schema = str(op.default._schema)
+    out_arg = next(a for a in op.default._schema.arguments if a.name == "out")
+    assert out_arg.alias_info is not None and out_arg.alias_info.is_write, schema
+    assert schema.endswith("-> ()"), schema
+    with FakeTensorMode():
+        q = torch.empty(3, 16, 128, dtype=torch.bfloat16)
+        kv = torch.empty(3, 128, dtype=torch.bfloat16)
+        ks = torch.empty(3, 256)
+        pos = torch.empty(3, dtype=torch.int64)
+        out = torch.empty(3, 16, 128, dtype=torch.bfloat16)
+        assert op(q, kv, ks, pos, out, "model.layers.0.self_attn.x") is None
+    cfg = A.Ernie5_5HCAConfig(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, head_dim=128,
+                              q_lora_rank=512, qk_rope_head_dim=64, o_groups=4, o_lora_rank=64,
+                              hybrid_mla_num_attention_heads=16, num_nextn_predict_layers=0)
+    vcfg = A.make_vllm_config(cfg, max_model_len=1152)
+    vcfg.compilation_config = SimpleNamespace(static_forward_context={})
+    layer = A.Ernie5_5HCAAttention(vcfg, prefix="model.layers.0.self_attn")
+    assert vcfg.compilation_config.static_forward_context[layer.layer_name] is layer
+    assert A._find_layer(layer.layer_name) is layer

@@ -171,6 +171,55 @@ class _Compressor(nn.Module):
         self.state_cache_prefix = f"{prefix}.state_cache"
 
 
+# ---------------------------------------------------------------------------
+# custom-op boundary
+# ---------------------------------------------------------------------------
+# The reference runs a layer's attention as ``torch.ops.vllm.deepseek_v4_attention(
+# hidden_states, positions, out, layer_name)``: a custom op that mutates ``out``,
+# with a fake implementation, which finds its layer by name in the forward
+# context (``V/models/deepseek_v4/attention.py:545-571``).  Its counterpart here
+# takes the layer's projected inputs.
+
+_LAYERS: dict[str, nn.Module] = {}
+
+
+def _register_layer(vllm_config: Any, name: str, layer: nn.Module) -> None:
+    """Make the layer findable by name: in vLLM's static forward context when
+    the config has one, and in this module's registry."""
+    _LAYERS[name] = layer
+    ctx = getattr(getattr(vllm_config, "compilation_config", None), "static_forward_context", None)
+    if isinstance(ctx, dict):
+        ctx[name] = layer
+
+
+def _find_layer(name: str) -> nn.Module:
+    try:
+        layers = get_forward_context().no_compile_layers
+    except RuntimeError:
+        layers = {}
+    layer = layers.get(name) if isinstance(layers, dict) else None
+    if layer is None:
+        layer = _LAYERS.get(name)
+    if layer is None:
+        raise KeyError(f"no HCA attention layer registered as {name!r}")
+    return layer
+
+
+@torch.library.custom_op("hca_b200::hca_attention", mutates_args=("out",))
+def hca_attention(q: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor, positions: torch.Tensor,
+                  out: torch.Tensor, layer_name: str) -> None:
+    """The layer's attention (KV insert, compressor, sparse decode / prefill)
+    into ``out`` ``[T, H_local, D]``, reading this step's metadata from the
+    forward context."""
+    layer = _find_layer(layer_name)
+    layer._attention(q, kv, kv_score, positions, out, get_forward_context().attn_metadata)
+
+
+@hca_attention.register_fake
+def _hca_attention_fake(q, kv, kv_score, positions, out, layer_name):
+    return None
+
+
 class Ernie5_5HCAAttention(nn.Module):
     """One HCA layer on the fp8 ``fp8_ds_mla`` cache (replaces
     ``Ernie5_5HCAFlashMLAAttention``, ``E/nvidia/attention.py:548-551``)."""
@@ -184,6 +233,7 @@ class Ernie5_5HCAAttention(nn.Module):
         _check_attn_tp(cfg, tp_size)
         self.prefix = prefix
         self.layer_name = f"{prefix}.deepseek_v4_multi_head_latent_attention"
+        _register_layer(vllm_config, self.layer_name, self)
         self.hidden_size = cfg.hidden_size
         self.n_heads = cfg.num_attention_heads
         self.n_local_heads = self.n_heads // tp_size
@@ -257,7 +307,9 @@ class Ernie5_5HCAAttention(nn.Module):
         if not isinstance(attn_metadata, dict):  # profile / dummy run
             o.zero_()
         else:
-            self._attention(q, kv, kv_score, positions, o, attn_metadata)
+            # the attention part is one opaque op that writes `o` in place (an
+            # eager break under graph compilation, as the reference's)
+            torch.ops.hca_b200.hca_attention(q, kv, kv_score, positions, o, self.layer_name)
         return self._output(o, positions, gate)
 
     def _attention(self, q, kv, kv_score, positions, o, md: dict) -> None:
