@@ -51,9 +51,37 @@ def peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst figure (a kernel timed alone)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def attention_flops(ctx: np.ndarray, heads: int, head_dim: int) -> int:
+    """sum over query tokens of H * rows(t) * 4 D, rows(t) = (p+1)//128 +
+    min(p+1, 128): the two GEMMs (S = Q K^T, O = P V) of one attention launch."""
+    p = (ctx[:, None] + np.arange(Q_PER_SEQ)[None, :]).reshape(-1)
+    rows = (p + 1) // 128 + np.minimum(p + 1, 128)
+    return int(rows.sum()) * heads * 4 * head_dim
+
+
 def contexts(rank: int) -> np.ndarray:
     rng = np.random.default_rng(1234 + rank)
     return rng.integers(CTX_LO, CTX_HI - Q_PER_SEQ, size=BATCH, endpoint=True)
+
+
+# config 4: 16 sequences whose last query is at position ~1,048,575 (8192
+# compressed entries plus the 128-token window each), 3 queries per sequence
+BATCH_1M, CTX_1M, MAX_COMPRESSED_1M = 16, 1048573, 8320
+
+
+def contexts_1m(rank: int) -> np.ndarray:
+    rng = np.random.default_rng(4321 + rank)
+    return CTX_1M - rng.integers(0, 128, size=BATCH_1M)
 
 
 def row_bytes_algo(head_dim: int, rope_dim: int = 64) -> int:
@@ -474,8 +502,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: the headline metric (config 2); prefill: config 3, a supplementary line")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "decode1m"],
+                    help="decode: the headline metric (config 2); prefill: config 3 and decode1m: config 4, "
+                         "supplementary lines")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="HCA layers per step (37 in the model; fewer only for profiler captures)")
     ap.add_argument("--items", type=int, default=0,
@@ -502,8 +531,11 @@ def main():
     dev = torch.device("cuda", local)
     dims = HCADims(heads=64, head_dim=args.head_dim, rope_dim=64, n_groups=8)
     wide = args.head_dim == 512
-    ctx = contexts(rank)
-    batch = make_decode_batch(ctx.tolist(), Q_PER_SEQ, dims, dev, seed=rank, max_model_len=CTX_HI)
+    long_ctx = args.workload == "decode1m"
+    ctx = contexts_1m(rank) if long_ctx else contexts(rank)
+    ctx_hi = MAX_COMPRESSED_1M * 128 if long_ctx else CTX_HI
+    maxc = MAX_COMPRESSED_1M if long_ctx else MAX_COMPRESSED
+    batch = make_decode_batch(ctx.tolist(), Q_PER_SEQ, dims, dev, seed=rank, max_model_len=ctx_hi)
     T = batch.num_tokens
     layers = args.layers
     caches = [alloc_layer_caches(batch, seed=10_000 * rank + l) for l in range(layers)]
@@ -512,17 +544,16 @@ def main():
     q_raw = torch.randn((layers, T, dims.heads, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
     kv = torch.randn((layers, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
     kv_score = torch.randn((layers, T, 2 * dims.head_dim), generator=g, device=dev)
-    cos_sin = rope_cos_sin_cache(CTX_HI + 8, dims.rope_dim, dims.rope_theta, dev)
+    cos_sin = rope_cos_sin_cache(ctx_hi + 8, dims.rope_dim, dims.rope_theta, dev)
     bufs: dict = {}
     splits = args.splits or None
-    md = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs, max_items=args.items or None)
+    md = build_decode_metadata(batch, maxc, num_splits=splits, buffers=bufs, max_items=args.items or None)
     q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
     o_buf = torch.empty_like(q_buf)
     outs = [None] * layers
 
     def step():
-        m = build_decode_metadata(batch, MAX_COMPRESSED, num_splits=splits, buffers=bufs,
-                                  max_items=args.items or None)
+        m = build_decode_metadata(batch, maxc, num_splits=splits, buffers=bufs, max_items=args.items or None)
         for l in range(layers):
             outs[l] = decode_layer(batch, m, caches[l], weights[l], q_raw[l], kv[l], kv_score[l], cos_sin,
                                    q_buf=q_buf, o_buf=o_buf)
@@ -599,9 +630,12 @@ def main():
     algo = algorithmic_bytes(ctx, dims.heads, dims.head_dim)
     hbm, src = peaks()
     achieved = algo / (attn_us * 1e-6) / 1e9
+    flops = attention_flops(ctx, dims.heads, dims.head_dim)
+    tpk, tsrc = tensor_peak()
+    tflops = flops / (attn_us * 1e-6) / 1e12
     traffic = None
     prof = os.path.join(ROOT, "profiles", "decode_attention_traffic.json")
-    if os.path.exists(prof) and not wide:
+    if os.path.exists(prof) and not wide and not long_ctx:
         try:
             with open(prof) as f:
                 traffic = json.load(f).get("bytes_per_launch")
@@ -642,7 +676,7 @@ def main():
                if cache_bytes > 126e6 else f"caches {cache_bytes / 1e6:.0f} MB fit in L2 (profiling case only)")
 
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not wide:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not wide and not long_ctx:
         sys.path.insert(0, ROOT)
         cpu = cpu_sample_tokens_per_s(15.0)
 
@@ -651,7 +685,9 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": (f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers"
+            "config": {"workload": (f"config 4 (16 req x 3 q at ~1M context: 8192 compressed + 128 window rows, "
+                                    f"H=64, D={dims.head_dim}, fp8 KV) x {layers} HCA layers" if long_ctx else
+                                    f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers"
                                     if not wide else
                                     f"config 2 requests at the model's head_dim (64 req x 3 q, ctx U[4K,128K], "
                                     f"H=64, D=512, fp8 KV) x {layers} HCA layers"),
@@ -665,7 +701,11 @@ def main():
                          "kernel": ("hca_wide_attention_kernel<decode> (CTA pairs)" if wide
                                     else "hca_tc_attention_kernel<decode>") + (" + split merge" if combine else ""),
                          "launch_us": attn_us,
-                         "algorithmic_bytes": algo},
+                         "algorithmic_bytes": algo,
+                         # decode is balanced between HBM and the tensor pipe (arithmetic intensity ~290
+                         # FLOP/B at config 2): the same launch against the bf16 tensor peak
+                         "tensor": {"achieved": tflops, "peak": tpk, "unit": "TFLOP/s", "frac": tflops / tpk,
+                                    "flops": flops, "peak_source": tsrc}},
             "cpu_baseline": cpu,
             "e2e": {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

@@ -380,3 +380,57 @@ def test_decode_prep_ragged_requests_match_three_ops(ops):
     assert torch.equal(qa.view(torch.int16), qf.view(torch.int16))
     for x, y in zip(a, f):
         assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+
+
+def test_decode_prep_rejected_drafts_are_rewritten(ops):
+    """ECHO/MTP rewrites: step A writes a token and its two drafts (KV rows,
+    compressor states, and any block a draft completes); the drafts are
+    rejected and step B re-submits those positions with new values plus the
+    next one.  The caches after A then B equal, byte for byte, those after
+    writing only the accepted token and then B: a block completed by a
+    rejected draft is recomputed from the rewritten states."""
+    from vllm_ernie_b200.decode import build_decode_metadata
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache
+
+    dims = HCADims(heads=64, head_dim=128)
+    ctx = [124, 125, 126, 127, 1000, 5000]  # block ends on token 3, 2, 1, 0 (positions ctx .. ctx + 3)
+    b = make_decode_batch(ctx, 4, dims, DEV, seed=27, max_model_len=64 * 128)
+    caches = alloc_layer_caches(b, seed=28)
+    md = build_decode_metadata(b, 64, num_splits=1)
+    R = len(ctx)
+    g = torch.Generator(device=DEV).manual_seed(29)
+    ape = torch.randn((128, 128), generator=g, device=DEV) * 0.1
+    w = 1.0 + 0.05 * torch.randn(128, generator=g, device=DEV)
+    cs = rope_cos_sin_cache(64 * 128 + 8, 64, dims.rope_theta, DEV)
+
+    def inputs(n):
+        return (torch.randn((n, 64, 128), generator=g, device=DEV).to(torch.bfloat16),
+                torch.randn((n, 128), generator=g, device=DEV).to(torch.bfloat16),
+                torch.randn((n, 256), generator=g, device=DEV))
+
+    def run(cache, tokens_per_req, first, inp):
+        sel = torch.tensor([r * 4 + first + j for r in range(R) for j in range(tokens_per_req)], device=DEV)
+        qsl = torch.arange(0, R + 1, dtype=torch.int32, device=DEV) * tokens_per_req
+        t2r = torch.arange(R, dtype=torch.int32, device=DEV).repeat_interleave(tokens_per_req)
+        q, kv, ks = inp
+        ops.decode_prep(q, kv, ks, ape, b.positions[sel].contiguous(), cs, cache[0], md.swa_slot[sel].contiguous(),
+                        64, cache[1], md.state_slot[sel].contiguous(), b.state_bt, 8, cache[2],
+                        md.comp_slot[sel].contiguous(), 2, w, qsl, t2r, R, 64, 1e-6, 128, 64)
+
+    a_in = inputs(3 * R)   # accepted token + two drafts per request
+    b_in = inputs(3 * R)   # the rewrite: drafts' positions with new values, plus the next position
+    first_only = tuple(x.view(R, 3, *x.shape[1:])[:, :1].reshape(R, *x.shape[1:]).contiguous() for x in a_in)
+    got = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    ref = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    run(got, 3, 0, a_in)
+    run(got, 3, 1, b_in)
+    run(ref, 1, 0, first_only)
+    run(ref, 3, 1, b_in)
+    torch.cuda.synchronize()
+    for x, y in zip(got, ref):
+        assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+    # the drafts did write (a block completed by a draft was computed, then recomputed)
+    mid = [t.clone() for t in (caches.swa, caches.state, caches.comp)]
+    run(mid, 3, 0, a_in)
+    torch.cuda.synchronize()
+    assert not torch.equal(mid[2], ref[2])
