@@ -167,7 +167,7 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
   const int nrows = padded_heads + 1;
   const int rpc = (nrows + gridDim.y - 1) / gridDim.y;
   const int row_lo = blockIdx.y * rpc, row_hi = min(nrows, row_lo + rpc);
-  constexpr int kBatch = 4;
+  constexpr int kBatch = D == 128 ? 8 : 4;  // rows loaded per warp before any is used
   for (int hb = row_lo + warp; hb < row_hi; hb += nwarps * kBatch) {
     WarpRow<D> rows[kBatch];
 #pragma unroll
@@ -827,11 +827,15 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
   auto* qi = static_cast<const __nv_bfloat16*>(q);
   auto* ki = static_cast<const __nv_bfloat16*>(kv);
   // few tokens (decode): CTAs of 4 warps over 4 rows each (many small CTAs
-  // spread over the SMs); many tokens (prefill): one 16-warp CTA per token
+  // spread over the SMs); many tokens (prefill): one CTA per token, its
+  // padded_heads + 1 rows over 9 warps of 8 rows in flight each (D=128) or 16
+  // warps of 4 (D=512)
   const bool few = num_tokens < 4096;
   const int ysplit = few ? (padded_heads + 1 + 3) / 4 : 1;
+  const int threads = few ? 128 : (head_dim == 128 ? 32 * ((padded_heads + 1 + 7) / 8) : 512);
+  if (threads > 1024) return HCA_E_UNSUPPORTED;
   return launch_pdl(head_dim == 128 ? qnorm_rope_kv_insert_kernel<128> : qnorm_rope_kv_insert_kernel<512>,
-                    dim3(num_tokens, ysplit), dim3(few ? 128 : 512), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
+                    dim3(num_tokens, ysplit), dim3(threads), 0, as_stream(stream), qo, q_out_stride_tok, q_out_stride_head, padded_heads, qi,
                     q_stride_tok, q_stride_head, num_heads, ki, kv_stride, swa_cache, page_size,
                     page_stride_bytes, slot_mapping, positions, cos_sin, cos_sin_stride, rope_dim, eps);
 }

@@ -275,11 +275,11 @@ __device__ __forceinline__ void cp16(void* dst, const void* src) {
                : "memory");
 }
 
-constexpr int kVhaStages = 4;
+constexpr int kVhaStages = 3;
 constexpr int kVhaDynSmem = kVhaStages * 64 * (128 + 8) * 2;
 
 template <int D, int MODE>
-__global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16,
+__global__ void __launch_bounds__(256, 3) vha_tok_kernel(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16,
                                                          int64_t ob_st, int64_t ob_sh, const __nv_bfloat16* o,
                                                          int64_t o_st, int64_t o_sh, const __nv_bfloat16* mix,
                                                          const int64_t* positions, const float* cos_sin,
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(256, 2) vha_tok_kernel(uint8_t* out_fp8, int32
   pdl_wait_and_release();
   constexpr int kCk = 128, kMaxH = 64, kMixStride = kMaxH + 8, kOStride = kCk + 8, kChunks = D / kCk;
   __shared__ __align__(16) __nv_bfloat16 mix_s[kMaxH * kMixStride];
-  constexpr int kStages = kVhaStages;  // O chunks in flight: the next three stream in while one is mixed
+  constexpr int kStages = kVhaStages;  // O chunks in flight: the next two stream in while one is mixed
   extern __shared__ __align__(16) uint8_t vha_dyn[];
   auto o_s = reinterpret_cast<__nv_bfloat16(*)[kMaxH * kOStride]>(vha_dyn);  // [kStages][...]
   __shared__ __align__(16) float cs_s[kStages][64];
