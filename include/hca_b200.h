@@ -44,7 +44,8 @@ const char* hca_status_string(int status);
 int hca_version(void);
 /* Device error word of the current device (synchronous read): non-zero if a
  * kernel gave up on a bounded wait (bit 0 loader, 1 dequant, 2 MMA, 3
- * softmax of hca_sparse_decode).  clear != 0 resets it to zero. */
+ * softmax of hca_sparse_decode; bit 4 the streamed many-token path of
+ * hca_qnorm_rope_kv_insert).  clear != 0 resets it to zero. */
 int hca_device_error(int32_t* value, int32_t clear);
 
 /* ---------------------------------------------------------------------- */

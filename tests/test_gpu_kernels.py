@@ -134,6 +134,46 @@ def test_qnorm_rope_kv_insert_matches_oracle(ops, head_dim):
     np.testing.assert_allclose(rows[:, nope:], ref_rows[:, nope:], rtol=2 ** -7, atol=1e-6)
 
 
+@pytest.mark.parametrize("head_dim,heads,padded", [(128, 64, 64), (128, 16, 64), (512, 16, 64)])
+def test_qnorm_rope_kv_insert_streamed_matches_per_token_kernel(ops, head_dim, heads, padded):
+    """At >= 4096 tokens with contiguous heads the library takes the streamed
+    kernel (bulk copies into a shared-memory ring); with a head stride != D
+    it takes the per-token kernel.  Both must write identical bytes (q and
+    the cache), and the q rows must match the oracle."""
+    rng = np.random.default_rng(heads + head_dim)
+    t, r, page = 4500, 64, 64
+    q = bf16_round(rng.standard_normal((t, heads, head_dim)).astype(np.float32) * 2)
+    kv = bf16_round(rng.standard_normal((t, head_dim)).astype(np.float32))
+    pos = rng.integers(0, 8000, size=t)
+    cos_sin = C.rope_cos_sin_cache(8192, r, 160000.0)
+    n_pages = (t + page - 1) // page + 1
+    slots = rng.permutation(n_pages * page)[:t].astype(np.int64)
+    slots[::97] = -1
+    pb = C.page_bytes(page, head_dim, r)
+    q_dev = T(q, torch.bfloat16)
+    # the same q with a head stride of D + 8: the per-token kernel
+    q_wide = torch.zeros((t, heads, head_dim + 8), dtype=torch.bfloat16, device=DEV)
+    q_wide[..., :head_dim] = q_dev
+    q_strided = q_wide[..., :head_dim]
+    assert q_strided.stride(1) != head_dim
+    outs = []
+    for qin in (q_dev, q_strided):
+        cache = torch.zeros((n_pages, pb), dtype=torch.uint8, device=DEV)
+        qo = ops.fused_qnorm_rope_kv_insert(qin, T(kv, torch.bfloat16), cache, T(slots), T(pos), T(cos_sin),
+                                            padded, 1e-6, page)
+        torch.cuda.synchronize()
+        outs.append((qo.view(torch.int16).cpu().numpy(), cache.cpu().numpy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+    assert ops.device_error() == 0
+    ref_q = O.q_prep(q, pos, cos_sin, r, 1e-6, padded_heads=padded)
+    got_q = outs[0][0].astype(np.int16).view(np.uint16).astype(np.uint32) << 16
+    got_q = got_q.view(np.float32)
+    np.testing.assert_allclose(got_q, ref_q, rtol=2 ** -7, atol=1e-6)
+    assert (got_q == ref_q).mean() > 0.99
+    assert not got_q[:, heads:].any()
+
+
 # --------------------------------------------------------------------------
 # compressor
 # --------------------------------------------------------------------------

@@ -1472,8 +1472,14 @@ int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 using namespace hca;
 
 // Device error word: bit 0 loader, bit 1 dequant, bit 2 MMA, bit 3 softmax
-// timed out on an mbarrier.  Zero in normal operation.
+// of the attention kernels, bit 4 the streamed Q prep timed out on an
+// mbarrier.  Zero in normal operation.
 __device__ int g_hca_device_error;
+
+int* hca::device_error_word() {
+  int* p = nullptr;
+  return cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_hca_device_error) == cudaSuccess ? p : nullptr;
+}
 
 extern "C" int hca_device_error(int32_t* value, int32_t clear) {
   if (!value) return HCA_E_INVALID;

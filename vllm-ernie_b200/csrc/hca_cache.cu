@@ -5,7 +5,10 @@
 // All of these are HBM-bound, byte-moving kernels: one warp (or one CTA)
 // per row, 16-byte vector accesses where the row layout allows, no tensor
 // cores.  Row geometry is templated on the head dim (128 or 512).
+#include <algorithm>
+
 #include "hca_common.cuh"
+#include "hca_tc.cuh"
 
 namespace hca {
 namespace {
@@ -205,6 +208,170 @@ __global__ void qnorm_rope_kv_insert_kernel(__nv_bfloat16* q_out, int64_t qo_st,
         rows[b].store_cache_row(row_ptr(cache, slot, page_size, page_stride, g), rope_dim, lane, true, r2.v);
       }
     }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Streamed Q prep for many tokens (prefill).  Persistent CTAs walk tokens
+// t = blockIdx.x, + gridDim.x, ...  Warp 8 (the producer) copies each
+// token's contiguous Q block (num_heads x D bf16), its KV row and its cos /
+// sin row into the next stage of a shared-memory ring with one bulk async
+// copy each (completion counted in bytes on the stage's `full` mbarrier).
+// Warps 0-7 (the consumers) take rows h = warp, warp + 8, ... of the token
+// out of shared memory, kStreamBatch at a time, store them and release the
+// stage on its `empty` mbarrier.  The arithmetic of every row is the one of
+// qnorm_rope_kv_insert_kernel (same lane layout, same order of operations),
+// so both kernels write identical bytes; this one keeps stages x 16 KB per CTA
+// in flight instead of a few rows per warp.
+// ----------------------------------------------------------------------------
+struct QPrepStream {
+  __nv_bfloat16* q_out;
+  int64_t qo_st;  // heads of a token are contiguous (stride D)
+  const __nv_bfloat16* q;
+  int64_t q_st;  // heads of a token are contiguous (stride D)
+  const __nv_bfloat16* kv;
+  int64_t kv_stride;
+  uint8_t* cache;
+  int64_t page_stride;
+  const int64_t* slot_mapping;
+  const int64_t* positions;
+  const float* cos_sin;
+  int64_t cs_stride;
+  int* err;  // bit 4 on a wait that gave up
+  int page_size, padded_heads, num_heads, rope_dim, num_tokens, stages;
+  uint32_t q_bytes, kv_off, cs_off, stage_bytes;
+  float eps;
+};
+
+constexpr int kStreamConsumers = 8;     // consumer warps; warp 8 is the producer
+constexpr int kStreamMaxStages = 8;
+constexpr int kStreamBatch = 4;         // rows a consumer warp reads before it uses any
+constexpr int kStreamErrBit = 1 << 4;
+
+template <int D>
+__global__ void __launch_bounds__(32 * (kStreamConsumers + 1)) qprep_stream_kernel(const QPrepStream P) {
+  extern __shared__ __align__(128) uint8_t qs_ring[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
+  __shared__ int64_t slot_s[kStreamMaxStages];
+  constexpr int E = WarpRow<D>::E;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = P.stages;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], kStreamConsumers);
+    }
+    tc::mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait_and_release();
+  const int T = P.num_tokens;
+  if (warp == kStreamConsumers) {
+    // producer: positions and slots of the next 32 tokens of this CTA are
+    // loaded one per lane, so the cos / sin address is known without a
+    // dependent load per token
+    int64_t pos_l = 0, slot_l = -1;
+    for (int k = 0;; ++k) {
+      const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+      if (t >= T) break;
+      if ((k & 31) == 0) {
+        const int64_t tl = t + static_cast<int64_t>(lane) * gridDim.x;
+        pos_l = tl < T ? P.positions[tl] : 0;
+        slot_l = tl < T ? P.slot_mapping[tl] : -1;
+      }
+      const int64_t pos = __shfl_sync(0xffffffffu, pos_l, k & 31);
+      const int64_t slot = __shfl_sync(0xffffffffu, slot_l, k & 31);
+      const int s = k % S, n = k / S;
+      int ok = 1;
+      if (lane == 0) {
+        if (n > 0 && !tc::mbar_wait(&empty[s], (n - 1) & 1)) ok = 0;
+        if (ok) {
+          uint8_t* st = qs_ring + static_cast<size_t>(s) * P.stage_bytes;
+          slot_s[s] = slot;
+          tc::mbar_arrive_expect_tx(&full[s], P.q_bytes + D * 2 + P.rope_dim * 4);
+          tc::bulk_copy_g2s(st, P.q + t * P.q_st, P.q_bytes, &full[s]);
+          tc::bulk_copy_g2s(st + P.kv_off, P.kv + t * P.kv_stride, D * 2, &full[s]);
+          tc::bulk_copy_g2s(st + P.cs_off, P.cos_sin + pos * P.cs_stride, P.rope_dim * 4, &full[s]);
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        if (lane == 0) atomicOr(P.err, kStreamErrBit);
+        break;
+      }
+    }
+    return;
+  }
+  // consumers
+  const int nope = D - P.rope_dim;
+  const int nrows = P.padded_heads + 1;
+  for (int k = 0;; ++k) {
+    const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+    if (t >= T) break;
+    const int s = k % S;
+    if (!tc::mbar_wait(&full[s], (k / S) & 1)) {
+      if (lane == 0) atomicOr(P.err, kStreamErrBit);
+      break;
+    }
+    const uint8_t* st = qs_ring + static_cast<size_t>(s) * P.stage_bytes;
+    const __nv_bfloat16* qs = reinterpret_cast<const __nv_bfloat16*>(st);
+    const float* cs = reinterpret_cast<const float*>(st + P.cs_off);
+    float pc[E / 2], ps[E / 2];
+#pragma unroll
+    for (int i = 0; i < E / 2; ++i) {
+      const int d = lane * E + 2 * i;
+      pc[i] = 1.0f;
+      ps[i] = 0.0f;
+      if (d >= nope) {
+        pc[i] = cs[(d - nope) >> 1];
+        ps[i] = cs[P.rope_dim / 2 + ((d - nope) >> 1)];
+      }
+    }
+    auto rope = [&](WarpRow<D>& r) {
+#pragma unroll
+      for (int i = 0; i < E / 2; ++i) rope_pair(r.v[2 * i], r.v[2 * i + 1], pc[i], ps[i]);
+    };
+    __nv_bfloat16* qo = P.q_out + t * P.qo_st;
+    for (int hb = warp; hb < nrows; hb += kStreamConsumers * kStreamBatch) {
+      WarpRow<D> rows[kStreamBatch];
+#pragma unroll
+      for (int b = 0; b < kStreamBatch; ++b) {
+        const int h = hb + b * kStreamConsumers;
+        if (h < P.num_heads) rows[b].load_bf16(qs + h * D, lane);
+        else if (h == P.padded_heads) rows[b].load_bf16(reinterpret_cast<const __nv_bfloat16*>(st + P.kv_off), lane);
+      }
+#pragma unroll
+      for (int b = 0; b < kStreamBatch; ++b) {
+        const int h = hb + b * kStreamConsumers;
+        if (h >= nrows) continue;
+        if (h < P.num_heads) {
+          WarpRow<D>& row = rows[b];
+          float ss = 0.0f;
+#pragma unroll
+          for (int i = 0; i < E; ++i) ss += row.v[i] * row.v[i];
+          ss = warp_sum(ss);
+          const float rrms = rsqrtf(ss / static_cast<float>(D) + P.eps);
+#pragma unroll
+          for (int i = 0; i < E; ++i) row.v[i] *= rrms;
+          rope(row);
+          row.store_bf16(qo + h * D, lane);
+        } else if (h < P.padded_heads) {
+          uint16_t* o = reinterpret_cast<uint16_t*>(qo + h * D) + lane * E;
+#pragma unroll
+          for (int i = 0; i < E; ++i) o[i] = 0;
+        } else {
+          // the KV row: RoPE, fp8 NoPE quant, insert
+          const int64_t slot = slot_s[s];
+          if (slot < 0) continue;
+          WarpRow<D> r2 = rows[b];
+          rope(r2);
+          const RowGeom g = row_geom(D, P.rope_dim);
+          rows[b].store_cache_row(row_ptr(P.cache, slot, P.page_size, P.page_stride, g), P.rope_dim, lane, true,
+                                  r2.v);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[s]);
   }
 }
 
@@ -826,11 +993,61 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
   auto* qo = static_cast<__nv_bfloat16*>(q_out);
   auto* qi = static_cast<const __nv_bfloat16*>(q);
   auto* ki = static_cast<const __nv_bfloat16*>(kv);
+  const bool few = num_tokens < 4096;
+  // many tokens (prefill) with contiguous heads and 16-byte aligned rows:
+  // the streamed kernel (persistent CTAs, bulk copies into a shared-memory ring)
+  const auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const int64_t q_bytes = static_cast<int64_t>(num_heads) * head_dim * 2;
+  const auto up16 = [](int64_t v) { return (v + 15) / 16 * 16; };
+  const int64_t stage_bytes = up16(q_bytes) + head_dim * 2 + up16(rope_dim * 4);
+  if (!few && q_stride_head == head_dim && q_out_stride_head == head_dim && a16(q) && a16(q_out) && a16(kv) &&
+      a16(cos_sin) && (q_stride_tok * 2) % 16 == 0 && (q_out_stride_tok * 2) % 16 == 0 && (kv_stride * 2) % 16 == 0 &&
+      (cos_sin_stride * 4) % 16 == 0 && (rope_dim * 4) % 16 == 0 && 2 * stage_bytes <= 200 * 1024) {
+    QPrepStream P;
+    P.q_out = qo;
+    P.qo_st = q_out_stride_tok;
+    P.q = qi;
+    P.q_st = q_stride_tok;
+    P.kv = ki;
+    P.kv_stride = kv_stride;
+    P.cache = swa_cache;
+    P.page_stride = page_stride_bytes;
+    P.slot_mapping = slot_mapping;
+    P.positions = positions;
+    P.cos_sin = cos_sin;
+    P.cs_stride = cos_sin_stride;
+    P.err = device_error_word();
+    if (!P.err) return HCA_E_CUDA;
+    P.page_size = page_size;
+    P.padded_heads = padded_heads;
+    P.num_heads = num_heads;
+    P.rope_dim = rope_dim;
+    P.num_tokens = num_tokens;
+    P.q_bytes = static_cast<uint32_t>(q_bytes);
+    P.kv_off = static_cast<uint32_t>(up16(q_bytes));
+    P.cs_off = P.kv_off + head_dim * 2;
+    P.stage_bytes = static_cast<uint32_t>(stage_bytes);
+    P.eps = eps;
+    // ~64 KB of stages per CTA and up to ~200 KB per SM: 4 stages x 3 CTAs
+    // per SM at 64 heads x 128 dims
+    P.stages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(kStreamMaxStages, 68000 / stage_bytes)));
+    const int64_t smem = P.stages * stage_bytes;
+    auto* kfn = head_dim == 128 ? qprep_stream_kernel<128> : qprep_stream_kernel<512>;
+    const int threads = 32 * (kStreamConsumers + 1);
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+      return HCA_E_CUDA;
+    // resident CTAs per SM (registers and shared memory), at most 3
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, static_cast<size_t>(smem)) != cudaSuccess)
+      return HCA_E_CUDA;
+    per_sm = std::max(1, std::min(3, per_sm));
+    const int grid = static_cast<int>(std::min<int64_t>(num_tokens, static_cast<int64_t>(per_sm) * device_sm_count()));
+    return launch_pdl(kfn, dim3(grid), dim3(threads), static_cast<size_t>(smem), as_stream(stream), P);
+  }
   // few tokens (decode): CTAs of 4 warps over 4 rows each (many small CTAs
-  // spread over the SMs); many tokens (prefill): one CTA per token, its
+  // spread over the SMs); many tokens otherwise: one CTA per token, its
   // padded_heads + 1 rows over 9 warps of 8 rows in flight each (D=128) or 16
   // warps of 4 (D=512)
-  const bool few = num_tokens < 4096;
   const int ysplit = few ? (padded_heads + 1 + 3) / 4 : 1;
   const int threads = few ? 128 : (head_dim == 128 ? 32 * ((padded_heads + 1 + 7) / 8) : 512);
   if (threads > 1024) return HCA_E_UNSUPPORTED;

@@ -83,6 +83,22 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
 
+// Device address of the library's error word (hca_device_error), or nullptr.
+int* device_error_word();
+
+// Streaming multiprocessors of the current device (queried once per process).
+inline int device_sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n = v;
+    else
+      n = 148;
+  }
+  return n;
+}
+
 // Geometry of one cached row: N fp8 bytes + R bf16, then N/64 + 1 scale bytes.
 struct RowGeom {
   int nope, data_bytes, scale_bytes;
