@@ -45,7 +45,8 @@ int hca_version(void);
 /* Device error word of the current device (synchronous read): non-zero if a
  * kernel gave up on a bounded wait (bit 0 loader, 1 dequant, 2 MMA, 3
  * softmax of hca_sparse_decode; bit 4 the streamed many-token path of
- * hca_qnorm_rope_kv_insert).  clear != 0 resets it to zero. */
+ * hca_qnorm_rope_kv_insert, bit 5 that of hca_vha_inv_rope_fp8_quant).
+ * clear != 0 resets it to zero. */
 int hca_device_error(int32_t* value, int32_t clear);
 
 /* ---------------------------------------------------------------------- */

@@ -1472,8 +1472,8 @@ int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 using namespace hca;
 
 // Device error word: bit 0 loader, bit 1 dequant, bit 2 MMA, bit 3 softmax
-// of the attention kernels, bit 4 the streamed Q prep timed out on an
-// mbarrier.  Zero in normal operation.
+// of the attention kernels, bit 4 the streamed Q prep, bit 5 the streamed
+// VHA output kernel timed out on an mbarrier.  Zero in normal operation.
 __device__ int g_hca_device_error;
 
 int* hca::device_error_word() {

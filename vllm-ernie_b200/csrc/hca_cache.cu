@@ -67,17 +67,37 @@ struct WarpRow {
     }
   }
 
+  // Rows known to be 8-byte aligned (shared-memory stages): no alignment test.
+  __device__ __forceinline__ void load_bf16_aligned(const __nv_bfloat16* row, int lane) {
+    const uint2* p = reinterpret_cast<const uint2*>(row + lane * E);
+#pragma unroll
+    for (int i = 0; i < E; i += 4) {
+      const uint2 w = p[i / 4];
+      v[i] = __uint_as_float(w.x << 16);
+      v[i + 1] = __uint_as_float(w.x & 0xffff0000u);
+      v[i + 2] = __uint_as_float(w.y << 16);
+      v[i + 3] = __uint_as_float(w.y & 0xffff0000u);
+    }
+  }
+
+  // Two round-to-nearest-even bf16 conversions in one instruction.
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+
+  __device__ __forceinline__ void store_bf16_aligned(__nv_bfloat16* row, int lane) const {
+    uint2* o = reinterpret_cast<uint2*>(row + lane * E);
+#pragma unroll
+    for (int i = 0; i < E; i += 4) o[i / 4] = make_uint2(pack2(v[i], v[i + 1]), pack2(v[i + 2], v[i + 3]));
+  }
+
   // bf16 of every element, 8-byte vector stores when aligned
   __device__ __forceinline__ void store_bf16(__nv_bfloat16* row, int lane) const {
     uint16_t* o = reinterpret_cast<uint16_t*>(row) + lane * E;
     if ((reinterpret_cast<uintptr_t>(o) & 7) == 0) {
 #pragma unroll
-      for (int i = 0; i < E; i += 4) {
-        uint2 w;
-        w.x = static_cast<uint32_t>(float_to_bf16_bits(v[i])) | (static_cast<uint32_t>(float_to_bf16_bits(v[i + 1])) << 16);
-        w.y = static_cast<uint32_t>(float_to_bf16_bits(v[i + 2])) | (static_cast<uint32_t>(float_to_bf16_bits(v[i + 3])) << 16);
-        *reinterpret_cast<uint2*>(o + i) = w;
-      }
+      for (int i = 0; i < E; i += 4) *reinterpret_cast<uint2*>(o + i) = make_uint2(pack2(v[i], v[i + 1]), pack2(v[i + 2], v[i + 3]));
     } else {
 #pragma unroll
       for (int i = 0; i < E; ++i) o[i] = float_to_bf16_bits(v[i]);
@@ -249,7 +269,7 @@ constexpr int kStreamBatch = 4;         // rows a consumer warp reads before it 
 constexpr int kStreamErrBit = 1 << 4;
 
 template <int D>
-__global__ void __launch_bounds__(32 * (kStreamConsumers + 1)) qprep_stream_kernel(const QPrepStream P) {
+__global__ void __launch_bounds__(32 * (kStreamConsumers + 1), D == 128 ? 4 : 1) qprep_stream_kernel(const QPrepStream P) {
   extern __shared__ __align__(128) uint8_t qs_ring[];
   __shared__ __align__(8) uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
   __shared__ int64_t slot_s[kStreamMaxStages];
@@ -336,8 +356,9 @@ __global__ void __launch_bounds__(32 * (kStreamConsumers + 1)) qprep_stream_kern
 #pragma unroll
       for (int b = 0; b < kStreamBatch; ++b) {
         const int h = hb + b * kStreamConsumers;
-        if (h < P.num_heads) rows[b].load_bf16(qs + h * D, lane);
-        else if (h == P.padded_heads) rows[b].load_bf16(reinterpret_cast<const __nv_bfloat16*>(st + P.kv_off), lane);
+        if (h < P.num_heads) rows[b].load_bf16_aligned(qs + h * D, lane);
+        else if (h == P.padded_heads)
+          rows[b].load_bf16_aligned(reinterpret_cast<const __nv_bfloat16*>(st + P.kv_off), lane);
       }
 #pragma unroll
       for (int b = 0; b < kStreamBatch; ++b) {
@@ -349,11 +370,12 @@ __global__ void __launch_bounds__(32 * (kStreamConsumers + 1)) qprep_stream_kern
 #pragma unroll
           for (int i = 0; i < E; ++i) ss += row.v[i] * row.v[i];
           ss = warp_sum(ss);
-          const float rrms = rsqrtf(ss / static_cast<float>(D) + P.eps);
+          // ss * (1 / D) == ss / D exactly: D is a power of two
+          const float rrms = rsqrtf(ss * (1.0f / static_cast<float>(D)) + P.eps);
 #pragma unroll
           for (int i = 0; i < E; ++i) row.v[i] *= rrms;
           rope(row);
-          row.store_bf16(qo + h * D, lane);
+          row.store_bf16_aligned(qo + h * D, lane);
         } else if (h < P.padded_heads) {
           uint16_t* o = reinterpret_cast<uint16_t*>(qo + h * D) + lane * E;
 #pragma unroll
@@ -1028,19 +1050,19 @@ extern "C" int hca_qnorm_rope_kv_insert(void* q_out, int64_t q_out_stride_tok,
     P.cs_off = P.kv_off + head_dim * 2;
     P.stage_bytes = static_cast<uint32_t>(stage_bytes);
     P.eps = eps;
-    // ~64 KB of stages per CTA and up to ~200 KB per SM: 4 stages x 3 CTAs
-    // per SM at 64 heads x 128 dims
-    P.stages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(kStreamMaxStages, 68000 / stage_bytes)));
+    // ~50 KB of stages per CTA and up to 4 CTAs (~200 KB) per SM: 3 stages
+    // x 4 CTAs per SM at 64 heads x 128 dims
+    P.stages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(kStreamMaxStages, 52000 / stage_bytes)));
     const int64_t smem = P.stages * stage_bytes;
     auto* kfn = head_dim == 128 ? qprep_stream_kernel<128> : qprep_stream_kernel<512>;
     const int threads = 32 * (kStreamConsumers + 1);
     if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
       return HCA_E_CUDA;
-    // resident CTAs per SM (registers and shared memory), at most 3
+    // resident CTAs per SM (registers and shared memory), at most 4
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, static_cast<size_t>(smem)) != cudaSuccess)
       return HCA_E_CUDA;
-    per_sm = std::max(1, std::min(3, per_sm));
+    per_sm = std::max(1, std::min(4, per_sm));
     const int grid = static_cast<int>(std::min<int64_t>(num_tokens, static_cast<int64_t>(per_sm) * device_sm_count()));
     return launch_pdl(kfn, dim3(grid), dim3(threads), static_cast<size_t>(smem), as_stream(stream), P);
   }

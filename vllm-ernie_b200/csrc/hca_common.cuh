@@ -29,24 +29,29 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // columns 16 cq .. 16 cq + 15 of the quad's 64-column segment, so the row
 // is written with one 16-byte store per lane instead of eight 2-byte ones.
 __device__ __forceinline__ uint4 quad_gather_fp8(const uint32_t pair[8], int cq) {
-  // w[k]: this lane's pairs for the 16 bytes that lane k of the quad stores
-  uint32_t w[4];
+  // m[x]: this lane's pairs 2x, 2x + 1; lane cq needs word cq of every quad
+  // lane s (a 4 x 4 word transpose over the quad), done as two butterfly
+  // exchanges: over lane bit 0 (words 0 <-> 1, 2 <-> 3), then over lane
+  // bit 1 (words 0 <-> 2, 1 <-> 3).  After both, m[s] = word cq of lane s.
+  uint32_t m[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) w[k] = (pair[2 * k] & 0xffffu) | (pair[2 * k + 1] << 16);
-  auto sel = [](const uint32_t* a, int i) { return i == 0 ? a[0] : i == 1 ? a[1] : i == 2 ? a[2] : a[3]; };
-  // round r: send the word for lane cq ^ r, receive lane (cq ^ r)'s word for us
-  uint32_t rec[4];
+  for (int x = 0; x < 4; ++x) m[x] = __byte_perm(pair[2 * x], pair[2 * x + 1], 0x5410);
+  const bool b0 = cq & 1, b1 = cq & 2;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) rec[r] = r == 0 ? sel(w, cq) : __shfl_xor_sync(0xffffffffu, sel(w, cq ^ r), r);
-  // got[s] = the word from quad lane s = rec[s ^ cq]
-  uint32_t got[4];
+  for (int x = 0; x < 4; x += 2) {
+    const uint32_t r = __shfl_xor_sync(0xffffffffu, b0 ? m[x] : m[x + 1], 1);
+    if (b0) m[x] = r; else m[x + 1] = r;
+  }
 #pragma unroll
-  for (int s2 = 0; s2 < 4; ++s2) got[s2] = sel(rec, s2 ^ cq);
+  for (int x = 0; x < 2; ++x) {
+    const uint32_t r = __shfl_xor_sync(0xffffffffu, b1 ? m[x] : m[x + 2], 2);
+    if (b1) m[x] = r; else m[x + 2] = r;
+  }
   uint4 o;
-  o.x = __byte_perm(got[0], got[1], 0x5410);
-  o.y = __byte_perm(got[2], got[3], 0x5410);
-  o.z = __byte_perm(got[0], got[1], 0x7632);
-  o.w = __byte_perm(got[2], got[3], 0x7632);
+  o.x = __byte_perm(m[0], m[1], 0x5410);
+  o.y = __byte_perm(m[2], m[3], 0x5410);
+  o.z = __byte_perm(m[0], m[1], 0x7632);
+  o.w = __byte_perm(m[2], m[3], 0x7632);
   return o;
 }
 

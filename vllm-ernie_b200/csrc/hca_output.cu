@@ -7,6 +7,7 @@
 // it once as e4m3 -- HBM-bound.  The head mix is a [H x H] x [H x D] product
 // per token (H = 64: 0.5 MFLOP/token), done on CUDA cores from L1.
 #include "hca_common.cuh"
+#include "hca_tc.cuh"
 
 namespace hca {
 namespace {
@@ -422,6 +423,230 @@ __global__ void __launch_bounds__(256, 3) vha_tok_kernel(uint8_t* out_fp8, int32
   }
 }
 
+// ----------------------------------------------------------------------------
+// Streamed VHA + inverse RoPE + FP8 quant for many tokens (prefill, D=128,
+// plugin scale layout).  Persistent CTAs walk tokens t = blockIdx.x,
+// + gridDim.x, ...  Warp 4 (the producer) copies each token's H rows of O
+// (256 bytes each, one bulk async copy per row into rows padded to 272 bytes,
+// so the transposed ldmatrix reads are free of bank conflicts) and its cos /
+// sin row into the next stage of a shared-memory ring.  The H / 16 consumer
+// warps of a group each own 16 output heads x all 128 dims: their mix rows
+// stay in registers for the whole kernel, the head amax is a quad shuffle,
+// and the stage is released right after the MMAs and the RoPE, before the
+// quant and stores.  With H < 64 several groups work on alternate tokens.
+// Per element the arithmetic is the one of vha_tok_kernel<128, 0> (same MMA
+// order over the heads), so both write identical bytes.
+// ----------------------------------------------------------------------------
+constexpr int kVsConsumers = 4;         // consumer warps; warp 4 is the producer
+constexpr int kVsStages = 4;
+constexpr int kVsRowBytes = 272;        // 256 bytes of O + 16 of padding
+constexpr int kVsStageBytes = 64 * kVsRowBytes + 256;  // H <= 64 rows + cos / sin (R <= 64)
+constexpr int kVsDynSmem = kVsStages * kVsStageBytes;
+constexpr int kVsErrBit = 1 << 5;
+
+struct VhaStream {
+  uint8_t* out_fp8;
+  int32_t* scale;
+  const __nv_bfloat16* o;
+  int64_t o_st, o_sh;
+  const __nv_bfloat16* mix;
+  const int64_t* positions;
+  const float* cos_sin;
+  int64_t cs_stride;
+  int* err;
+  int num_tokens, aligned_t, num_heads, n_groups, rope_dim;
+};
+
+// m16n8k16 with a zero accumulator input (the first k block of a tile).
+__device__ __forceinline__ void mma16816_z(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(0.0f));
+}
+
+// (x * s, y * s) with one packed instruction (each product rounded as fmul.rn).
+__device__ __forceinline__ float2 mul2(float x, float y, float s) {
+  uint64_t d;
+  const float2 a = make_float2(x, y), b = make_float2(s, s);
+  asm("mul.rn.f32x2 %0, %1, %2;\n"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+
+// Two e4m3 conversions (clamp to +-448, round to nearest even) in one
+// instruction: lo in bits 0-7, hi in bits 8-15.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;\n" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <int kH>
+__global__ void __launch_bounds__(32 * (kVsConsumers + 1), 3) vha_stream_kernel(const VhaStream P) {
+  extern __shared__ __align__(128) uint8_t vs_ring[];
+  __shared__ __align__(8) uint64_t full[kVsStages], empty[kVsStages];
+  constexpr int D = 128, kRope = 64, kNope = D - kRope, kMixStride = 64 + 8;
+  constexpr int kWpg = kH / 16;             // consumer warps per token
+  constexpr int kG = kVsConsumers / kWpg;   // token groups
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int hpg = kH / P.n_groups;
+  const int grp = warp / kWpg, mem = warp % kWpg;
+  // the mix (a weight, not written by the previous kernel) is staged in the
+  // ring before the dependency wait; each consumer warp keeps its 16 rows as
+  // MMA A fragments
+  __nv_bfloat16* mix_s = reinterpret_cast<__nv_bfloat16*>(vs_ring);
+  for (int i = threadIdx.x; i < kH * (kH / 8); i += blockDim.x) {
+    const int r = i / (kH / 8), c8 = i % (kH / 8);
+    cp16(&mix_s[r * kMixStride + c8 * 8], P.mix + static_cast<int64_t>(r) * kH + c8 * 8);
+  }
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kVsStages; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], kWpg);
+    }
+    tc::mbar_fence_init();
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  __syncthreads();
+  uint32_t a[kH / 16][4];
+  if (warp < kVsConsumers) {
+#pragma unroll
+    for (int kk = 0; kk < kH / 16; ++kk)
+      ldsm_x4(a[kk], &mix_s[(mem * 16 + (lane & 15)) * kMixStride + kk * 16 + (lane >> 4) * 8], false);
+  }
+  __syncthreads();  // the ring is overwritten from here on
+  pdl_wait_and_release();
+  const int T = P.num_tokens;
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < (P.aligned_t - T) * kH; i += blockDim.x)
+      P.scale[static_cast<int64_t>(i % kH) * P.aligned_t + T + i / kH] = 0;
+  if (warp == kVsConsumers) {
+    // producer: positions of the next 32 tokens of this CTA, one per lane
+    int64_t pos_l = 0;
+    for (int k = 0;; ++k) {
+      const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+      if (t >= T) break;
+      if ((k & 31) == 0) {
+        const int64_t tl = t + static_cast<int64_t>(lane) * gridDim.x;
+        pos_l = tl < T ? P.positions[tl] : 0;
+      }
+      const int64_t pos = __shfl_sync(0xffffffffu, pos_l, k & 31);
+      const int s = k % kVsStages, n = k / kVsStages;
+      int ok = 1;
+      if (lane == 0) {
+        if (n > 0 && !tc::mbar_wait(&empty[s], (n - 1) & 1)) ok = 0;
+        if (ok) tc::mbar_arrive_expect_tx(&full[s], kH * 256 + kRope * 4);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(P.err, kVsErrBit);
+        break;
+      }
+      uint8_t* st = vs_ring + s * kVsStageBytes;
+#pragma unroll
+      for (int r = lane; r < kH; r += 32)
+        tc::bulk_copy_g2s(st + r * kVsRowBytes, P.o + t * P.o_st + r * P.o_sh, 256, &full[s]);
+      if (lane == 0) tc::bulk_copy_g2s(st + 64 * kVsRowBytes, P.cos_sin + pos * P.cs_stride, kRope * 4, &full[s]);
+    }
+    return;
+  }
+  const int gq = lane >> 2, cq = lane & 3;
+  const int h0 = mem * 16 + gq, h1 = h0 + 8;
+  uint8_t* r0b = P.out_fp8 + (static_cast<int64_t>(h0 / hpg) * T) * (hpg * D) + (h0 % hpg) * D + 16 * cq;
+  uint8_t* r1b = P.out_fp8 + (static_cast<int64_t>(h1 / hpg) * T) * (hpg * D) + (h1 % hpg) * D + 16 * cq;
+  // this lane's ldmatrix row within a 16-row k block, and its column
+  const uint32_t ring_u32 = tc::smem_u32(vs_ring);
+  const uint32_t ld_off = ((lane & 7) + ((lane >> 3) & 1) * 8) * kVsRowBytes + (lane >> 4) * 16;
+  for (int k = grp;; k += kG) {
+    const int64_t t = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+    if (t >= T) break;
+    const int s = k % kVsStages;
+    if (!tc::mbar_wait(&full[s], (k / kVsStages) & 1)) {
+      if (lane == 0) atomicOr(P.err, kVsErrBit);
+      break;
+    }
+    const uint32_t st = ring_u32 + s * kVsStageBytes;
+    const float* cs = reinterpret_cast<const float*>(vs_ring + s * kVsStageBytes + 64 * kVsRowBytes);
+    float acc[16][4];
+#pragma unroll
+    for (int kk = 0; kk < kH / 16; ++kk) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        uint32_t bq[4];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(bq[0]), "=r"(bq[1]), "=r"(bq[2]), "=r"(bq[3])
+                     : "r"(st + ld_off + kk * 16 * kVsRowBytes + j * 16));
+        if (kk == 0) {
+          mma16816_z(acc[j], a[kk], bq);
+          mma16816_z(acc[j + 1], a[kk], bq + 2);
+        } else {
+          mma16816_o(acc[j], a[kk], bq);
+          mma16816_o(acc[j + 1], a[kk], bq + 2);
+        }
+      }
+    }
+    // inverse GPT-J RoPE: columns 8 j + 2 cq, + 1 are RoPE dims for j >= 8
+#pragma unroll
+    for (int j = kNope / 8; j < 16; ++j) {
+      const int pr = (j * 8 + 2 * cq - kNope) >> 1;
+      const float c = cs[pr], sn = cs[kRope / 2 + pr];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const float e = acc[j][2 * hh], od = acc[j][2 * hh + 1];
+        acc[j][2 * hh] = e * c + od * sn;
+        acc[j][2 * hh + 1] = od * c - e * sn;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&empty[s]);
+    // head amax (max is exact in any order: a tree, then over the quad)
+    float m0[8], m1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      m0[j] = fmaxf(fmaxf(fabsf(acc[j][0]), fabsf(acc[j][1])), fmaxf(fabsf(acc[j + 8][0]), fabsf(acc[j + 8][1])));
+      m1[j] = fmaxf(fmaxf(fabsf(acc[j][2]), fabsf(acc[j][3])), fmaxf(fabsf(acc[j + 8][2]), fabsf(acc[j + 8][3])));
+    }
+#pragma unroll
+    for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) {
+        m0[j] = fmaxf(m0[j], m0[j + w]);
+        m1[j] = fmaxf(m1[j], m1[j + w]);
+      }
+    float am0 = m0[0], am1 = m1[0];
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      am0 = fmaxf(am0, __shfl_xor_sync(0xffffffffu, am0, off));
+      am1 = fmaxf(am1, __shfl_xor_sync(0xffffffffu, am1, off));
+    }
+    const int e0 = ue8m0_exponent(am0, 1e-10f, false), e1 = ue8m0_exponent(am1, 1e-10f, false);
+    const float i0 = exp2i(-e0), i1 = exp2i(-e1);
+    uint8_t* r0 = r0b + t * (hpg * D);
+    uint8_t* r1 = r1b + t * (hpg * D);
+#pragma unroll
+    for (int seg = 0; seg < 2; ++seg) {
+      uint32_t p0[8], p1[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 y0 = mul2(acc[seg * 8 + j][0], acc[seg * 8 + j][1], i0);
+        const float2 y1 = mul2(acc[seg * 8 + j][2], acc[seg * 8 + j][3], i1);
+        p0[j] = e4m3x2(y0.x, y0.y);
+        p1[j] = e4m3x2(y1.x, y1.y);
+      }
+      *reinterpret_cast<uint4*>(r0 + seg * 64) = quad_gather_fp8(p0, cq);
+      *reinterpret_cast<uint4*>(r1 + seg * 64) = quad_gather_fp8(p1, cq);
+    }
+    if (cq == 0) {
+      P.scale[static_cast<int64_t>(h0) * P.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e0));
+      P.scale[static_cast<int64_t>(h1) * P.aligned_t + t] = static_cast<int32_t>(encode_ue8m0(e1));
+    }
+  }
+}
+
 // x * sigmoid(gate) -> 1x128 FP8; one CTA of 128 threads per (512-col pack, row).
 __global__ void __launch_bounds__(128) sigmoid_mul_quant_kernel(
     uint8_t* out, int32_t* scale, const __nv_bfloat16* x, int64_t x_stride,
@@ -470,6 +695,37 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
         reinterpret_cast<uintptr_t>(mix) % 16 || reinterpret_cast<uintptr_t>(cos_sin) % 16 || cs_stride % 4 ||
         rope_dim > 64 || reinterpret_cast<uintptr_t>(out_fp8) % 16)
       return HCA_E_UNSUPPORTED;
+    if (MODE == 0 && head_dim == 128 && num_tokens >= 1024 && rope_dim == 64 &&
+        (num_heads == 16 || num_heads == 32 || num_heads == 64)) {
+      // many tokens: the streamed kernel (persistent CTAs, one bulk copy per O row)
+      auto* kfn = num_heads == 64 ? vha_stream_kernel<64> : num_heads == 32 ? vha_stream_kernel<32> : vha_stream_kernel<16>;
+      static bool vs_smem_set[3] = {false, false, false};
+      const int ki = num_heads == 64 ? 0 : num_heads == 32 ? 1 : 2;
+      if (!vs_smem_set[ki]) {
+        if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVsDynSmem) != cudaSuccess)
+          return HCA_E_CUDA;
+        vs_smem_set[ki] = true;
+      }
+      VhaStream V;
+      V.out_fp8 = out_fp8;
+      V.scale = scale;
+      V.o = op;
+      V.o_st = o_st;
+      V.o_sh = o_sh;
+      V.mix = mp;
+      V.positions = positions;
+      V.cos_sin = cos_sin;
+      V.cs_stride = cs_stride;
+      V.err = device_error_word();
+      if (!V.err) return HCA_E_CUDA;
+      V.num_tokens = num_tokens;
+      V.aligned_t = aligned;
+      V.num_heads = num_heads;
+      V.n_groups = n_groups;
+      V.rope_dim = rope_dim;
+      const int grid = min(num_tokens, 3 * device_sm_count());
+      return launch_pdl(kfn, dim3(grid), dim3(32 * (kVsConsumers + 1)), kVsDynSmem, s, V);
+    }
     // tokens per CTA: the mix is loaded once per CTA; keep >= 2 CTAs per SM busy
     const int tpc = max(1, min(16, aligned / (2 * 148 * 2)));
     const int ctas = (aligned + tpc - 1) / tpc;
