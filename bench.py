@@ -366,12 +366,12 @@ def prefill_contexts(rank: int) -> np.ndarray:
     return 128 * rng.integers(0, 960, size=PREFILL_SEQS, endpoint=True)
 
 
-def prefill_flops(ctx: np.ndarray, heads: int, head_dim: int) -> float:
+def prefill_flops(ctx: np.ndarray, heads: int, head_dim: int, chunk: int = PREFILL_CHUNK) -> float:
     """Attention FLOPs of one layer: sum over query tokens of
     heads x rows x 4 D, rows = (p + 1) // 128 + min(p + 1, 128)."""
     tot = 0
     for c in ctx.tolist():
-        p = np.arange(c, c + PREFILL_CHUNK, dtype=np.int64)
+        p = np.arange(c, c + chunk, dtype=np.int64)
         tot += int(((p + 1) // 128 + np.minimum(p + 1, 128)).sum())
     return float(tot) * heads * 4 * head_dim
 
@@ -384,7 +384,8 @@ def run_prefill(args, ws, rank, local):
     dev = torch.device("cuda", local)
     dims = HCADims(heads=64, head_dim=128, rope_dim=64, n_groups=8)
     ctx = prefill_contexts(rank)
-    batch = make_decode_batch(ctx.tolist(), PREFILL_CHUNK, dims, dev, seed=rank, max_model_len=CTX_HI)
+    chunk = args.prefill_chunk
+    batch = make_decode_batch(ctx.tolist(), chunk, dims, dev, seed=rank, max_model_len=CTX_HI)
     T = batch.num_tokens
     layers = args.layers if args.layers != LAYERS else 4
     caches = [alloc_layer_caches(batch, seed=20_000 * rank + l) for l in range(layers)]
@@ -394,7 +395,7 @@ def run_prefill(args, ws, rank, local):
              for _ in range(layers)]
     kv = torch.randn((layers, T, dims.head_dim), generator=g, device=dev).to(torch.bfloat16)
     kv_score = torch.randn((layers, T, 2 * dims.head_dim), generator=g, device=dev)
-    cos_sin = rope_cos_sin_cache(CTX_HI + PREFILL_CHUNK + 8, dims.rope_dim, dims.rope_theta, dev)
+    cos_sin = rope_cos_sin_cache(CTX_HI + chunk + 8, dims.rope_dim, dims.rope_theta, dev)
     bufs: dict = {}
     q_buf = torch.empty((T, dims.heads, dims.head_dim), dtype=torch.bfloat16, device=dev)
     o_buf = torch.empty_like(q_buf)
@@ -459,7 +460,49 @@ def run_prefill(args, ws, rank, local):
     e1.record()
     torch.cuda.synchronize()
     attn_us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
-    flops = prefill_flops(ctx, dims.heads, dims.head_dim)
+
+    # the streamed Q prep and VHA kernels alone, back to back over the layers
+    # (each launch reads a 1 GB input: larger than L2)
+    def graph_us(fn):
+        fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        with torch.cuda.graph(gr):
+            fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gr.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del gr
+        return a.elapsed_time(b) * 1e3 / (reps * layers)
+
+    qprep_us = graph_us(lambda: [ops.fused_qnorm_rope_kv_insert(
+        q_raw[l], kv[l], caches[l].swa, md.swa_slot, batch.positions, cos_sin, dims.heads, dims.eps, dims.swa_page,
+        dims.rope_dim, out=q_buf) for l in range(layers)])
+    vha_us = graph_us(lambda: [ops.vha_inv_rope_fp8_quant(
+        o_buf, weights[l].vha_mix, batch.positions, cos_sin, dims.n_groups, dims.nope, dims.rope_dim)
+        for l in range(layers)])
+    hd, hh, rd = dims.head_dim, dims.heads, dims.rope_dim
+    cache_row = (hd - rd) + 2 * rd + (hd - rd) // 64 + 1
+    qprep_bytes = T * (2 * hh * hd * 2 + hd * 2 + rd * 4 + cache_row)
+    vha_bytes = T * (hh * hd * 2 + hh * hd + hh * 4 + rd * 4)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            hbm_peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        hbm_peak = 6650.0
+    streams = {k: {"us": us, "algorithmic_bytes": nb, "gbs": nb / (us * 1e-6) / 1e9,
+                   "frac_hbm": nb / (us * 1e-6) / 1e9 / hbm_peak}
+               for k, us, nb in (("qprep_stream_kernel", qprep_us, qprep_bytes),
+                                 ("vha_stream_kernel", vha_us, vha_bytes))}
+    flops = prefill_flops(ctx, dims.heads, dims.head_dim, chunk)
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak, src = float(json.load(f)["bf16_tflops"]), "measured (burst)"
@@ -471,14 +514,15 @@ def run_prefill(args, ws, rank, local):
             "metric": PREFILL_METRIC, "value": ws * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"config 3 (8 x 8192-token chunks, prior 128*U[0,960], H=64, D=128, fp8 KV) "
+            "config": {"workload": f"config 3 (8 x {chunk}-token chunks, prior 128*U[0,960], H=64, D=128, fp8 KV) "
                                    f"x {layers} HCA layers", "parallelism": f"dp{ws}", "layers": layers,
                        "tokens_per_step_per_gpu": T, "per_layer_us": ms * 1e3 / layers,
-                       "l2": "inputs larger than L2 (1 GB of Q per layer)"},
+                       "l2": f"inputs larger than L2 ({T * dims.heads * dims.head_dim * 2 / 2**30:.2f} GB of Q per layer)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": None, "peak_source": src,
                          "kernel": "hca_tc_attention_kernel<prefill>", "launch_us": attn_us,
                          "algorithmic_flops": flops},
+            "streams": streams,
             "cpu_baseline": None, "e2e": None,
             "gpu_launches": (4 + 5 * layers) * args.steps,
             "clocks": clk.summary(),
@@ -505,6 +549,8 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "decode1m"],
                     help="decode: the headline metric (config 2); prefill: config 3 and decode1m: config 4, "
                          "supplementary lines")
+    ap.add_argument("--prefill-chunk", type=int, default=PREFILL_CHUNK,
+                    help="tokens per sequence of the prefill workload (config 3: 8192; smaller for profiling)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="HCA layers per step (37 in the model; fewer only for profiler captures)")
     ap.add_argument("--items", type=int, default=0,
