@@ -538,46 +538,112 @@ __device__ __forceinline__ CompressCtx compress_begin(int64_t t, int64_t s_blk, 
 
 constexpr int kPoolBatch = 16;  // pooled states per batch of independent loads
 
-// Batch 0 of this thread's pooled states (channel c of its group's first
-// kPoolBatch positions) into pre[j * kCompressThreads + tid] (score) and
-// pre[(kPoolBatch + j) * kCompressThreads + tid] (kv); row_off must be
-// visible to the CTA.  Each thread reads back only its own entries.
+// Running online-softmax state of one (group, channel) thread of the pooling.
+struct PoolAcc {
+  float m, den, acc;
+};
+
+// One batch of kPoolBatch pooled positions (score sc, kv value kv; unused
+// members -inf / 0) folded into the running state.
+__device__ __forceinline__ void pool_batch(PoolAcc& a, const float* sc, const float* kv) {
+  float mb = a.m;
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) mb = fmaxf(mb, sc[j]);
+  const float f = a.m == -INFINITY ? 0.0f : expf(a.m - mb);
+  a.den *= f;
+  a.acc *= f;
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) {
+    const float w = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - mb);
+    a.den += w;
+    a.acc += w * kv[j];
+  }
+  a.m = mb;
+}
+
+// Start of the last batch of the last token group: the pooled positions from
+// here on are the only ones a fast-path compression leaves for after the wait.
 template <int D>
-__device__ __forceinline__ void compress_stage_batch0(const float* state, int state_width, int ratio,
-                                                      const int64_t* row_off, float* pre) {
+__host__ __device__ constexpr int last_pool_batch(int ratio) {
+  return (kCompressThreads / D - 1) * ((ratio + kCompressThreads / D - 1) / (kCompressThreads / D)) +
+         ((ratio - 1 - (kCompressThreads / D - 1) * ((ratio + kCompressThreads / D - 1) / (kCompressThreads / D))) /
+          kPoolBatch) * kPoolBatch;
+}
+
+// pool_batch on a batch staged in this thread's column of `pre`
+// (pre[j * kCompressThreads] score, pre[(kPoolBatch + j) * kCompressThreads]
+// kv): the same operations in the same order, with few registers live.
+__device__ __forceinline__ void pool_batch_smem(PoolAcc& a, const float* pre) {
+  float mb = a.m;
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) mb = fmaxf(mb, pre[j * kCompressThreads]);
+  const float f = a.m == -INFINITY ? 0.0f : expf(a.m - mb);
+  a.den *= f;
+  a.acc *= f;
+#pragma unroll
+  for (int j = 0; j < kPoolBatch; ++j) {
+    const float sc = pre[j * kCompressThreads];
+    const float w = sc == -INFINITY ? 0.0f : expf(sc - mb);
+    a.den += w;
+    a.acc += w * pre[(kPoolBatch + j) * kCompressThreads];
+  }
+  a.m = mb;
+}
+
+// Before the dependency wait: pool this thread's states of earlier steps
+// (block positions below n_old) in the batches compress_pool would use, each
+// staged through this thread's column of `pre` (pre[j * kCompressThreads +
+// tid] score, pre[(kPoolBatch + j) * kCompressThreads + tid] kv).  The batch
+// holding position n_old (the last of the last group) is not pooled: it stays
+// staged, without its members from this launch, which the state save writes
+// into the same slots before compress_pool pools the batch.  row_off must be
+// visible to the CTA.
+template <int D>
+__device__ __forceinline__ void compress_prepool(const float* state, int state_width, int ratio, const int64_t* row_off,
+                                                 int n_old, float* pre, PoolAcc& a) {
   constexpr int kGroups = kCompressThreads / D;
   const int c = threadIdx.x % D, grp = threadIdx.x / D;
   const int per = (ratio + kGroups - 1) / kGroups;
   const int i0 = grp * per, i1 = min(ratio, i0 + per);
-  float sc[kPoolBatch], kv[kPoolBatch];
+  float* col = pre + threadIdx.x;
+  a.m = -INFINITY;
+  a.den = 0.0f;
+  a.acc = 0.0f;
+  constexpr int kHalf = kPoolBatch / 2;
+  for (int b0 = i0; b0 < i1; b0 += kPoolBatch) {
+    // half a batch of loads in flight before any is stored (the whole batch
+    // at once would not fit the registers of two CTAs per SM)
 #pragma unroll
-  for (int j = 0; j < kPoolBatch; ++j) {
-    const int i = i0 + j;
-    sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
-    kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
-  }
+    for (int h = 0; h < kPoolBatch; h += kHalf) {
+      float sc[kHalf], kv[kHalf];
 #pragma unroll
-  for (int j = 0; j < kPoolBatch; ++j) {
-    pre[j * kCompressThreads + threadIdx.x] = sc[j];
-    pre[(kPoolBatch + j) * kCompressThreads + threadIdx.x] = kv[j];
+      for (int j = 0; j < kHalf; ++j) {
+        const int i = b0 + h + j;
+        const bool ld = i < i1 && i < n_old;
+        sc[j] = ld ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
+        kv[j] = ld ? __ldcg(state + row_off[i] + c) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < kHalf; ++j) {
+        const int i = b0 + h + j;
+        if (i < n_old || i >= i1) {  // slots of this launch's states are the save's
+          col[(h + j) * kCompressThreads] = sc[j];
+          col[(kPoolBatch + h + j) * kCompressThreads] = kv[j];
+        }
+      }
+    }
+    if (min(b0 + kPoolBatch, i1) > n_old) break;  // the pending batch
+    pool_batch_smem(a, col);
   }
-}
-
-// Pooled positions (counted back from the block's last) that batch 0 of
-// every group leaves out: states saved in the current launch may lie among
-// them without changing that batch.
-template <int D>
-__device__ __forceinline__ int compress_batch0_margin(int ratio) {
-  constexpr int kGroups = kCompressThreads / D;
-  const int per = (ratio + kGroups - 1) / kGroups;
-  return ratio - (kGroups - 1) * per - kPoolBatch;
 }
 
 // Second part: pool the states, normalise, quantise and store the row (the
-// whole CTA; returns with every thread past its last barrier).  `pre`: batch
-// 0 staged by compress_stage_batch0, or nullptr to load it here.
+// whole CTA; returns with every thread past its last barrier).  pre_pooled:
+// nullptr (load and pool every batch here), or this thread's state after
+// compress_prepool with the pending batch complete in `pre`.
 template <int D>
-__device__ __forceinline__ void compress_pool(const CompressCtx& x, const float* pre, const float* state,
+__device__ __forceinline__ void compress_pool(const CompressCtx& x, const PoolAcc* pre_pooled, const float* pre,
+                                              const float* state,
                                               int state_width, float eps, uint8_t* kv_cache, int kv_page_size,
                                               int64_t kv_page_stride, int rope_dim, int ratio, float* red,
                                               const int64_t* row_off, float* part_flat) {
@@ -591,16 +657,27 @@ __device__ __forceinline__ void compress_pool(const CompressCtx& x, const float*
   const int64_t slot = x.slot;
   const int per = (ratio + kGroups - 1) / kGroups;
   const int i0 = grp * per, i1 = min(ratio, i0 + per);
-  float m = -INFINITY, den = 0.0f, acc = 0.0f;
-  for (int b0 = i0; b0 < i1; b0 += kSub) {
-    float sc[kSub], kv[kSub];
-    if (b0 == i0 && pre) {
+  PoolAcc pa;
+  if (pre_pooled) {
+    // the earlier-step batches were pooled before the wait; the last batch of
+    // the last group is staged in pre, this launch's states included
+    pa = *pre_pooled;
+    const int pend = last_pool_batch<D>(ratio);
+    if (pend >= i0 && pend < i1) {
+      float sc[kSub], kv[kSub];
 #pragma unroll
       for (int j = 0; j < kSub; ++j) {
         sc[j] = pre[j * kCompressThreads + threadIdx.x];
         kv[j] = pre[(kSub + j) * kCompressThreads + threadIdx.x];
       }
-    } else {
+      pool_batch(pa, sc, kv);
+    }
+  } else {
+    pa.m = -INFINITY;
+    pa.den = 0.0f;
+    pa.acc = 0.0f;
+    for (int b0 = i0; b0 < i1; b0 += kSub) {
+      float sc[kSub], kv[kSub];
 #pragma unroll
       for (int j = 0; j < kSub; ++j) {
         const int i = b0 + j;
@@ -609,24 +686,12 @@ __device__ __forceinline__ void compress_pool(const CompressCtx& x, const float*
         sc[j] = i < i1 ? __ldcg(state + row_off[i] + state_width + c) : -INFINITY;
         kv[j] = i < i1 ? __ldcg(state + row_off[i] + c) : 0.0f;
       }
+      pool_batch(pa, sc, kv);
     }
-    float mb = m;
-#pragma unroll
-    for (int j = 0; j < kSub; ++j) mb = fmaxf(mb, sc[j]);
-    const float f = m == -INFINITY ? 0.0f : expf(m - mb);
-    den *= f;
-    acc *= f;
-#pragma unroll
-    for (int j = 0; j < kSub; ++j) {
-      const float w = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - mb);
-      den += w;
-      acc += w * kv[j];
-    }
-    m = mb;
   }
-  part[0][grp][c] = m;
-  part[1][grp][c] = den;
-  part[2][grp][c] = acc;
+  part[0][grp][c] = pa.m;
+  part[1][grp][c] = pa.den;
+  part[2][grp][c] = pa.acc;
   __syncthreads();
   float comp = 0.0f;
   if (grp == 0) {
@@ -681,7 +746,7 @@ __device__ __forceinline__ void compress_token(
   const CompressCtx x = compress_begin<D>(t, s_blk, s_tok, t2r, positions, kv_slot, bt, bt_stride, block_size, norm_w,
                                           cos_sin, cs_stride, rope_dim, ratio, row_off);
   __syncthreads();
-  compress_pool<D>(x, nullptr, state, state_width, eps, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red,
+  compress_pool<D>(x, nullptr, nullptr, state, state_width, eps, kv_cache, kv_page_size, kv_page_stride, rope_dim, ratio, red,
                    row_off, part_flat);
 }
 
@@ -909,19 +974,26 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
       break;
     }
   CompressCtx cx{};
-  bool staged = false;
+  // Fast path (uniform across the CTA): the block's positions from this
+  // launch -- the request's tokens up to the block end, consecutive, all with
+  // a state slot -- are at most one pooling batch, the last of the last
+  // group.  The earlier-step states (no kernel of this step writes them) are
+  // then pooled before the wait, and the pending batch takes this launch's
+  // states from shared memory, written where they are saved.
+  bool fast = false;
+  int64_t blk_start = 0;
+  PoolAcc pa{-INFINITY, 0.0f, 0.0f};
   if (jb >= 0) {
     cx = compress_begin<D>(t0 + jb, p.s_blk, p.s_tok, p.t2r, p.positions, p.comp_slot, p.state_bt, p.state_bt_stride,
                            p.state_page, p.norm_w, p.cos_sin, p.cs_stride, p.rope_dim, p.ratio, row_off);
+    const int64_t p0 = p.positions[t0], pend = p.positions[t0 + jb];
+    const int nnew = static_cast<int>(pend - p0 + 1);
+    blk_start = pend - p.ratio + 1;
+    fast = nnew >= 1 && nnew <= kPoolBatch && nnew <= p.ratio - last_pool_batch<D>(p.ratio);
+    for (int k = 0; fast && k <= jb; ++k)
+      fast = p.state_slot[t0 + k] >= 0 && p.positions[t0 + k] == p0 + k;
     __syncthreads();
-    // Batch 0 of every group holds only states of earlier steps when this
-    // launch's tokens up to the block end fall in the margin (uniform across
-    // the CTA): no kernel of this step writes those, so they are staged in
-    // shared memory before the wait too.
-    if (p.positions[t0 + jb] - p.positions[t0] < compress_batch0_margin<D>(p.ratio)) {
-      compress_stage_batch0<D>(p.state, p.state_width, p.ratio, row_off, pre_s);
-      staged = true;
-    }
+    if (fast) compress_prepool<D>(p.state, p.state_width, p.ratio, row_off, p.ratio - nnew, pre_s, pa);
   }
   pdl_wait();  // kv and the compressor inputs are outputs of the layer's projections
   // KV rows: one warp per token
@@ -949,13 +1021,26 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
     const int slot = static_cast<int>(slot64);
     const int blk = slot / p.state_page;
     float* sb = p.state + blk * p.s_blk + (slot - blk * p.state_page) * p.s_tok;
-    const int pm = static_cast<int>(p.positions[t]) % p.ratio;
-    sb[c] = p.st_kv[t * p.st_kv_stride + c];
-    sb[p.state_width + c] = p.st_score[t * p.st_score_stride + c] + p.ape[pm * p.ape_stride + c];
+    const int64_t pos = p.positions[t];
+    const int pm = static_cast<int>(pos) % p.ratio;
+    const float kvv = p.st_kv[t * p.st_kv_stride + c];
+    const float scv = p.st_score[t * p.st_score_stride + c] + p.ape[pm * p.ape_stride + c];
+    sb[c] = kvv;
+    sb[p.state_width + c] = scv;
+    if (fast && pos >= blk_start && pos < blk_start + p.ratio) {
+      // this launch's member of the pending batch: the slot of its pooling
+      // thread (last group, channel c)
+      constexpr int kGroups = kCompressThreads / D;
+      const int bi = static_cast<int>(pos - blk_start);
+      const int owner = (bi / ((p.ratio + kGroups - 1) / kGroups)) * D + c;
+      const int jj = bi - last_pool_batch<D>(p.ratio);
+      pre_s[jj * kCompressThreads + owner] = scv;
+      pre_s[(kPoolBatch + jj) * kCompressThreads + owner] = kvv;
+    }
   }
   __syncthreads();  // the states (and row_off) are visible to the whole CTA
   if (jb >= 0) {
-    compress_pool<D>(cx, staged ? pre_s : nullptr, p.state, p.state_width, p.eps, p.comp_cache, p.comp_page,
+    compress_pool<D>(cx, fast ? &pa : nullptr, pre_s, p.state, p.state_width, p.eps, p.comp_cache, p.comp_page,
                      p.comp_pstride, p.rope_dim, p.ratio, red, row_off, &part[0][0][0]);
     __syncthreads();
   }
