@@ -317,15 +317,16 @@ def test_vha_inv_rope_fp8_quant_matches_oracle(ops, head_dim, t):
     np.testing.assert_allclose(y.float().cpu().numpy(), y_ref, rtol=2 ** -7, atol=1e-5)
 
 
-@pytest.mark.parametrize("heads,groups", [(64, 8), (32, 4), (16, 4)])
-def test_vha_fp8_quant_streamed_matches_per_token_kernel(ops, heads, groups):
+@pytest.mark.parametrize("heads,groups,t", [(64, 8, 1900), (32, 4, 1900), (16, 4, 1900), (64, 8, 1901)])
+def test_vha_fp8_quant_streamed_matches_per_token_kernel(ops, heads, groups, t):
     """At >= 1024 tokens (D=128) the library takes the streamed VHA kernel
     (persistent CTAs, bulk row copies, 16 heads x 128 dims per warp, several
     token groups per CTA below 64 heads); below it the per-token-block
     kernel.  The same tokens run in calls of < 1024 tokens must give the
-    identical e4m3 bytes and scales."""
-    rng = np.random.default_rng(heads)
-    t, d, r = 1900, 128, 64
+    identical e4m3 bytes and scales; the scale rows of the padding tokens up
+    to the next multiple of 4 are zero."""
+    rng = np.random.default_rng(heads + t)
+    d, r = 128, 64
     o = T(bf16_round(rng.standard_normal((t, heads, d)).astype(np.float32)), torch.bfloat16)
     u = rng.standard_normal((heads, 16)).astype(np.float32) / 8
     v = rng.standard_normal((heads, 16)).astype(np.float32) / 8
@@ -337,6 +338,10 @@ def test_vha_fp8_quant_streamed_matches_per_token_kernel(ops, heads, groups):
     assert ops.device_error() == 0
     got_d = data.contiguous().view(torch.uint8).cpu().numpy()
     got_s = scale.contiguous().cpu().numpy()
+    # scale is a [t] view of a [groups, hpg, aligned(t)] buffer: its padding columns
+    full = torch.as_strided(scale, (groups, heads // groups, (t + 3) // 4 * 4),
+                            (scale.stride(1), scale.stride(2), scale.stride(0))).cpu().numpy()
+    assert not full[:, :, t:].any()
     for a, b in ((0, 1000), (1000, t)):
         d2, s2 = ops.vha_inv_rope_fp8_quant(o[a:b], mix, pos[a:b], cs, groups, d - r, r)
         assert np.array_equal(got_d[a:b], d2.contiguous().view(torch.uint8).cpu().numpy())
