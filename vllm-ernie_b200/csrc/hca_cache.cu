@@ -484,10 +484,10 @@ __global__ void save_partial_states_kernel(float* state, int64_t s_blk, int64_t 
 
 // ----------------------------------------------------------------------------
 // Block compressor: a 512-thread CTA per 32 tokens pools each of them that
-// completes a block.  Thread (g, c)
-// owns channel c of token group g (512 / D groups split the `ratio` pooled
-// tokens); each thread pools its tokens 32 at a time with independent loads
-// (online softmax per channel), the groups merge in shared memory, then the
+// completes a block.  Thread (g, c) owns channel c of token group g (512 / D
+// groups split the `ratio` pooled tokens); each thread pools its tokens in
+// batches of kPoolBatch with independent loads (online softmax per channel,
+// one rescale per batch), the groups merge in shared memory, then the
 // D threads of group 0 apply RMSNorm, the NoPE quant of the bf16 rounding,
 // and RoPE of the fp32 normed value at the block start position, and store
 // the row into the compressed cache.
@@ -961,7 +961,7 @@ __global__ void __launch_bounds__(kCompressThreads, 2) decode_prep_kernel(const 
   __shared__ float red[32];
   __shared__ int64_t row_off[512];
   __shared__ float part[3][kCompressThreads / D][D];
-  extern __shared__ float pre_s[];  // batch 0 of the pooled states: kPrepDynSmem bytes
+  extern __shared__ float pre_s[];  // one pooling batch per thread column: kPrepDynSmem bytes
   const int r = blockIdx.x;
   const int t0 = p.qsl[r], t1 = p.qsl[r + 1];
   const RowGeom g = row_geom(D, p.rope_dim);
