@@ -1626,13 +1626,10 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
     return launch_pdl(hca_attention_combine_kernel<512, false>, dim3(num_groups, (P.max_rows + 15) / 16), dim3(256),
                       0, s, P);
   }
-  static bool smem_set = false;  // one attribute call per process (same value every time)
-  if (!smem_set) {
-    if (cudaFuncSetAttribute(hca_tc_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             tcd::kSmemBytes) != cudaSuccess)
-      return HCA_E_CUDA;
-    smem_set = true;
-  }
+  static bool smem_set[kMaxDevices] = {};
+  if (set_func_attr_once(hca_tc_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tcd::kSmemBytes,
+                         smem_set) != HCA_OK)
+    return HCA_E_CUDA;
   const int lrc = launch_pdl(hca_tc_attention_kernel<false>, schedule ? dim3(max_items, 1) : dim3(num_splits, num_groups),
                              dim3(tcd::kThreads), tcd::kSmemBytes, s, P, err);
   if (lrc != HCA_OK) return lrc;
@@ -1733,13 +1730,10 @@ extern "C" int hca_sparse_decode_vha_fp8_quant(
   V.aligned_t = (num_tokens + 3) / 4 * 4;
   V.n_groups = n_groups;
   V.num_groups = group_starts ? num_groups : num_tokens;
-  static bool carveout_set = false;  // two CTAs per SM: prefer shared memory over L1 (same value every time)
-  if (!carveout_set) {
-    if (cudaFuncSetAttribute(hca_combine_vha_quant_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return HCA_E_CUDA;
-    carveout_set = true;
-  }
+  static bool carveout_set[kMaxDevices] = {};  // two CTAs per SM: prefer shared memory over L1
+  if (set_func_attr_once(hca_combine_vha_quant_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared, carveout_set) != HCA_OK)
+    return HCA_E_CUDA;
   return launch_pdl(hca_combine_vha_quant_kernel, dim3(V.aligned_t), dim3(512), 0, as_stream(stream), P, V);
 }
 
@@ -1843,13 +1837,10 @@ extern "C" int hca_sparse_prefill(void* out, int64_t out_stride_tok, int64_t out
     HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(swa_cache) % 16 == 0 && reinterpret_cast<uintptr_t>(comp_cache) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride_tok % 8 == 0 && q_stride_head % 8 == 0);
     HCA_CHECK_ARG(out_stride_head % 8 == 0 && out_stride_tok % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0);
-    static bool smem_set = false;  // one attribute call per process (same value every time)
-    if (!smem_set) {
-      if (cudaFuncSetAttribute(hca_tc_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               tcd::kSmemBytes) != cudaSuccess)
-        return HCA_E_CUDA;
-      smem_set = true;
-    }
+    static bool smem_set[kMaxDevices] = {};
+    if (set_func_attr_once(hca_tc_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           tcd::kSmemBytes, smem_set) != HCA_OK)
+      return HCA_E_CUDA;
     int* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_hca_device_error) != cudaSuccess) return HCA_E_CUDA;
     // tiles never straddle requests: at most tokens / G + requests of them

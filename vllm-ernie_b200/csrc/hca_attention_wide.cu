@@ -640,13 +640,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
 int launch_wide_attention(const AttnParams& P, bool prefill, int num_groups, int max_group_tokens, int* err,
                           cudaStream_t s) {
   using namespace tcw;
-  static bool smem_set[2] = {false, false};  // one attribute call per kernel and process
+  static bool smem_set[2][kMaxDevices] = {};  // per kernel and device
   auto kernel = prefill ? hca_wide_attention_kernel<true> : hca_wide_attention_kernel<false>;
-  if (!smem_set[prefill]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
-      return HCA_E_CUDA;
-    smem_set[prefill] = true;
-  }
+  if (set_func_attr_once(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes, smem_set[prefill]) != HCA_OK)
+    return HCA_E_CUDA;
   const int tiles_per_group = prefill || P.sched ? 1 : (max_group_tokens + P.group_tokens - 1) / P.group_tokens;
   const int64_t pairs = prefill ? static_cast<int64_t>(num_groups)
                         : P.sched ? static_cast<int64_t>(P.sched_items)

@@ -1312,12 +1312,10 @@ extern "C" int hca_decode_prep(
   const int rows_per_cta = head_dim == 128 ? prep_rows<128>() : prep_rows<512>();
   const int64_t q_ctas = (static_cast<int64_t>(num_tokens) * padded_heads + rows_per_cta - 1) / rows_per_cta;
   auto kernel = head_dim == 128 ? decode_prep_kernel<128> : decode_prep_kernel<512>;
-  static bool smem_set[2] = {false, false};  // one attribute call per kernel and process
-  if (!smem_set[head_dim == 512]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepDynSmem) != cudaSuccess)
-      return HCA_E_CUDA;
-    smem_set[head_dim == 512] = true;
-  }
+  static bool smem_set[2][kMaxDevices] = {};  // per kernel and device
+  if (set_func_attr_once(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrepDynSmem, smem_set[head_dim == 512]) !=
+      HCA_OK)
+    return HCA_E_CUDA;
   return launch_pdl(kernel, dim3(static_cast<unsigned>(num_reqs + q_ctas)), dim3(kCompressThreads), kPrepDynSmem,
                     as_stream(stream), p);
 }

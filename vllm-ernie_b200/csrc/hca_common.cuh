@@ -91,6 +91,23 @@ inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b)
 // Device address of the library's error word (hca_device_error), or nullptr.
 int* device_error_word();
 
+constexpr int kMaxDevices = 64;
+
+// cudaFuncSetAttribute once per (kernel, device): an attribute set while one
+// device is current does not carry to another device's context.  `done` holds
+// one kernel's flags for one attribute (devices past kMaxDevices set it on
+// every call).
+template <typename K>
+inline int set_func_attr_once(K kernel, cudaFuncAttribute attr, int value, bool (&done)[kMaxDevices]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HCA_E_CUDA;
+  const bool tracked = dev >= 0 && dev < kMaxDevices;
+  if (tracked && done[dev]) return HCA_OK;
+  if (cudaFuncSetAttribute(kernel, attr, value) != cudaSuccess) return HCA_E_CUDA;
+  if (tracked) done[dev] = true;
+  return HCA_OK;
+}
+
 // Streaming multiprocessors of the current device (queried once per process).
 inline int device_sm_count() {
   static int n = 0;

@@ -699,13 +699,10 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
         (num_heads == 16 || num_heads == 32 || num_heads == 64)) {
       // many tokens: the streamed kernel (persistent CTAs, one bulk copy per O row)
       auto* kfn = num_heads == 64 ? vha_stream_kernel<64> : num_heads == 32 ? vha_stream_kernel<32> : vha_stream_kernel<16>;
-      static bool vs_smem_set[3] = {false, false, false};
+      static bool vs_smem_set[3][kMaxDevices] = {};  // per kernel and device
       const int ki = num_heads == 64 ? 0 : num_heads == 32 ? 1 : 2;
-      if (!vs_smem_set[ki]) {
-        if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVsDynSmem) != cudaSuccess)
-          return HCA_E_CUDA;
-        vs_smem_set[ki] = true;
-      }
+      if (set_func_attr_once(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVsDynSmem, vs_smem_set[ki]) != HCA_OK)
+        return HCA_E_CUDA;
       VhaStream V;
       V.out_fp8 = out_fp8;
       V.scale = scale;
@@ -730,12 +727,10 @@ int launch_vha(uint8_t* out_fp8, int32_t* scale, __nv_bfloat16* out_bf16, int64_
     const int tpc = max(1, min(16, aligned / (2 * 148 * 2)));
     const int ctas = (aligned + tpc - 1) / tpc;
     auto* kfn = head_dim == 128 ? vha_tok_kernel<128, MODE> : vha_tok_kernel<512, MODE>;
-    static bool smem_set[2] = {false, false};  // per head dim (same value every time)
-    if (!smem_set[head_dim == 128]) {
-      if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVhaDynSmem) != cudaSuccess)
-        return HCA_E_CUDA;
-      smem_set[head_dim == 128] = true;
-    }
+    static bool smem_set[2][kMaxDevices] = {};  // per head dim and device
+    if (set_func_attr_once(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kVhaDynSmem, smem_set[head_dim == 128]) !=
+        HCA_OK)
+      return HCA_E_CUDA;
     return launch_pdl(kfn, dim3(ctas), dim3(256), kVhaDynSmem, s, out_fp8, scale, out_bf16, ob_st, ob_sh, op, o_st, o_sh, mp, positions,
                       cos_sin, cs_stride, num_tokens, aligned, num_heads, n_groups, rope_dim, tpc);
   }
