@@ -108,17 +108,17 @@ inline int set_func_attr_once(K kernel, cudaFuncAttribute attr, int value, bool 
   return HCA_OK;
 }
 
-// Streaming multiprocessors of the current device (queried once per process).
+// Streaming multiprocessors of the current device (queried once per device;
+// 148, a B200's count, if the query fails).
 inline int device_sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-      n = v;
-    else
-      n = 148;
-  }
-  return n;
+  static int n[kMaxDevices] = {};
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  const bool tracked = dev >= 0 && dev < kMaxDevices;
+  if (tracked && n[dev] > 0) return n[dev];
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+  if (tracked) n[dev] = v;
+  return v;
 }
 
 // Geometry of one cached row: N fp8 bytes + R bf16, then N/64 + 1 scale bytes.
