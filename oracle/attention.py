@@ -14,8 +14,14 @@ interface documents them
 * the sink multiplies the output by ``exp(lse) / (exp(lse) + exp(sink_h))``;
   a token with no rows outputs zeros.
 
-The closed FlashMLA binary is not run; this restatement is the only pin of
-the attention core ("parity unpinned" by a reference run).
+The closed FlashMLA binary is not run.  The restatement is pinned against
+vLLM's readable DeepSeek-V4 sparse attention kernels for the same op, cache
+layout and sink (``_sparse_attn_decode_ragged_kernel`` /
+``_sparse_attn_prefill_ragged_kernel`` in
+``vllm/v1/attention/ops/rocm_aiter_mla_sparse.py``, driven as in
+``vllm/models/deepseek_v4/amd/rocm.py``): ``tests/golden/make_golden.py``
+runs them under the Triton interpreter at D=512 and
+``tests/test_oracle_golden.py`` checks this module against their outputs.
 """
 
 from __future__ import annotations

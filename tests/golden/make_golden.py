@@ -1,7 +1,8 @@
 """Generate golden vectors by running the reference's own Triton kernels on
 the CPU (Triton interpreter).  Run in the build container only:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    HCA_REFERENCE_ATTENTION=<plugin>/src/vllm_ernie/models/ernie5_5/nvidia/attention.py \
+        TRITON_INTERPRET=1 python tests/golden/make_golden.py [insert|compressor|metadata|output|attention ...]
 
 Sources executed:
 
@@ -33,12 +34,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-PLUGIN_ATTENTION = Path(
-    os.environ.get(
-        "HCA_REFERENCE_ATTENTION",
-        "/root/reference/src/vllm_ernie/models/ernie5_5/nvidia/attention.py",
-    )
-)
+# The plugin's ``src/vllm_ernie/models/ernie5_5/nvidia/attention.py`` (needed
+# by the "output" fixtures only): set HCA_REFERENCE_ATTENTION to its path.
+PLUGIN_ATTENTION_ENV = "HCA_REFERENCE_ATTENTION"
 
 D, R, NOPE = 512, 64, 448
 
@@ -112,17 +110,39 @@ def patch_interpreter() -> None:
 
     interp.InterpreterBuilder.create_dot = create_dot
 
+    # Elementwise arithmetic on two bf16 tensors (e.g. the fp8 dequant
+    # ``x.to(bf16) * scale.to(bf16)``) would also act on the raw bit
+    # patterns: evaluate it in fp32 and round to bf16 (RTNE), as the compiled
+    # kernel's fp32-promoted arithmetic does.
+    stock_binary = interp.InterpreterBuilder.binary_op
+
+    def binary_op(self, lhs, rhs, op):
+        if lhs.dtype.scalar.name != "bf16" or rhs.dtype.scalar.name != "bf16":
+            return stock_binary(self, lhs, rhs, op)
+        widen = lambda h: (h.data.astype(np.uint32) << 16).view(np.float32)  # noqa: E731
+        res = op(widen(lhs), widen(rhs))
+        if res.dtype != np.float32:
+            return interp.TensorHandle(res, lhs.dtype.scalar)
+        bits = torch.from_numpy(np.ascontiguousarray(res)).to(torch.bfloat16).view(torch.int16).numpy()
+        return interp.TensorHandle(bits.view(np.uint16).reshape(np.shape(res)), lhs.dtype.scalar)
+
+    interp.InterpreterBuilder.binary_op = binary_op
+
 
 def plugin_kernels():
     """Load the plugin's two @triton.jit kernels from its source file."""
     from vllm.triton_utils import tl, triton
 
-    tree = ast.parse(PLUGIN_ATTENTION.read_text())
+    path = os.environ.get(PLUGIN_ATTENTION_ENV)
+    if not path:
+        raise SystemExit(f"set {PLUGIN_ATTENTION_ENV} to the plugin's ernie5_5/nvidia/attention.py")
+    path = Path(path)
+    tree = ast.parse(path.read_text())
     wanted = {"_vha_inv_rope_quant_kernel", "_sigmoid_mul_quant_kernel"}
     nodes = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name in wanted]
     assert {n.name for n in nodes} == wanted
     ns = {"tl": tl, "triton": triton}
-    exec(compile(ast.Module(body=nodes, type_ignores=[]), str(PLUGIN_ATTENTION), "exec"), ns)
+    exec(compile(ast.Module(body=nodes, type_ignores=[]), str(path), "exec"), ns)
     return ns["_vha_inv_rope_quant_kernel"], ns["_sigmoid_mul_quant_kernel"]
 
 
@@ -330,10 +350,180 @@ def gen_norm_and_output(g: torch.Generator) -> None:
         save(f"sigmoid_mul_quant_{rows}x{hidden}", x=x, gate=gate, fp8=q, scale=s.contiguous())
 
 
+def _bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _fill_rows(cache: torch.Tensor, slots: np.ndarray, block: int, g: torch.Generator) -> None:
+    """Write N(0, 1) rows (bf16, then the reference's fp8 insert) at ``slots``."""
+    from vllm.models.deepseek_v4.common.ops.cache_utils import quantize_and_insert_k_cache
+
+    slots = np.unique(slots[slots >= 0]).astype(np.int64)
+    k = torch.randn(len(slots), D, generator=g).bfloat16()
+    quantize_and_insert_k_cache(k, cache, torch.from_numpy(slots), block_size=block)
+
+
+def gen_attention() -> None:
+    """Sparse decode and prefill attention at D=512, through vLLM's readable
+    DeepSeek-V4 Triton kernels ``_sparse_attn_decode_ragged_kernel`` and
+    ``_sparse_attn_prefill_ragged_kernel``
+    (``vllm/v1/attention/ops/rocm_aiter_mla_sparse.py``), fed the way
+    ``vllm/models/deepseek_v4/amd/rocm.py`` ``_forward_decode`` /
+    ``_forward_prefill`` feed them: builders' index tables, ragged packing,
+    the bf16 gather workspace and ``combine_topk_swa_indices`` for prefill.
+    Every step runs reference code; its own seed keeps the fixture
+    independent of the other generators."""
+    from vllm.models.deepseek_v4.common.ops.cache_utils import (
+        combine_topk_swa_indices,
+        dequantize_and_gather_k_cache_triton,
+    )
+    from vllm.v1.attention.backends.mla.flashmla_sparse import build_c128a_topk_metadata
+    from vllm.v1.attention.backends.mla.sparse_swa import (
+        _compute_prefill_metadata_kernel,
+        _compute_swa_indices_and_lens_kernel,
+    )
+    from vllm.v1.attention.ops import rocm_aiter_mla_sparse as ra
+
+    g = torch.Generator().manual_seed(5)
+    H, W, ratio, swa_page, comp_page = 16, 128, 128, 64, 2
+    comp_stride = 1728  # 2 x 584 bytes padded to the 576-byte page alignment
+    scale = D ** -0.5
+    maxc = 128  # compressed index width (max_model_len 16384)
+
+    def caches(n_swa_pages: int, n_comp_pages: int):
+        swa = torch.zeros(n_swa_pages, swa_page * 584, dtype=torch.uint8)
+        comp = torch.zeros(n_comp_pages, comp_stride, dtype=torch.uint8)
+        return swa, comp
+
+    def as_pages(raw: torch.Tensor, block: int) -> torch.Tensor:
+        return raw.as_strided((raw.shape[0], block, 584), (raw.stride(0), 584, 1))
+
+    sinks = {
+        "random": torch.randn(H, generator=g),
+        "neginf": torch.full((H,), -float("inf")),
+        "none": None,
+    }
+
+    # ---------------- decode: 4 requests, MTP-style consecutive tokens ----
+    # r0 crosses a compression boundary between its tokens, r1 fills the
+    # window exactly, r2 is window-only, r3's second token is padding.
+    q_lens = [3, 3, 1, 2]
+    seq_lens = torch.tensor([1025, 130, 5, 300], dtype=torch.int32)
+    R_ = len(q_lens)
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32)
+    T = int(qsl[-1])
+    t2r = torch.repeat_interleave(torch.arange(R_, dtype=torch.int32), torch.tensor(q_lens))
+    positions = torch.cat([torch.arange(int(s) - q, int(s)) for s, q in zip(seq_lens, q_lens)]).to(torch.int64)
+    n_swa_pages, n_comp_pages = 24, 8
+    swa_bt = torch.stack([torch.randperm(n_swa_pages, generator=g)[:17] for _ in range(R_)]).to(torch.int32)
+    comp_bt = torch.stack([torch.randperm(n_comp_pages, generator=g)[:8] for _ in range(R_)]).to(torch.int32)
+    slot_mapping = swa_bt[t2r.long(), positions // swa_page].long() * swa_page + positions % swa_page
+    slot_mapping[T - 1] = -1  # padding token
+    is_valid = slot_mapping >= 0
+    swa_idx = torch.full((T, 1, W), -1, dtype=torch.int32)
+    swa_lens = torch.zeros(T, dtype=torch.int32)
+    _compute_swa_indices_and_lens_kernel[(T,)](
+        swa_idx, swa_idx.stride(0), swa_lens, W, qsl, seq_lens, t2r, is_valid, swa_bt,
+        swa_bt.stride(0), swa_page, TRITON_BLOCK_SIZE=1024)
+    gdec = torch.full((T, maxc), -1, dtype=torch.int32)
+    dlens = torch.zeros(T, dtype=torch.int32)
+    plocal = torch.full((1, maxc), -1, dtype=torch.int32)
+    build_c128a_topk_metadata(positions, ratio, T, t2r, comp_bt, comp_page, slot_mapping, gdec, dlens,
+                              plocal, max_compressed_tokens=maxc)
+    swa_raw, comp_raw = caches(n_swa_pages, n_comp_pages)
+    sidx = swa_idx[:, 0].numpy()
+    _fill_rows(swa_raw, np.concatenate([sidx[t, : int(swa_lens[t])] for t in range(T)]), swa_page, g)
+    gd = gdec.numpy()
+    _fill_rows(comp_raw, np.concatenate([gd[t, : int(dlens[t])] for t in range(T)]), comp_page, g)
+    q = torch.randn(T, H, D, generator=g).bfloat16()
+
+    main_i, main_p = ra.build_ragged_indices_from_dense(swa_idx[:, 0], swa_lens,
+                                                        num_rows=n_swa_pages * swa_page)
+    extra_i, extra_p = ra.build_ragged_indices_from_dense(gdec, dlens, num_rows=n_comp_pages * comp_page)
+    main_cache, extra_cache = as_pages(swa_raw, swa_page), as_pages(comp_raw, comp_page)
+    outs = {}
+    for name, sink in sinks.items():
+        out = torch.empty(T, H, D, dtype=torch.bfloat16)
+        ra._sparse_attn_decode_ragged_kernel[(T, triton_cdiv(H, 16))](
+            q, main_cache, main_i, main_p, extra_cache, extra_i, extra_p,
+            sink if sink is not None else torch.empty(1), out,
+            q.stride(0), q.stride(1), out.stride(0), out.stride(1),
+            main_cache.stride(0), extra_cache.stride(0),
+            main_cache.shape[0] * main_cache.shape[1], extra_cache.shape[0] * extra_cache.shape[1],
+            main_cache.shape[1], extra_cache.shape[1], scale, H,
+            HAS_ATTN_SINK=sink is not None, HAS_EXTRA=True, NOPE_DIM=NOPE, NOPE_BLOCK=512,
+            ROPE_DIM=R, IS_FNUZ=False, BLOCK_H=16, BLOCK_K=16, num_warps=8)
+        outs[f"out_{name}"] = _bf16_bits(out)
+    save("sparse_decode_d512", q=_bf16_bits(q), positions=positions, query_start_loc=qsl,
+         seq_lens=seq_lens, swa_block_table=swa_bt, comp_block_table=comp_bt, slot_mapping=slot_mapping,
+         swa_indices=swa_idx[:, 0], swa_lens=swa_lens, comp_indices=gdec, comp_lens=dlens,
+         swa_cache=swa_raw, comp_cache=comp_raw, sink=sinks["random"], scale=np.float64(scale), **outs)
+
+    # ---------------- prefill: 3 chunks, window-only / boundary-crossing ----
+    chunks = [(0, 6), (1020, 6), (380, 5)]  # (prior context, chunk tokens)
+    q_lens = [c for _, c in chunks]
+    seq_lens = torch.tensor([p + c for p, c in chunks], dtype=torch.int32)
+    R_ = len(chunks)
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32)
+    T = int(qsl[-1])
+    t2r = torch.repeat_interleave(torch.arange(R_, dtype=torch.int32), torch.tensor(q_lens))
+    positions = torch.cat([torch.arange(int(s) - q, int(s)) for s, q in zip(seq_lens, q_lens)]).to(torch.int64)
+    swa_bt = torch.stack([torch.randperm(n_swa_pages, generator=g)[:17] for _ in range(R_)]).to(torch.int32)
+    comp_bt = torch.stack([torch.randperm(n_comp_pages, generator=g)[:8] for _ in range(R_)]).to(torch.int32)
+    slot_mapping = swa_bt[t2r.long(), positions // swa_page].long() * swa_page + positions % swa_page
+    gather_lens = torch.empty(R_, dtype=torch.int32)
+    _compute_prefill_metadata_kernel[(1,)](gather_lens, seq_lens, qsl, R_, 0, W, BLOCK_SIZE=4)
+    gdec = torch.full((1, maxc), -1, dtype=torch.int32)
+    dlens = torch.zeros(1, dtype=torch.int32)
+    plocal = torch.full((T, maxc), -1, dtype=torch.int32)
+    build_c128a_topk_metadata(positions, ratio, 0, t2r, comp_bt, comp_page, slot_mapping, gdec, dlens,
+                              plocal, max_compressed_tokens=maxc)
+    swa_raw, comp_raw = caches(n_swa_pages, n_comp_pages)
+    # rows the gather reads: the last gather_len positions of each request,
+    # and every compressed entry below seq_len // ratio
+    wslots, cslots = [], []
+    for r in range(R_):
+        s, gl = int(seq_lens[r]), int(gather_lens[r])
+        pos = np.arange(s - gl, s)
+        wslots.append(swa_bt[r].numpy()[pos // swa_page].astype(np.int64) * swa_page + pos % swa_page)
+        ce = np.arange(s // ratio)
+        cslots.append(comp_bt[r].numpy()[ce // comp_page].astype(np.int64) * comp_page + ce % comp_page)
+    _fill_rows(swa_raw, np.concatenate(wslots), swa_page, g)
+    _fill_rows(comp_raw, np.concatenate(cslots), comp_page, g)
+    q = torch.randn(T, H, D, generator=g).bfloat16()
+    N = maxc
+    M = N + W + T
+    kv = torch.zeros(R_, M, D, dtype=torch.bfloat16)
+    dequantize_and_gather_k_cache_triton(kv, as_pages(comp_raw, comp_page), seq_lens // ratio, None, comp_bt,
+                                         comp_page, offset=0)
+    dequantize_and_gather_k_cache_triton(kv, as_pages(swa_raw, swa_page), seq_lens, gather_lens, swa_bt,
+                                         swa_page, offset=N)
+    comb, comb_lens = combine_topk_swa_indices(plocal, qsl, seq_lens, gather_lens, W, ratio, maxc, M, N)
+    rag_i, rag_p = ra.build_ragged_indices_from_dense(comb, comb_lens, num_rows=R_ * M)
+    kv2 = kv.view(-1, D)
+    outs = {}
+    for name, sink in sinks.items():
+        out = torch.empty(T, H, D, dtype=torch.bfloat16)
+        ra._sparse_attn_prefill_ragged_kernel[(T, triton_cdiv(H, 16))](
+            q, kv2, rag_i, rag_p, sink if sink is not None else torch.empty(1), out,
+            q.stride(0), q.stride(1), q.stride(2), kv2.stride(0), kv2.stride(1),
+            out.stride(0), out.stride(1), out.stride(2), H, D, kv2.shape[0], scale,
+            HAS_ATTN_SINK=sink is not None, BLOCK_H=16, BLOCK_D=512, BLOCK_K=16, num_warps=8)
+        outs[f"out_{name}"] = _bf16_bits(out)
+    save("sparse_prefill_d512", q=_bf16_bits(q), positions=positions, query_start_loc=qsl, seq_lens=seq_lens,
+         token_to_req=t2r, swa_block_table=swa_bt, comp_block_table=comp_bt, gather_lens=gather_lens,
+         combined=comb, combined_lens=comb_lens, swa_cache=swa_raw, comp_cache=comp_raw,
+         sink=sinks["random"], scale=np.float64(scale), **outs)
+
+
+def triton_cdiv(a: int, b: int) -> int:
+    return (a + b - 1) // b
+
+
 def main() -> None:
     patch_interpreter()
     g = torch.Generator().manual_seed(0)
-    which = sys.argv[1:] or ["insert", "compressor", "metadata", "output"]
+    which = sys.argv[1:] or ["insert", "compressor", "metadata", "output", "attention"]
     if "insert" in which:
         gen_insert_and_gather(g)
     if "compressor" in which:
@@ -342,6 +532,8 @@ def main() -> None:
         gen_metadata(g)
     if "output" in which:
         gen_norm_and_output(g)
+    if "attention" in which:
+        gen_attention()
 
 
 if __name__ == "__main__":

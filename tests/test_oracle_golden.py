@@ -169,3 +169,73 @@ def test_layer_oracle_emulated_vs_exact():
     ex = HCALayerOracle(shape, w, max_len=1152, num_reqs=2, emulate_quant=False).forward(h, qsl, sl)
     assert np.isfinite(em).all() and np.isfinite(ex).all()
     assert np.linalg.norm(em - ex) / np.linalg.norm(ex) < 5e-2
+
+
+def bf16_bits_to_f32(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+# The attention fixtures run vLLM's readable DeepSeek-V4 sparse attention
+# (rocm_aiter_mla_sparse.py, Triton) in fp32 with bf16 P and a bf16 output;
+# the oracle evaluates in fp64.  Parity bar for the attention output:
+ATTN_MAX_ABS, ATTN_MAX_REL_L2 = 2e-2, 5e-3
+
+
+def _check_attn(ours: np.ndarray, ref: np.ndarray) -> None:
+    assert np.isfinite(ours).all() and np.isfinite(ref).all()
+    err = np.abs(ours.astype(np.float64) - ref)
+    rel = np.linalg.norm(ours.astype(np.float64) - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert err.max() <= ATTN_MAX_ABS and rel <= ATTN_MAX_REL_L2, (err.max(), rel)
+
+
+def test_decode_attention_index_tables_match_reference():
+    """The decode fixture's window and compressed index tables, rebuilt by
+    the oracle's builders (bit-exact)."""
+    g = load("sparse_decode_d512")
+    qsl, seq_lens = g["query_start_loc"], g["seq_lens"]
+    T = int(qsl[-1])
+    t2r = M.token_to_req_indices(qsl)
+    idx = np.full((T, 128), -1, np.int32)
+    lens = np.zeros(T, np.int32)
+    M.swa_indices_and_lens(T, 128, qsl, seq_lens, t2r, g["slot_mapping"] >= 0, g["swa_block_table"], 64,
+                           idx, lens)
+    assert np.array_equal(lens, g["swa_lens"]) and np.array_equal(idx, g["swa_indices"])
+    gd = np.full((T, 128), -1, np.int32)
+    dl = np.zeros(T, np.int32)
+    M.c128a_topk_metadata(g["positions"], 128, T, t2r, g["comp_block_table"], 2, g["slot_mapping"], gd, dl,
+                          np.zeros((1, 128), np.int32), 128)
+    assert np.array_equal(dl, g["comp_lens"]) and np.array_equal(gd, g["comp_indices"])
+    # the cases the fixture is meant to hold
+    assert (g["swa_lens"] == 0).any() and (g["comp_lens"] == 0).any() and g["swa_lens"].max() == 128
+    assert len(set(g["comp_lens"][:3].tolist())) == 2  # a compression boundary between MTP tokens
+
+
+@pytest.mark.parametrize("sink", ["random", "neginf", "none"])
+def test_oracle_sparse_decode_matches_reference_kernel(sink):
+    from oracle import attention as A
+
+    g = load("sparse_decode_d512")
+    q = bf16_bits_to_f32(g["q"])
+    sk = {"random": g["sink"], "neginf": np.full_like(g["sink"], -np.inf), "none": None}[sink]
+    ours = A.sparse_decode(q, g["swa_cache"], 64, g["swa_indices"], g["swa_lens"], g["comp_cache"], 2,
+                           g["comp_indices"], g["comp_lens"], float(g["scale"]), sk, D, R)
+    ref = bf16_bits_to_f32(g[f"out_{sink}"])
+    _check_attn(ours, ref)
+    empty = g["swa_lens"] == 0
+    assert np.array_equal(ref[empty], np.zeros_like(ref[empty]))
+
+
+@pytest.mark.parametrize("sink", ["random", "neginf", "none"])
+def test_oracle_sparse_prefill_matches_reference_kernel(sink):
+    """The oracle's prefill straight on the paged caches against the
+    reference's gather-workspace pipeline (dequant gather, combined
+    indices, sparse prefill kernel)."""
+    from oracle import attention as A
+
+    g = load("sparse_prefill_d512")
+    q = bf16_bits_to_f32(g["q"])
+    sk = {"random": g["sink"], "neginf": np.full_like(g["sink"], -np.inf), "none": None}[sink]
+    ours = A.sparse_prefill_paged(q, g["positions"], g["token_to_req"], g["swa_cache"], 64,
+                                  g["swa_block_table"], g["comp_cache"], 2, g["comp_block_table"], 128, 128,
+                                  float(g["scale"]), sk, D, R)
+    _check_attn(ours, bf16_bits_to_f32(g[f"out_{sink}"]))
