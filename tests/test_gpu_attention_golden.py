@@ -65,10 +65,16 @@ def test_decode_d512_matches_reference_kernel(sink, layout):
     if layout == "per_token_2_splits":
         kw = dict(num_splits=2)
     else:
-        qsl = _t(g["query_start_loc"])
+        # a request's consecutive tokens share a group; a group is all valid
+        # tokens or all padding (the entry points' contract), so the padding
+        # token of the last request forms its own group
+        qsl = g["query_start_loc"]
+        starts = np.concatenate([qsl[:-1], [qsl[-1] - 1, qsl[-1]]]).astype(np.int32)
+        assert g["swa_lens"][starts[-2]] == 0 and (g["swa_lens"][:starts[-2]] > 0).all()
+        gs = _t(starts)
         max_items = 16
-        sched = ops.decode_schedule(qsl, q.shape[0], sl, cl, max_items)
-        kw = dict(group_starts=qsl, max_group_tokens=int(np.diff(g["query_start_loc"]).max()), schedule=sched,
+        sched = ops.decode_schedule(gs, q.shape[0], sl, cl, max_items, head_dim=D)
+        kw = dict(group_starts=gs, max_group_tokens=int(np.diff(starts).max()), schedule=sched,
                   max_items=max_items)
     out = ops.sparse_decode(q, swa, 64, si, sl, comp, 2, ci, cl, float(g["scale"]), _sink(g, sink), **kw)
     torch.cuda.synchronize()

@@ -233,6 +233,14 @@ def decode_prep(q, kv, kv_score, ape, positions, cos_sin_cache, swa_kv_cache, sw
 # ---------------------------------------------------------------------------
 
 
+def set_attention_wait_limit_ns(limit_ns: int) -> None:
+    """Limit of every mbarrier wait of the head_dim-128 attention kernel for
+    launches made from now on (``< 0``: the default 2 s; ``0``: a wait not
+    already satisfied fails at once).  A diagnostic for testing the bounded
+    waits; it has no counterpart in the reference."""
+    call("hca_set_attention_wait_limit_ns", int(limit_ns))
+
+
 def device_error(clear: bool = True) -> int:
     """The library's device error word (non-zero if a kernel gave up on a
     bounded wait); synchronous."""
@@ -260,11 +268,13 @@ class DecodeWorkspace:
 _WS = DecodeWorkspace()
 
 
-def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_items: int, out=None):
+def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_items: int, out=None,
+                    head_dim: int = 128):
     """Per-step decode work list (the role of FlashMLA's ``get_mla_metadata``
     tile-scheduler metadata): ``int32[hca_decode_schedule_ints]``, valid for
     every layer of the step.  ``max_items`` = one wave of CTAs (the SM count,
-    at least the number of groups)."""
+    at least the number of groups); ``head_dim`` selects the attention kernel
+    whose chunk size the list counts in (a list is refused by the other)."""
     _check_cuda(swa_lens)
     num_groups = num_tokens if group_starts is None else group_starts.numel() - 1
     n = lib().hca_decode_schedule_ints(num_groups, max_items)
@@ -273,7 +283,7 @@ def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_item
     if out is None or out.numel() != n:
         out = torch.empty(n, dtype=torch.int32, device=swa_lens.device)
     call("hca_decode_schedule", _p(out), max_items, _p(group_starts), num_groups, num_tokens, _p(swa_lens),
-         _p(comp_lens), _s())
+         _p(comp_lens), head_dim, _s())
     return out
 
 
