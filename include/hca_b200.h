@@ -45,8 +45,7 @@ int hca_version(void);
 /* Device error word of the current device (synchronous read): non-zero if a
  * kernel gave up on a bounded wait (bit 0 loader, 1 dequant, 2 MMA, 3
  * softmax of hca_sparse_decode; bit 4 the streamed many-token path of
- * hca_qnorm_rope_kv_insert, bit 5 that of hca_vha_inv_rope_fp8_quant; bit 6
- * a decode work list built for another head_dim).
+ * hca_qnorm_rope_kv_insert, bit 5 that of hca_vha_inv_rope_fp8_quant).
  * clear != 0 resets it to zero. */
 int hca_device_error(int32_t* value, int32_t clear);
 
@@ -249,20 +248,17 @@ int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_stride_head
  * V/models/deepseek_v4/nvidia/flashmla.py:210-302 and
  * V/v1/attention/backends/mla/flashmla_sparse.py:565-687).  Group g's union
  * rows (window of its first token + tail of its last token + the last
- * token's compressed rows) make c_g chunks of the attention kernel for
- * head_dim (128 rows at head_dim 128, 64 at 512); the smallest per-CTA chunk
+ * token's compressed rows) make c_g chunks of 64; the smallest per-CTA chunk
  * budget whose CTA count fits max_items (at most 16 CTAs per group, at least
  * one) is chosen, so the longest CTA of one wave is as short as possible.
  * schedule: int32[hca_decode_schedule_ints(num_groups, max_items)], 16-byte
  * aligned; max_items >= num_groups (one wave = the SM count).  group_starts
  * as for hca_sparse_decode (NULL: one token per group, num_groups = tokens);
- * comp_lens NULL = no compressed rows.  The last int records the chunk size:
- * a decode launch of another head_dim refuses the list (device error bit 6)
- * and writes nothing.  Valid for every layer of the step. */
+ * comp_lens NULL = no compressed rows.  Valid for every layer of the step. */
 int64_t hca_decode_schedule_ints(int32_t num_groups, int32_t max_items);
 int hca_decode_schedule(int32_t* schedule, int32_t max_items, const int32_t* group_starts,
                         int32_t num_groups, int32_t num_tokens, const int32_t* swa_lens,
-                        const int32_t* comp_lens, int32_t head_dim, void* stream);
+                        const int32_t* comp_lens, void* stream);
 
 /* Limit, in ns, of every mbarrier wait of the head_dim-128 attention kernel
  * for launches made from now on in this process (default 2e9; < 0 restores

@@ -73,7 +73,7 @@ def test_decode_d512_matches_reference_kernel(sink, layout):
         assert g["swa_lens"][starts[-2]] == 0 and (g["swa_lens"][:starts[-2]] > 0).all()
         gs = _t(starts)
         max_items = 16
-        sched = ops.decode_schedule(gs, q.shape[0], sl, cl, max_items, head_dim=D)
+        sched = ops.decode_schedule(gs, q.shape[0], sl, cl, max_items)
         kw = dict(group_starts=gs, max_group_tokens=int(np.diff(starts).max()), schedule=sched,
                   max_items=max_items)
     out = ops.sparse_decode(q, swa, 64, si, sl, comp, 2, ci, cl, float(g["scale"]), _sink(g, sink), **kw)

@@ -634,175 +634,90 @@ __device__ __forceinline__ void vha_mix_quant_token(const AttnParams& P, const V
 }
 
 // ============================================================================
-// tcgen05 attention kernel (head_dim 128 = 64 e4m3 NoPE + 64 bf16 RoPE), for
-// decode (a group's chunk range) and chunked prefill (a tile of tokens).
+// tcgen05 decode kernel (head_dim 128 = 64 e4m3 NoPE + 64 bf16 RoPE)
 //
-// One CTA per work item, up to 256 query rows = two M=128 tiles.  KV rows
-// stream in chunks of 128, the N of the S MMA: an M128 N128 K16 MMA costs the
-// tensor pipe as long as an M128 N64 one (measured on B200: ~66 cycles each),
-// so wider S tiles double its useful rate.
-//   warps 0-7  softmax: tile t = warp / 4, TMEM lane quadrant = warp % 4
+// One CTA per (group, split); up to 256 query rows = two M=128 tiles.
+//   warps 0-7  softmax: tile t = warp / 4, TMEM lane quadrant = warp % 4,
+//              one thread per query row (S row read from TMEM, P written back)
 //   warp  8    MMA issuer (lane 0) + TMEM owner
-//   warps 9-10 producers: warp w owns rows 64 w .. 64 w + 63 of every chunk,
-//              two rows per lane (slot resolution, scale, token mask,
-//              dequantisation).  The gather is 16-byte cp.async with
-//              consecutive lanes on consecutive pieces of a row: the bf16
-//              RoPE half lands straight in the 128B-swizzled K tile, the e4m3
-//              NoPE half and the row's scale block in a raw stage that the
-//              row's lane then dequantises (e4m3 x UE8M0 -> bf16) into the
-//              K tile.  kKBufs chunks are in flight.
-// S = Q K^T: M=128, N=128, K=128 (8 x K16), Q and K tile K-major in smem.
-// O += P V: M=128, N=128, K=128 (8 x K16), P from TMEM, V = the same K tile
-// read MN-major.  TMEM: O of tile t at columns 128 t, S (then P, bf16 pairs)
-// of tile t at 256 + 128 t.  The MMA issue order ping-pongs the tiles,
-// S0(i) S1(i) | PV0(i) S0(i+1) | PV1(i) S1(i+1) | ..., so the tensor pipe
-// works on one tile while softmax works on the other.
-// Query rows of a tile with R rows: R > 64 puts q = ceil(R / 4) rows at the
-// start of each TMEM lane quadrant; R <= 64 puts every row in two lanes of a
-// quadrant (ln and ln + 16), the first taking KV columns 0-63 of each chunk
-// and the second 64-127 (zeros in the other half of its P row), so the
-// exponentials of a half-full tile are spread over both lanes and all four
-// SM sub-partitions; the epilogue adds the two partial rows.
-// Softmax runs in base 2 with the row max raised lazily (O is rescaled only
-// when the max grows by more than 2^8).  Every mbarrier wait is bounded; a
-// timeout sets the device error word.
+//   warps 9-12 producers: each owns 16 of the 64 KV rows of every chunk.  It
+//              resolves their slots from the index tables, gathers the rows
+//              with 16-byte cp.async into its slice of a kStages-deep raw ring
+//              (kStages - 1 chunks in flight, completion by cp.async groups),
+//              then dequantises them (e4m3 x UE8M0 -> bf16, RoPE half copied)
+//              into the 128B-swizzled K tile.  A random-row gather is bound by
+//              the requests one SM keeps in flight, so four warps issue them.
+// S = Q K^T: M=128, N=64, K=128 (8 x K16), Q and K tile K-major in smem.
+// O += P V: M=128, N=128, K=64 (4 x K16), P from TMEM, V = the same K tile
+// read MN-major.  TMEM: O tiles at columns 0 / 128, S/P double-buffered at
+// 256 + (tile * 2 + buf) * 64.  Softmax runs in base 2 with the row max
+// raised lazily (O is rescaled only when the max grows by more than 2^8).
+// Every mbarrier wait is bounded; a timeout sets the device error word.
 // ============================================================================
 namespace tcd {
-using namespace tc;
 constexpr int kD = 128;
 constexpr int kNope = 64;
 constexpr int kRowBytes = 192;  // kNope e4m3 + 64 bf16
-constexpr int kCh = 128;        // KV rows per chunk = N of the S MMA
-constexpr int kKBufs = 3;       // chunks in flight (bf16 K tiles, raw NoPE stages)
+constexpr int kCh = 64;         // KV rows per step
+constexpr int kStages = 4;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kMmaWarp = 8;
 constexpr int kProdWarp0 = 9;
-// 11 warps: at most 3 per SM sub-partition, so a thread may hold 168
-// registers (13 warps would cap it at 128 and spill the softmax)
-constexpr int kProdWarps = 2;
-constexpr int kProdRows = kCh / kProdWarps;  // 64: rows lane and lane + 32 of a warp's slice
-constexpr int kRowsPerLane = kProdRows / 32;
+constexpr int kProdWarps = 4;
+constexpr int kProdRows = kCh / kProdWarps;  // 16 rows of each chunk per producer warp
 constexpr int kThreads = (kProdWarp0 + kProdWarps) * 32;
 constexpr int kMaxRows = 256;
-constexpr int kQRegion = 128 * 128;  // 128 rows x 64 bf16 dims (one 128-byte swizzle column)
-constexpr int kQTile = 2 * kQRegion; // dims 0-63 | 64-127
+constexpr int kQTile = 2 * 128 * 128;          // two 64-column regions of 128 rows x 128 B
+constexpr int kQRegion = 128 * 128;
 constexpr int kQOff = 0;
-constexpr int kKRegion = kCh * 128;
-constexpr int kKBuf = 2 * kKRegion;  // NoPE dims | RoPE dims
-constexpr int kKOff = kQOff + 2 * kQTile;                 // 65536
-constexpr int kRawNope = kCh * kNope;                     // e4m3 bytes of a stage (16-byte pieces swizzled by row)
-constexpr int kRawStage = kRawNope + kCh * 16;            // + the 16-byte block holding each row's scale byte
-constexpr int kRawOff = kKOff + kKBufs * kKBuf;           // 163840
-constexpr int kKMaskOff = kRawOff + kKBufs * kRawStage;   // [kbuf][token][4] 32-bit column masks
-constexpr int kKMaskWords = 32 * 4;
-constexpr int kBarOff = kKMaskOff + kKBufs * kKMaskWords * 4;
+constexpr int kKBufs = 4;                      // bf16 K-tile ring: dequant runs ahead of the MMAs
+constexpr int kKOff = kQOff + 2 * kQTile;      // 65536
+constexpr int kKRegion = kCh * 128;            // 8192
+constexpr int kKBuf = 2 * kKRegion;            // 16384
+constexpr int kRawOff = kKOff + kKBufs * kKBuf;
+// raw stage: e4m3 NoPE [64][64] | bf16 RoPE [64][128] | 16-byte scale blocks [64][16]
+constexpr int kRawNope = 0;
+constexpr int kRawRope = kCh * kNope;
+constexpr int kRawSblk = kRawRope + kCh * 128;
+constexpr int kRawStage = kRawSblk + kCh * 16;  // 13312
+constexpr int kScaleOff = kRawOff + kStages * kRawStage;  // [stage][row] byte index of the scale in its block
+constexpr int kMaskOff = kScaleOff + kStages * kCh;       // [stage][row] token mask | kOkBit
+constexpr int kKMaskOff = kMaskOff + kStages * kCh * 4;   // [kbuf][token][4] 16-bit column masks
+constexpr int kBarOff = kKMaskOff + kKBufs * kCh * 4;
 // k_full[kKBufs] k_empty[kKBufs] s_full[2] p_full[2] pv_done[2] q_full
 constexpr int kNumBars = 2 * kKBufs + 7;
 constexpr int kMiscOff = kBarOff + kNumBars * 8;
 constexpr int kTokOff = kMiscOff + 64;  // [32] + [32] ints
-constexpr int kCtxOff = kTokOff + 256;  // [16] ints: the softmax epilogue's context
-constexpr int kSmemBytes = kCtxOff + 64 + 1024;  // + 1024 alignment slack
+constexpr int kSmemBytes = kTokOff + 256 + 1024;  // + 1024 alignment slack
 constexpr int kQWarps = 9;  // softmax warps + MMA warp load Q
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOkBit = 1u << 31;
-static_assert(kMaxRows * kD * 4 <= kRawOff - kQOff, "fp32 partial staging fits in the Q and K tiles");
-static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
-__device__ __forceinline__ uint32_t s_col(int tile) { return 256u + static_cast<uint32_t>(tile) * 128u; }
+__device__ __forceinline__ uint32_t s_col(int tile, int buf) { return 256u + (tile * 2 + buf) * 64u; }
 
-// Rows in M-tile `tile`.
-__device__ __forceinline__ int tile_rows(int tile, int rows_q) { return min(128, rows_q - tile * 128); }
-
-// Query row held by TMEM lane / smem row `rit` of M-tile `tile`, or -1 (see
-// the layout note above: R > 64 rows spread q = ceil(R / 4) per quadrant,
-// R <= 64 rows in lanes ln and ln + 16 of each quadrant).
+// Query row held by TMEM lane / smem row `rit` of M-tile `tile`, or -1: a
+// tile with R valid rows puts q = ceil(R / 4) of them at the start of each
+// 32-lane quadrant.
 __device__ __forceinline__ int tile_row_to_query(int tile, int rit, int rows_q) {
-  const int R = tile_rows(tile, rows_q);
+  const int R = min(128, rows_q - tile * 128);
   if (R <= 0) return -1;
   const int q = (R + 3) >> 2;
-  const int quad = rit >> 5;
-  const int ln = R <= 64 ? (rit & 15) : (rit & 31);
+  const int quad = rit >> 5, ln = rit & 31;
   const int local = quad * q + ln;
   return (ln < q && local < R) ? tile * 128 + local : -1;
 }
 
 // Lane quadrants (softmax warps) of M-tile `tile` that hold query rows.
 __device__ __forceinline__ int active_quads(int tile, int rows_q) {
-  const int R = tile_rows(tile, rows_q);
+  const int R = min(128, rows_q - tile * 128);
   if (R <= 0) return 0;
   const int q = (R + 3) >> 2;
   return (R + q - 1) / q;
 }
 
-// Offset of 16-byte NoPE piece j (0-3) of row r in a raw stage: pieces are
-// XOR-swizzled so the row-per-lane reads of the dequantisation are
-// bank-conflict free.
-__device__ __forceinline__ int raw_nope_off(int r, int j) { return r * kNope + ((j ^ ((r >> 1) & 3)) << 4); }
-
 __device__ __forceinline__ void report(int* err, uint32_t* s_err, int code) {
   *s_err = 1;
   if (err) atomicOr(err, code);
-}
-
-// Row max of 64 S values (as bits) with a tree of 3-input maxima.
-__device__ __forceinline__ float max64(const uint32_t* sr) {
-  float m8[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    m8[k] = fmax3(__uint_as_float(sr[k]), __uint_as_float(sr[k + 8]), __uint_as_float(sr[k + 16]));
-#pragma unroll
-  for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 24]), __uint_as_float(sr[k + 32]));
-#pragma unroll
-  for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 40]), __uint_as_float(sr[k + 48]));
-#pragma unroll
-  for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(sr[k + 56]));
-  return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
-}
-
-// Columns whose bit is clear in (lo, hi) become -inf: they drop out of the
-// max and 2^-inf = 0.
-__device__ __forceinline__ void mask64(uint32_t* sr, uint32_t lo, uint32_t hi) {
-  if ((lo & hi) == 0xffffffffu) return;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    sr[j] = ((lo >> j) & 1u) ? sr[j] : 0xff800000u;
-    sr[32 + j] = ((hi >> j) & 1u) ? sr[32 + j] : 0xff800000u;
-  }
-}
-
-// 2^x of a pair on the FMA pipe, for the share of the exponentials taken
-// off the SFU (which also does the bf16 conversions and bounds the softmax):
-// x is clamped to >= -127 (a masked -inf gives exactly 0), rounded to the
-// integer n by adding 1.5 * 2^23 (n lands in the low mantissa bits), and
-// 2^(x - n), x - n in [-0.5, 0.5], is a cubic with value 1 at 0 whose
-// coefficients were fitted to minimise the relative error on that interval
-// (max 1.0e-4, well below a bf16 P's 2^-9); n is added to the exponent
-// field as an integer.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -127.0f);
-  x.y = fmaxf(x.y, -127.0f);
-  const float2 t = add2(x, make_float2(12582912.0f, 12582912.0f));
-  const float2 n = add2(t, make_float2(-12582912.0f, -12582912.0f));
-  const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
-  float2 p = fma2(make_float2(5.500872806e-02f, 5.500872806e-02f), f, make_float2(2.422107160e-01f, 2.422107160e-01f));
-  p = fma2(p, f, make_float2(6.932829022e-01f, 6.932829022e-01f));
-  p = fma2(p, f, make_float2(1.0f, 1.0f));
-  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
-}
-
-// P = 2^(s * scale - m) of 32 S values as 16 bf16 pairs (in place, sr[0..15]);
-// exponents by packed FMAs, a quarter of them by the FMA-pipe polynomial and
-// the rest by the SFU, the row sum added into acc.
-__device__ __forceinline__ void exp32(uint32_t* sr, float scale, float nb, float2* acc) {
-  const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(nb, nb);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const float2 x = fma2(make_float2(__uint_as_float(sr[2 * j]), __uint_as_float(sr[2 * j + 1])), sc2, nb2);
-    const float2 p2 = ((j * 5) % 16) < 4 ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
-    acc[j & 3] = add2(acc[j & 3], p2);
-    sr[j] = pack_bf16(p2.x, p2.y);
-  }
 }
 }  // namespace tcd
 
@@ -833,10 +748,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     single = true;
   } else if (P.sched) {
     const int4 it = reinterpret_cast<const int4*>(P.sched)[blockIdx.x];
-    // a work list built for another kernel's chunk size is refused
-    const int unit = P.sched[4 * P.sched_items + 2 * P.sched_groups];
-    if (it.x < 0 || unit != kCh) {
-      if (unit != kCh && threadIdx.x == 0 && err) atomicOr(err, 64);
+    if (it.x < 0) {
       pdl_wait();
       return;
     }
@@ -883,7 +795,10 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
   uint64_t* pv_done = p_full + 2;
   uint64_t* q_full = pv_done + 2;
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kMiscOff);  // [0] tmem, [1] err
+  uint8_t* scale_s = smem + kScaleOff;
+  uint32_t* mask_s = reinterpret_cast<uint32_t*>(smem + kMaskOff);
   uint32_t* kmask = reinterpret_cast<uint32_t*>(smem + kKMaskOff);
+
   int* tok_len = reinterpret_cast<int*>(smem + kTokOff);  // [32] window length per token
   int* tok_clen = tok_len + 32;                             // [32] compressed length per token
 
@@ -897,10 +812,10 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
       mbar_init(k_full + b, kProdWarps);
       mbar_init(k_empty + b, 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(s_full + t, 1);
-      mbar_init(p_full + t, t == 0 ? (act0 > 0 ? act0 : 1) : (act1 > 0 ? act1 : 1));
-      mbar_init(pv_done + t, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full + b, 1);
+      mbar_init(p_full + b, nact);  // one arrival per softmax warp with rows
+      mbar_init(pv_done + b, 1);
     }
     mbar_init(q_full, kQWarps * 32 + kQWarps);  // per-thread cp.async completions + one arrival per warp
     misc[1] = 0;
@@ -910,29 +825,22 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     tok_len[threadIdx.x] = P.swa_lens[G.t0 + threadIdx.x];
     tok_clen[threadIdx.x] = P.comp_cache ? P.comp_lens[G.t0 + threadIdx.x] : 0;
   }
-  // what only the softmax epilogue needs, read back after its loop so it
-  // holds no registers across it
-  int* ectx = reinterpret_cast<int*>(smem + kCtxOff);
-  if (threadIdx.x == 32) {
-    ectx[0] = single;
-    ectx[1] = static_cast<int>(item);
-    ectx[2] = static_cast<int>(item >> 32);
-    ectx[3] = G.t0;
-  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
 
   if (warp < kSoftmaxWarps || warp == kMmaWarp) {
     pdl_wait();  // Q was written by an earlier kernel of this layer
-    // Q rows -> K-major 128B-swizzled M=128 tiles in the lane layout above
-    // (rows not held zero), loaded by the softmax and MMA warps while the
-    // producers already stream KV.  Valid rows arrive by cp.async (all in
-    // flight at once, completion counted on q_full); padding rows are zeroed
-    // with plain stores.
+    // Q rows -> two K-major 128B-swizzled M=128 tiles (rows past rows_q zero),
+    // loaded by the softmax and MMA warps while the loader already streams KV.
+    // A tile with R < 128 query rows spreads them evenly over the four TMEM
+    // lane quadrants (q = ceil(R / 4) rows each) so every SM sub-partition
+    // runs the same softmax load.
+    // Valid rows arrive by cp.async (all copies in flight at once, completion
+    // counted on q_full); padding rows are zeroed with plain stores.
     const int qt = warp < kSoftmaxWarps ? threadIdx.x : kSoftmaxWarps * 32 + lane;
-    for (int it = qt; it < ntiles * 128 * (kD / 8); it += kQWarps * 32) {
-      const int row = it >> 4, ch = it & 15;
+    for (int item = qt; item < ntiles * 128 * (kD / 8); item += kQWarps * 32) {
+      const int row = item >> 4, ch = item & 15;
       const int tile = row >> 7, rit = row & 127, region = ch >> 3, c8 = ch & 7;
       const int r = tile_row_to_query(tile, rit, rows_q);
       uint8_t* dst = smem + kQOff + tile * kQTile + region * kQRegion + rit * 128 + ((c8 ^ (rit & 7)) << 4);
@@ -951,191 +859,166 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
 
   if (warp >= kProdWarp0) {
     // -------------------------------------------------------------- producer
-    const int pw = warp - kProdWarp0;
-    // Slot, token mask and cache of one row of a chunk.
-    struct Res {
+    const int row0 = (warp - kProdWarp0) * kProdRows;  // this warp's rows of every chunk
+    // Slot, token mask and cache of row row0 + lane (lanes < kProdRows) of
+    // chunk c, from the index tables; the per-token lengths deciding the mask
+    // are in shared memory.
+    struct Resolved {
       int64_t slot;
       uint32_t mask;
       bool comp;
     };
-    // this lane's rows of chunk c: pw * 64 + lane + 32 h
-    auto resolve = [&](int c, Res* R) {
-#pragma unroll
-      for (int h = 0; h < kRowsPerLane; ++h) {
-        const int u = c * kCh + pw * kProdRows + h * 32 + lane;
-        R[h].slot = -1;
-        R[h].mask = 0;
-        R[h].comp = false;
-        if (u >= n_u) continue;
-        if (kPrefill) {
+    auto resolve = [&](int c, Resolved& R) {
+      const int u = c * kCh + row0 + lane;
+      R.slot = -1;
+      R.mask = 0;
+      R.comp = false;
+      if (kPrefill) {
+        // positions: window row u is position win_start + u, compressed row
+        // u - n_win is entry u - n_win; slots through the block tables
+        if (lane < kProdRows && u < n_u) {
           bool comp;
           int64_t slot;
           uint32_t m;
           row_source<true>(P, G, u, comp, slot, m);
-          R[h].slot = slot;
-          R[h].comp = comp;
-          R[h].mask = m;
-        } else {
-          uint32_t m = 0;
-          if (u < G.n_win) {
-            R[h].slot = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
-                                   : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
-            for (int k = 0; k < G.ntok; ++k) {
-              const int lk = tok_len[k];
-              if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) m |= 1u << k;
-            }
-          } else {
-            const int ci = u - G.n_win;
-            R[h].slot = P.comp_idx[G.last_tok * P.comp_idx_st + ci];
-            R[h].comp = true;
-            for (int k = 0; k < G.ntok; ++k)
-              if (ci < tok_clen[k]) m |= 1u << k;
-          }
-          R[h].mask = m;
+          R.slot = slot;
+          R.comp = comp;
+          R.mask = m;
         }
+      } else if (lane < kProdRows && u < n_u) {
+        uint32_t m = 0;
+        if (u < G.n_win) {
+          R.slot = u < G.len0 ? P.swa_idx[G.first_tok * P.swa_idx_st + u]
+                              : P.swa_idx[G.last_tok * P.swa_idx_st + (G.len_last - (G.n_win - u))];
+          for (int k = 0; k < G.ntok; ++k) {
+            const int lk = tok_len[k];
+            if (lk > 0 && u >= k + G.len0 - lk && u <= k + G.len0 - 1) m |= 1u << k;
+          }
+        } else {
+          const int ci = u - G.n_win;
+          R.slot = P.comp_idx[G.last_tok * P.comp_idx_st + ci];
+          R.comp = true;
+          for (int k = 0; k < G.ntok; ++k)
+            if (ci < tok_clen[k]) m |= 1u << k;
+        }
+        R.mask = m;
       }
     };
-    // Gather local chunk i (this lane's rows resolved in R) into K buffer /
-    // raw stage i % kKBufs and close one cp.async group; past the last chunk
-    // an empty group keeps the count uniform.  sb[h] gets the row's scale
-    // byte index within its 16-byte scale block.
-    auto issue = [&](int i, const Res* R, uint32_t* sb) {
+    // Gather this warp's rows of local chunk i into raw stage i % kStages and
+    // close one cp.async group (an empty group past the last chunk keeps the
+    // group count uniform).
+    auto issue = [&](int i, const Resolved& R) {
       if (i < n) {
-        const int s = i % kKBufs;
+        const int s = i % kStages;
         uint8_t* const stage = smem + kRawOff + s * kRawStage;
-        uint8_t* const kt = smem + kKOff + s * kKBuf;
+        const int row = row0 + lane;
+        // Row addresses in 32-bit slot arithmetic: a slot is below 2^31 in
+        // any cache that fits in device memory (every row takes > 64 bytes).
+        const bool ok = R.slot >= 0;
+        uint64_t rbase = 0;
+        if (ok) {
+          const uint32_t sl = static_cast<uint32_t>(R.slot);
+          const uint32_t psz = R.comp ? static_cast<uint32_t>(P.comp_page) : static_cast<uint32_t>(P.swa_page);
+          const uint32_t page = sl / psz, off = sl - page * psz;
+          const uint8_t* base =
+              (R.comp ? P.comp_cache : P.swa_cache) + static_cast<int64_t>(page) * (R.comp ? P.comp_pstride : P.swa_pstride);
+          rbase = reinterpret_cast<uint64_t>(base + off * kRowBytes);
+          const uintptr_t sa = reinterpret_cast<uintptr_t>(base + psz * kRowBytes + off * (kNope / kQuantBlock + 1));
+          cp_async16(stage + kRawSblk + row * 16, reinterpret_cast<const void*>(sa & ~uintptr_t(15)));
+          scale_s[s * kCh + row] = static_cast<uint8_t>(sa & 15);
+        }
+        if (lane < kProdRows) mask_s[s * kCh + row] = ok ? (R.mask | kOkBit) : 0u;
+        // 12 pieces of 16 bytes per row, consecutive lanes on consecutive
+        // pieces (a cp.async instruction touches ~3 rows); pieces 0-3 are the
+        // e4m3 NoPE bytes, 4-11 the bf16 RoPE half.
 #pragma unroll
-        for (int h = 0; h < kRowsPerLane; ++h) {
-          const int row = pw * kProdRows + h * 32 + lane;
-          // Row addresses in 32-bit slot arithmetic: a slot is below 2^31 in
-          // any cache that fits in device memory (every row takes > 64 bytes).
-          uint64_t rbase = 0;
-          sb[h] = 0;
-          if (R[h].slot >= 0) {
-            const uint32_t sl = static_cast<uint32_t>(R[h].slot);
-            const uint32_t psz = R[h].comp ? static_cast<uint32_t>(P.comp_page) : static_cast<uint32_t>(P.swa_page);
-            const uint32_t page = sl / psz, off = sl - page * psz;
-            const uint8_t* base = (R[h].comp ? P.comp_cache : P.swa_cache) +
-                                  static_cast<int64_t>(page) * (R[h].comp ? P.comp_pstride : P.swa_pstride);
-            rbase = reinterpret_cast<uint64_t>(base + off * kRowBytes);
-            const uintptr_t sa = reinterpret_cast<uintptr_t>(base + psz * kRowBytes + off * (kNope / kQuantBlock + 1));
-            cp_async16(stage + kRawNope + row * 16, reinterpret_cast<const void*>(sa & ~uintptr_t(15)));
-            sb[h] = static_cast<uint32_t>(sa & 15);
-          }
-          // 12 pieces of 16 bytes per row for the warp's 32 rows of this
-          // half, consecutive lanes on consecutive pieces (a cp.async
-          // instruction touches ~3 rows); pieces 0-3 are the e4m3 NoPE bytes,
-          // 4-11 the bf16 RoPE half.
-#pragma unroll
-          for (int k = 0; k < 32 * (kRowBytes / 16) / 32; ++k) {
-            const int piece = k * 32 + lane;
-            const int r = piece / (kRowBytes / 16), j = piece - r * (kRowBytes / 16);
-            const uint64_t src = __shfl_sync(0xffffffffu, rbase, r);
-            const int rr = pw * kProdRows + h * 32 + r;
-            uint8_t* dst = j < 4 ? stage + raw_nope_off(rr, j) : kt + kKRegion + rr * 128 + (((j - 4) ^ (rr & 7)) << 4);
-            if (src) cp_async16(dst, reinterpret_cast<const void*>(src + j * 16));
-          }
+        for (int k = 0; k < kProdRows * (kRowBytes / 16) / 32; ++k) {
+          const int piece = k * 32 + lane;
+          const int r = piece / (kRowBytes / 16), j = piece - r * (kRowBytes / 16);
+          const uint64_t src = __shfl_sync(0xffffffffu, rbase, r);
+          uint8_t* dst = j < 4 ? stage + kRawNope + (row0 + r) * kNope + j * 16
+                               : stage + kRawRope + (row0 + r) * 128 + (j - 4) * 16;
+          if (src) cp_async16(dst, reinterpret_cast<const void*>(src + j * 16));
         }
       }
       cp_async_commit();
     };
-    // Dequantise this lane's rows of local chunk i into its K tile, publish
-    // the chunk's per-token column masks and mark the tile full.
-    auto finish = [&](int i, const Res* R, const uint32_t* sb) {
-      const int s = i % kKBufs;
+    // prologue: the first kStages - 1 chunks (index loads first, all in flight)
+    Resolved rq[kStages - 1];
+#pragma unroll
+    for (int i = 0; i < kStages - 1; ++i) {
+      rq[i].slot = -1;
+      if (i < n) resolve(c_begin + i, rq[i]);
+    }
+    pdl_wait();  // the cache rows: the kernel before may still be inserting
+#pragma unroll
+    for (int i = 0; i < kStages - 1; ++i) issue(i, rq[i]);
+    Resolved rn;  // slots of the next chunk to issue
+    rn.slot = -1;
+    if (kStages - 1 < n) resolve(c_begin + kStages - 1, rn);
+    for (int i = 0; i < n; ++i) {
+      const int s = i % kStages, b = i % kKBufs;
+      issue(i + kStages - 1, rn);
+      if (i + kStages < n) resolve(c_begin + i + kStages, rn);
+      cp_async_wait_group<kStages - 1>();  // chunk i's group has landed
+      __syncwarp();
+      if (i >= kKBufs && !mbar_wait(k_empty + b, ((i / kKBufs) - 1) & 1, wait_ns)) {
+        report(err, misc + 1, 2);
+        break;
+      }
       const uint8_t* stage = smem + kRawOff + s * kRawStage;
-      uint8_t* kt = smem + kKOff + s * kKBuf;
+      uint8_t* kt = smem + kKOff + b * kKBuf;
+      // NoPE: lane -> row row0 + lane / 2, 32 e4m3 values (half lane & 1)
+      {
+        const int r = row0 + (lane >> 1), h = lane & 1;
+        const uint32_t mask = mask_s[s * kCh + r];
+        const bool ok = (mask & kOkBit) != 0;
+        // rows that are not loaded must come out exactly zero: their smem
+        // bytes are stale (a stale scale of 255 would be inf, 0 * inf = NaN)
+        const float sc = ok ? exp2i(static_cast<int>(stage[kRawSblk + r * 16 + scale_s[s * kCh + r]]) - 127) : 0.0f;
 #pragma unroll
-      for (int h = 0; h < kRowsPerLane; ++h) {
-        const int row = pw * kProdRows + h * 32 + lane;
-        const bool ok = R[h].slot >= 0;
-        if (ok) {
-          const float sc = exp2i(static_cast<int>(stage[kRawNope + row * 16 + sb[h]]) - 127);
+        for (int q = 0; q < 2; ++q) {
+          const uint4 in = ok ? *reinterpret_cast<const uint4*>(stage + kRawNope + r * kNope + h * 32 + q * 16)
+                              : make_uint4(0, 0, 0, 0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 in = *reinterpret_cast<const uint4*>(stage + raw_nope_off(row, q));
-#pragma unroll
-            for (int w2 = 0; w2 < 2; ++w2) {
-              const uint32_t w0 = w2 ? in.z : in.x, w1 = w2 ? in.w : in.y;
-              const float2 f0 = e4m3x2_to_float2(static_cast<uint16_t>(w0 & 0xffff));
-              const float2 f1 = e4m3x2_to_float2(static_cast<uint16_t>(w0 >> 16));
-              const float2 f2 = e4m3x2_to_float2(static_cast<uint16_t>(w1 & 0xffff));
-              const float2 f3 = e4m3x2_to_float2(static_cast<uint16_t>(w1 >> 16));
-              uint4 o;
-              o.x = pack_bf16(f0.x * sc, f0.y * sc);
-              o.y = pack_bf16(f1.x * sc, f1.y * sc);
-              o.z = pack_bf16(f2.x * sc, f2.y * sc);
-              o.w = pack_bf16(f3.x * sc, f3.y * sc);
-              const int c8 = q * 2 + w2;  // 16-byte chunk of the 128-byte NoPE row
-              *reinterpret_cast<uint4*>(kt + row * 128 + ((c8 ^ (row & 7)) << 4)) = o;
-            }
-          }
-        } else {
-          // rows that are not loaded must be exactly zero in both halves:
-          // their shared memory holds stale bytes (a NaN there would give
-          // 0 * NaN = NaN in P.V)
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            *reinterpret_cast<uint4*>(kt + row * 128 + (c8 << 4)) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(kt + kKRegion + row * 128 + (c8 << 4)) = make_uint4(0, 0, 0, 0);
+          for (int w2 = 0; w2 < 2; ++w2) {
+            const uint32_t w0 = w2 ? in.z : in.x, w1 = w2 ? in.w : in.y;
+            const float2 f0 = e4m3x2_to_float2(static_cast<uint16_t>(w0 & 0xffff));
+            const float2 f1 = e4m3x2_to_float2(static_cast<uint16_t>(w0 >> 16));
+            const float2 f2 = e4m3x2_to_float2(static_cast<uint16_t>(w1 & 0xffff));
+            const float2 f3 = e4m3x2_to_float2(static_cast<uint16_t>(w1 >> 16));
+            uint4 o;
+            o.x = pack_bf16(f0.x * sc, f0.y * sc);
+            o.y = pack_bf16(f1.x * sc, f1.y * sc);
+            o.z = pack_bf16(f2.x * sc, f2.y * sc);
+            o.w = pack_bf16(f3.x * sc, f3.y * sc);
+            const int c8 = h * 4 + q * 2 + w2;  // 16-byte chunk of the 128-byte NoPE row
+            *reinterpret_cast<uint4*>(kt + r * 128 + ((c8 ^ (r & 7)) << 4)) = o;
           }
         }
-        // per-token 32-bit column masks: word (k * 4 + w) of buffer s covers
-        // KV rows 32 w .. 32 w + 31
-        const uint32_t mask = ok ? R[h].mask : 0u;
+      }
+      // RoPE half: 16 rows x 8 pieces, copied into K-tile region 1
+#pragma unroll
+      for (int k = 0; k < kProdRows * 8 / 32; ++k) {
+        const int piece = k * 32 + lane;
+        const int r = row0 + (piece >> 3), c8 = piece & 7;
+        const bool ok = (mask_s[s * kCh + r] & kOkBit) != 0;
+        const uint4 v = ok ? *reinterpret_cast<const uint4*>(stage + kRawRope + r * 128 + c8 * 16) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(kt + kKRegion + r * 128 + ((c8 ^ (r & 7)) << 4)) = v;
+      }
+      // per-token 16-bit column masks of these rows: halfword (k * 4 + warp
+      // slice) of buffer b, so word k * 2 + hi covers KV rows hi * 32 .. + 31
+      {
+        const uint32_t mask = lane < kProdRows ? mask_s[s * kCh + row0 + lane] : 0u;
+        uint16_t* km16 = reinterpret_cast<uint16_t*>(kmask + b * kCh);
         for (int k = 0; k < G.ntok; ++k) {
           const uint32_t bits = __ballot_sync(0xffffffffu, (mask >> k) & 1u);
-          if (lane == 0) kmask[s * kKMaskWords + k * 4 + pw * kRowsPerLane + h] = bits;
+          if (lane == 0) km16[k * 4 + (row0 / kProdRows)] = static_cast<uint16_t>(bits & 0xffffu);
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(k_full + s);
-    };
-    // prologue: the first kKBufs chunks (index loads first, all in flight)
-    static_assert(kKBufs == 3, "the producer keeps three chunks' rows in registers");
-    Res r0[kRowsPerLane], r1[kRowsPerLane], r2[kRowsPerLane];
-    uint32_t b0[kRowsPerLane], b1[kRowsPerLane], b2[kRowsPerLane];
-#pragma unroll
-    for (int h = 0; h < kRowsPerLane; ++h) r0[h].slot = r1[h].slot = r2[h].slot = -1;
-    if (0 < n) resolve(c_begin, r0);
-    if (1 < n) resolve(c_begin + 1, r1);
-    if (2 < n) resolve(c_begin + 2, r2);
-    pdl_wait();  // the cache rows: the kernel before may still be inserting
-    issue(0, r0, b0);  // cp.async groups 0, 1, 2
-    issue(1, r1, b1);
-    issue(2, r2, b2);
-    // Iteration i finishes chunk i, then refills chunk i - 1's buffer with
-    // chunk i + 2 (group i + 2).  The refill waits for chunk i - 1's last MMA
-    // only after chunk i is marked full: the MMA warp issues S(i) before the
-    // P.V(i - 1) that frees the buffer.
-    for (int i = 0; i < n; ++i) {
-      if (i + 2 < n && i >= 1) resolve(c_begin + i + 2, r2);  // index loads overlap the wait below
-      if (i == 0)
-        cp_async_wait_group<2>();  // chunk i's group has landed
-      else
-        cp_async_wait_group<1>();
-      __syncwarp();
-      finish(i, r0, b0);
-      if (i >= 1) {
-        if (i + 2 < n) {
-          if (!mbar_wait(k_empty + (i - 1) % kKBufs, ((i - 1) / kKBufs) & 1, wait_ns)) {
-            report(err, misc + 1, 2);
-            break;
-          }
-          issue(i + 2, r2, b2);
-        } else {
-          cp_async_commit();
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < kRowsPerLane; ++h) {
-        r0[h] = r1[h];
-        b0[h] = b1[h];
-        r1[h] = r2[h];
-        b1[h] = b2[h];
-        r2[h].slot = -1;
-      }
+      if (lane == 0) mbar_arrive(k_full + b);
     }
     cp_async_wait_group<0>();  // no copy may still target shared memory at exit
   } else if (warp == kMmaWarp) {
@@ -1152,68 +1035,59 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
       // Q arrived through cp.async (generic proxy); the MMAs read it through
       // the async proxy
       fence_proxy_async_smem();
-      auto issue_s = [&](int i, int t) {
-        const int kb = i % kKBufs;
+      auto issue_s = [&](int i) {
+        const int kb = i % kKBufs, sb = i & 1;
         tc_fence_after();
+        for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t qo = (t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32) >> 4;
-          const uint32_t ko = (kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32) >> 4;
-          umma_ss(tmem + s_col(t), dq + qo, dk + ko, idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t qo = (t * kQTile + (kk >> 2) * kQRegion + (kk & 3) * 32) >> 4;
+            const uint32_t ko = (kb * kKBuf + (kk >> 2) * kKRegion + (kk & 3) * 32) >> 4;
+            umma_ss(tmem + s_col(t, sb), dq + qo, dk + ko, idesc_s, kk > 0 ? 1u : 0u);
+          }
         }
-        umma_commit(s_full + t);
+        umma_commit(s_full + sb);
       };
-      auto issue_pv = [&](int i, int t) {
-        const int kb = i % kKBufs;
+      auto issue_pv = [&](int i) {
+        const int kb = i % kKBufs, sb = i & 1;
         tc_fence_after();
+        for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
-        for (int kk = 0; kk < kCh / 16; ++kk)
-          umma_ts(tmem + t * 128, tmem + s_col(t) + kk * 8, dv + ((kb * kKBuf + kk * 2048) >> 4), idesc_o,
-                  (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(pv_done + t);
+          for (int kk = 0; kk < kCh / 16; ++kk)
+            umma_ts(tmem + t * 128, tmem + s_col(t, sb) + kk * 8, dv + ((kb * kKBuf + kk * 2048) >> 4), idesc_o,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(k_empty + kb);
+        umma_commit(pv_done + sb);
       };
-      // S(i + 1) of a tile goes out right after its P.V(i) (the S buffer
-      // holds P(i) until then) as soon as K(i + 1) is full; the waits suspend
-      // the thread and are bounded.
+      // Issue order S(0), then per chunk S(i + 1) -- as soon as its K tile is
+      // ready, so softmax finds the next S waiting -- and P.V(i) once softmax
+      // has written P(i).  S(i + 1) reuses the TMEM buffer of chunk i - 1,
+      // whose P.V is already issued.  The waits suspend the thread (no
+      // polling that would take issue slots from the softmax warps) and are
+      // bounded: an error after kWaitLimitNs.
       if (ok && n > 0) {
         ok = mbar_wait(k_full, 0, wait_ns);
-        if (ok) {
-          issue_s(0, 0);
-          if (ntiles > 1) issue_s(0, 1);
-        }
+        if (ok) issue_s(0);
       }
       for (int i = 0; ok && i < n; ++i) {
-        const int kb = i % kKBufs;
-        const bool next = i + 1 < n;
-        ok = mbar_wait(p_full, i & 1, wait_ns);
-        if (!ok) break;
-        issue_pv(i, 0);
-        if (ntiles == 1) umma_commit(k_empty + kb);
-        if (next) {
+        if (i + 1 < n) {
           ok = mbar_wait(k_full + (i + 1) % kKBufs, ((i + 1) / kKBufs) & 1, wait_ns);
           if (!ok) break;
-          issue_s(i + 1, 0);
+          issue_s(i + 1);
         }
-        if (ntiles > 1) {
-          ok = mbar_wait(p_full + 1, i & 1, wait_ns);
-          if (!ok) break;
-          issue_pv(i, 1);
-          umma_commit(k_empty + kb);
-          if (next) issue_s(i + 1, 1);
-        }
+        ok = mbar_wait(p_full + (i & 1), (i >> 1) & 1, wait_ns);
+        if (!ok) break;
+        issue_pv(i);
       }
       if (!ok) report(err, misc + 1, 4);
     }
     __syncwarp();
   } else {
     // --------------------------------------------------------------- softmax
-    // one lane per query row (R > 64) or two lanes per row (R <= 64), its S
-    // row in TMEM lane `rit` of tile t
+    // one thread per query row: its S row lives in TMEM lane `rit` of tile t
     const int t = warp >> 2, quad = warp & 3;
     const int rit = quad * 32 + lane;
-    const int R_t = tile_rows(t, rows_q);
-    const bool split = R_t <= 64;
-    const int half = split ? (lane >> 4) : 0;
     const int r = tile_row_to_query(t, rit, rows_q);
     const bool row_valid = r >= 0;
     const bool warp_active = __any_sync(0xffffffffu, row_valid);
@@ -1221,47 +1095,46 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     const int head = row_valid ? r % H : 0;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t o_col = static_cast<uint32_t>(t) * 128u;
-    const uint32_t s_addr = tmem + lane_addr + s_col(t);
     const float scale = P.scale_log2;
-    // barriers and masks by 32-bit shared addresses (registers are scarce here)
-    const uint32_t sbar = smem_u32(smem + kBarOff);
-    const uint32_t s_full_a = sbar + (2 * kKBufs + t) * 8, p_full_a = s_full_a + 16, pv_done_a = s_full_a + 32;
-    const uint32_t kmask_a = smem_u32(smem + kKMaskOff) + tok * 16;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
     if (warp_active) {
       for (int i = 0; i < n; ++i) {
-        const int kb = i % kKBufs;
-        if (!mbar_wait_a(s_full_a, i & 1, wait_ns) || !mbar_wait_a(sbar + kb * 8, (i / kKBufs) & 1, wait_ns)) {
+        const int b = i & 1, kb = i % kKBufs;
+        if (!mbar_wait(s_full + b, (i >> 1) & 1, wait_ns) || !mbar_wait(k_full + kb, (i / kKBufs) & 1, wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // this row's token columns of the chunk: bit j of word w = KV row 32 w + j
-        const uint4 km = lds128(kmask_a + kb * kKMaskWords * 4);
-        const uint32_t w[4] = {row_valid ? km.x : 0u, row_valid ? km.y : 0u, row_valid ? km.z : 0u,
-                               row_valid ? km.w : 0u};
-        // the whole S row in one TMEM round trip: columns 0-63 in sr, 64-127 in s2
-        uint32_t sr[64], s2[64];
+        // valid columns of this row's token: bit j of lo / hi = KV row j / 32 + j
+        const uint32_t lo = row_valid ? kmask[kb * kCh + tok * 2] : 0u;
+        const uint32_t hi = row_valid ? kmask[kb * kCh + tok * 2 + 1] : 0u;
+        const bool full = (lo & hi) == 0xffffffffu;
+        const uint32_t s_addr = tmem + lane_addr + s_col(t, b);
+        uint32_t sr[kCh];
         tmem_ld32(s_addr, sr);
         tmem_ld32(s_addr + 32, sr + 32);
-        tmem_ld32(s_addr + 64, s2);
-        tmem_ld32(s_addr + 96, s2 + 32);
         tmem_wait_ld();
-        float mx;
-        if (!split) {
-          mask64(sr, w[0], w[1]);
-          mask64(s2, w[2], w[3]);
-          mx = fmaxf(max64(sr), max64(s2));
-        } else {
-          // a split lane keeps its half (a TMEM load takes one column
-          // address for the whole warp, so both halves were loaded)
+        // masked columns become -inf: they drop out of the max and 2^-inf = 0
+        if (!full) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) sr[j] = half ? s2[j] : sr[j];
-          mask64(sr, half ? w[2] : w[0], half ? w[3] : w[1]);
-          mx = max64(sr);
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          for (int j = 0; j < 32; ++j) {
+            sr[j] = ((lo >> j) & 1u) ? sr[j] : 0xff800000u;
+            sr[32 + j] = ((hi >> j) & 1u) ? sr[32 + j] : 0xff800000u;
+          }
         }
+        // row max as a tree of 3-input maxima (short dependency chains)
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          m8[k] = fmax3(__uint_as_float(sr[k]), __uint_as_float(sr[k + 8]), __uint_as_float(sr[k + 16]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 24]), __uint_as_float(sr[k + 32]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(sr[k + 40]), __uint_as_float(sr[k + 48]));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(sr[k + 56]));
+        float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         mx *= scale;  // scale > 0 commutes with the max
         // raise the running max lazily: only when it grows by more than 2^8
         const bool need = mx > m_used + 8.0f;
@@ -1269,36 +1142,34 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
         float f = 1.0f;
         if (rescale) {
           const float new_m = fmaxf(m_used, mx);
-          f = m_used == -INFINITY ? 0.0f : ex2_approx(m_used - new_m);
+          f = m_used == -INFINITY ? 0.0f : exp2f(m_used - new_m);
           l *= f;
           m_used = new_m;
         }
+        // P = 2^(s * scale - m) as bf16 pairs; exponents by packed FMAs,
+        // row sum in four packed accumulators
         const float nb = m_used == -INFINITY ? 0.0f : -m_used;
+        const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(nb, nb);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        exp32(sr, scale, nb, acc);
-        exp32(sr + 32, scale, nb, acc);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sr[16 + j] = sr[32 + j];
-        if (!split) {
-          exp32(s2, scale, nb, acc);
-          exp32(s2 + 32, scale, nb, acc);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) s2[16 + j] = s2[32 + j];
-        } else {
-          // this lane's P words go to its half, zeros to the other
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            s2[j] = half ? sr[j] : 0u;
-            sr[j] = half ? 0u : sr[j];
+          for (int j = 0; j < 16; ++j) {
+            const float2 x = fma2(make_float2(__uint_as_float(sr[hh * 32 + 2 * j]), __uint_as_float(sr[hh * 32 + 2 * j + 1])),
+                                  sc2, nb2);
+            const float2 p2 = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            acc[j & 3] = add2(acc[j & 3], p2);
+            pk[j] = pack_bf16(p2.x, p2.y);
           }
+          tmem_st16(s_addr + hh * 16, pk);
         }
-        tmem_st32(s_addr, sr);
-        tmem_st32(s_addr + 32, s2);
         const float2 a01 = add2(add2(acc[0], acc[1]), add2(acc[2], acc[3]));
-        l += a01.x + a01.y;
+        const float rs = a01.x + a01.y;
+        l += rs;
         if (rescale && i > 0) {
           // O holds chunks < i at the old max: wait for PV(i-1), then scale it
-          if (!mbar_wait_a(pv_done_a, (i - 1) & 1, wait_ns)) {
+          if (!mbar_wait(pv_done + ((i - 1) & 1), ((i - 1) >> 1) & 1, wait_ns)) {
             ok = false;
             break;
           }
@@ -1316,94 +1187,58 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_a(p_full_a);
+        if (lane == 0) mbar_arrive(p_full + b);
       }
       if (ok && n > 0) {
-        // the last P.V of this tile (and, before the Q and K tiles are
-        // reused as staging, of the other tile)
-        if (!mbar_wait_a(pv_done_a, (n - 1) & 1, wait_ns)) ok = false;
-        const uint32_t pv_other_a = sbar + (2 * kKBufs + 4 + (t ^ 1)) * 8;
-        if (ok && !ectx[0] && ntiles > 1 && !mbar_wait_a(pv_other_a, (n - 1) & 1, wait_ns)) ok = false;
+        if (!mbar_wait(pv_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, wait_ns)) ok = false;
         tc_fence_after();
       }
       if (!ok) report(err, misc + 1, 8);
-      // a split row's two lanes hold partial sums of one row at the same max
-      if (split) l += __shfl_xor_sync(0xffffffffu, l, 16);
       // ---- epilogue: normalise (single split) or write the partial ----
-      const bool single = ectx[0] != 0;
-      const int64_t item = static_cast<int64_t>(static_cast<uint32_t>(ectx[1])) |
-                           (static_cast<int64_t>(ectx[2]) << 32);
-      const int g_t0 = ectx[3];
-      const int r = tile_row_to_query(t, rit, rows_q);
-      const int tok = row_valid ? r / H : 0;
-      const int head = row_valid ? r % H : 0;
-      const bool any_o = ok && n > 0;
-      const bool have_o = any_o && l > 0.0f;
-      // columns of every 32 this lane writes: all, or its 16
-      const int c_lo = split ? half * 16 : 0;
+      const bool have_o = ok && n > 0 && l > 0.0f;
       if (single) {
         const float sink2 = (P.sink && row_valid) ? P.sink[head] * kLog2e : -INFINITY;
         const float inv = have_o ? 1.0f / (l + exp2f(sink2 - m_used)) : 0.0f;
-        __nv_bfloat16* orow = P.out + (g_t0 + tok) * P.o_st + head * P.o_sh;
+        __nv_bfloat16* orow = P.out + (G.t0 + tok) * P.o_st + head * P.o_sh;
 #pragma unroll 1
         for (int q4 = 0; q4 < kD / 32; ++q4) {
           uint32_t o[32];
-          if (any_o) {
+          if (ok && n > 0) {
             tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
             tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = 0u;
-          }
-          if (split) {
-            // add the pair's partial rows; the upper lane takes columns 16-31
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              o[e] = __float_as_uint(__uint_as_float(o[e]) + __shfl_xor_sync(0xffffffffu, __uint_as_float(o[e]), 16));
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = half ? o[16 + e] : o[e];
           }
           if (row_valid) {
             uint32_t pkd[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e)
               pkd[e] = have_o ? pack_bf16(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv) : 0u;
-            uint4* dst = reinterpret_cast<uint4*>(orow + q4 * 32 + c_lo);
-            const int nvec = split ? 2 : 4;  // 16-byte stores: 16 or 32 columns
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              if (e < nvec) dst[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2], pkd[4 * e + 3]);
+              reinterpret_cast<uint4*>(orow + q4 * 32)[e] = make_uint4(pkd[4 * e], pkd[4 * e + 1], pkd[4 * e + 2], pkd[4 * e + 3]);
           }
         }
-        if (P.lse && row_valid && half == 0)
-          P.lse[(g_t0 + tok) * H + head] = have_o ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
+        if (P.lse && row_valid)
+          P.lse[(G.t0 + tok) * H + head] = have_o ? (m_used + log2f(l)) * 0.6931471805599453f : -INFINITY;
       } else {
         // The fp32 partial rows are staged in shared memory (the Q and K
-        // tiles are free once the last MMA of both tiles has completed) as
-        // query-ordered 512-byte rows whose 16-byte chunks are XOR-swizzled
-        // by row, so both the per-lane row writes and the per-warp row reads
-        // below are bank-conflict free; each warp then stores whole rows, one
+        // tiles are free once the last MMA has completed) as query-ordered
+        // 512-byte rows whose 16-byte chunks are XOR-swizzled by row, so both
+        // the per-thread row writes and the per-warp row reads below are
+        // bank-conflict free; each warp then stores whole rows, one
         // coalesced 512-byte line group per instruction.
+        const int64_t rr = item * P.max_rows + (row_valid ? r : 0);
         float* stage = reinterpret_cast<float*>(smem + kQOff);  // [rows][128] fp32
+        const bool any_o = ok && n > 0;
 #pragma unroll 1
         for (int q4 = 0; q4 < kD / 32; ++q4) {
           uint32_t o[32];
           if (any_o) {
             tmem_ld32(tmem + lane_addr + o_col + q4 * 32, o);
             tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = 0u;
-          }
-          if (split) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              o[e] = __float_as_uint(__uint_as_float(o[e]) + __shfl_xor_sync(0xffffffffu, __uint_as_float(o[e]), 16));
           }
           if (row_valid && have_o) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              if (split && (e >> 2) != half) continue;  // a split lane stores its 16 of the 32 columns
               const int j = q4 * 8 + e;  // 16-byte chunk of the row
               *reinterpret_cast<float4*>(stage + r * kD + ((j ^ (r & 7)) << 2)) =
                   make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
@@ -1411,8 +1246,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
             }
           }
         }
-        if (row_valid && half == 0) {
-          const int64_t rr = item * P.max_rows + r;
+        if (row_valid) {
           P.ws_ml[rr * 2] = have_o ? m_used : -INFINITY;
           P.ws_ml[rr * 2 + 1] = have_o ? l : 0.0f;
         }
@@ -1421,7 +1255,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
           // uniform across the CTA, even when a wait timed out; rows whose sum
           // is zero carry whatever the stage holds: the merge never reads them
           asm volatile("bar.sync 2, %0;\n" ::"r"(nact * 32) : "memory");
-          const int aidx = t == 0 ? quad : act0 + quad;  // index among active warps
+          const int aidx = (warp >> 2) == 0 ? (warp & 3) : act0 + (warp & 3);  // index among active warps
           for (int row = aidx; row < rows_q; row += nact) {
             const float4 v = *reinterpret_cast<const float4*>(stage + row * kD + ((lane ^ (row & 7)) << 2));
             reinterpret_cast<float4*>(P.ws_o + (item * P.max_rows + row) * kD)[lane] = v;
@@ -1441,8 +1275,7 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
 
 // ============================================================================
 // Decode work list (one CTA, kSchedThreads threads).  Group g has c_g chunks
-// of `chunk` union rows (the consuming kernel's own count: 128 for the
-// head_dim-128 kernel, 64 for the head_dim-512 pairs).  The smallest per-CTA
+// of 64 union rows (the decode kernel's own count).  The smallest per-CTA
 // chunk budget t with sum_g max(1, ceil(c_g / t)) <= max_items and at most
 // kSchedMaxSplits CTAs per group is found by bisection; group g then gets
 // s_g = max(1, ceil(c_g / t)) CTAs over even chunk ranges, numbered group by
@@ -1453,7 +1286,7 @@ constexpr int kSchedMaxGroups = 8192;
 constexpr int kSchedMaxSplits = 16;
 
 __device__ __forceinline__ int sched_chunks(const int32_t* group_starts, const int32_t* swa_lens,
-                                            const int32_t* comp_lens, int g, int chunk) {
+                                            const int32_t* comp_lens, int g) {
   const int t0 = group_starts ? group_starts[g] : g;
   const int t1 = group_starts ? group_starts[g + 1] : g + 1;
   const int len0 = swa_lens[t0];
@@ -1461,7 +1294,7 @@ __device__ __forceinline__ int sched_chunks(const int32_t* group_starts, const i
   const int len_last = swa_lens[t1 - 1];
   const int extra = min(t1 - t0 - 1, len_last);
   const int n_comp = comp_lens ? max(comp_lens[t1 - 1], 0) : 0;
-  return (len0 + extra + n_comp + chunk - 1) / chunk;
+  return (len0 + extra + n_comp + tcd::kCh - 1) / tcd::kCh;
 }
 
 __device__ __forceinline__ int block_sum(int v, int* red) {
@@ -1476,12 +1309,12 @@ __device__ __forceinline__ int block_sum(int v, int* red) {
 
 __global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
     int32_t* sched, int max_items, const int32_t* group_starts, int num_groups, const int32_t* swa_lens,
-    const int32_t* comp_lens, int chunk) {
+    const int32_t* comp_lens) {
   __shared__ int c_s[kSchedMaxGroups];
   __shared__ int red[kSchedThreads / 32];
   int maxc = 1;
   for (int g = threadIdx.x; g < num_groups; g += kSchedThreads) {
-    c_s[g] = sched_chunks(group_starts, swa_lens, comp_lens, g, chunk);
+    c_s[g] = sched_chunks(group_starts, swa_lens, comp_lens, g);
     maxc = max(maxc, c_s[g]);
   }
   for (int o = 16; o > 0; o >>= 1) maxc = max(maxc, __shfl_xor_sync(0xffffffffu, maxc, o));
@@ -1546,8 +1379,6 @@ __global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
   // idle slots past the last item
   for (int i = total + threadIdx.x; i < max_items; i += kSchedThreads)
     reinterpret_cast<int4*>(sched)[i] = make_int4(-1, 0, 0, 0);
-  // the chunk size the list counts in, checked by the consuming kernel
-  if (threadIdx.x == 0) groups[2 * num_groups] = chunk;
 }
 
 // ============================================================================
@@ -1645,8 +1476,7 @@ using namespace hca;
 
 // Device error word: bit 0 loader, bit 1 dequant, bit 2 MMA, bit 3 softmax
 // of the attention kernels, bit 4 the streamed Q prep, bit 5 the streamed
-// VHA output kernel timed out on an mbarrier; bit 6 a decode work list built
-// for another head_dim.  Zero in normal operation.
+// VHA output kernel timed out on an mbarrier.  Zero in normal operation.
 __device__ int g_hca_device_error;
 
 int* hca::device_error_word() {
@@ -1674,7 +1504,16 @@ extern "C" int64_t hca_sparse_decode_workspace_bytes(int32_t num_groups, int32_t
   return o + ml;
 }
 
-static uint64_t attention_wait_ns();
+// Limit of every mbarrier wait of the head_dim-128 attention kernel for
+// launches made from now on; < 0 restores the default.  A diagnostic: with
+// 0 a wait that is not already satisfied fails at once, so the launch ends
+// early with its device error bits set (used to test the bounded waits).
+static std::atomic<int64_t> g_attn_wait_ns{-1};
+
+static uint64_t attention_wait_ns() {
+  const int64_t v = g_attn_wait_ns.load();
+  return v < 0 ? tc::kWaitLimitNs : static_cast<uint64_t>(v);
+}
 
 static bool attn_shape_ok(int num_heads, int head_dim, int rope_dim, int group_tokens) {
   return head_dim == 128 && rope_dim == 64 && num_heads > 0 && num_heads % 16 == 0 &&
@@ -1775,7 +1614,6 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   P.max_rows = max_group_tokens * num_heads;
   P.sched = schedule;
   P.sched_items = schedule ? max_items : 0;
-  P.sched_groups = schedule ? num_groups : 0;
   P.force_partials = fused;
   P.wait_ns = attention_wait_ns();
   // partial slots: groups x splits, or one per work-list item
@@ -1843,49 +1681,25 @@ extern "C" int hca_sparse_decode(void* out, int64_t out_stride_tok, int64_t out_
 
 extern "C" int64_t hca_decode_schedule_ints(int32_t num_groups, int32_t max_items) {
   if (num_groups < 0 || max_items < num_groups || max_items < 1 || num_groups > kSchedMaxGroups) return -1;
-  return 4 * static_cast<int64_t>(max_items) + 2 * static_cast<int64_t>(num_groups) + 1;
+  return 4 * static_cast<int64_t>(max_items) + 2 * static_cast<int64_t>(num_groups);
 }
 
 extern "C" int hca_decode_schedule(int32_t* schedule, int32_t max_items, const int32_t* group_starts,
                                    int32_t num_groups, int32_t num_tokens, const int32_t* swa_lens,
-                                   const int32_t* comp_lens, int32_t head_dim, void* stream) {
+                                   const int32_t* comp_lens, void* stream) {
   HCA_CHECK_ARG(hca_decode_schedule_ints(num_groups, max_items) > 0);
   HCA_CHECK_ARG(num_tokens >= 0 && (group_starts || num_groups == num_tokens));
   HCA_CHECK_ARG(schedule && reinterpret_cast<uintptr_t>(schedule) % 16 == 0);
-  // rows per work unit of the kernel that consumes the list
-  int chunk = 0;
-  if (head_dim == 128)
-    chunk = tcd::kCh;
-  else if (head_dim == 512)
-    chunk = kWideChunkRows;
-  else
-    return HCA_E_UNSUPPORTED;
   if (num_groups == 0) {
     // every CTA idle
     hca_decode_schedule_kernel<<<1, kSchedThreads, 0, as_stream(stream)>>>(schedule, max_items, group_starts, 0,
-                                                                           swa_lens, comp_lens, chunk);
+                                                                           swa_lens, comp_lens);
     return HCA_LAUNCH_STATUS();
   }
   HCA_CHECK_ARG(swa_lens);
   hca_decode_schedule_kernel<<<1, kSchedThreads, 0, as_stream(stream)>>>(schedule, max_items, group_starts,
-                                                                         num_groups, swa_lens, comp_lens, chunk);
+                                                                         num_groups, swa_lens, comp_lens);
   return HCA_LAUNCH_STATUS();
-}
-
-// Limit of every mbarrier wait of the head_dim-128 attention kernel for
-// launches made from now on; < 0 restores the default.  A diagnostic: with
-// 0 a wait that is not already satisfied fails at once, so the launch ends
-// early with its device error bits set (used to test the bounded waits).
-static std::atomic<int64_t> g_attn_wait_ns{-1};
-
-extern "C" int hca_set_attention_wait_limit_ns(int64_t limit_ns) {
-  g_attn_wait_ns.store(limit_ns);
-  return HCA_OK;
-}
-
-static uint64_t attention_wait_ns() {
-  const int64_t v = g_attn_wait_ns.load();
-  return v < 0 ? tc::kWaitLimitNs : static_cast<uint64_t>(v);
 }
 
 extern "C" int64_t hca_sparse_decode_vha_workspace_bytes(int32_t max_items, int32_t max_group_tokens,
@@ -1936,6 +1750,11 @@ extern "C" int hca_sparse_decode_vha_fp8_quant(
                          cudaSharedmemCarveoutMaxShared, carveout_set) != HCA_OK)
     return HCA_E_CUDA;
   return launch_pdl(hca_combine_vha_quant_kernel, dim3(V.aligned_t), dim3(512), 0, as_stream(stream), P, V);
+}
+
+extern "C" int hca_set_attention_wait_limit_ns(int64_t limit_ns) {
+  g_attn_wait_ns.store(limit_ns);
+  return HCA_OK;
 }
 
 extern "C" int hca_sparse_decode_scheduled(void* out, int64_t out_stride_tok, int64_t out_stride_head,

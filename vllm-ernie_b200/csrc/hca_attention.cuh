@@ -62,7 +62,6 @@ struct AttnParams {
   // i (group -1: idle), then per group {first item, items}
   const int32_t* sched;
   int sched_items;
-  int sched_groups;  // groups the list was built for (its chunk-size word follows their entries)
   // every CTA writes its partial, even a group's only CTA (the merge happens
   // in the fused combine + VHA kernel)
   int force_partials;
@@ -188,9 +187,6 @@ __device__ __forceinline__ void row_source(const AttnParams& P, const Group& G, 
 // hca_attention_wide.cu.
 int launch_wide_attention(const AttnParams& P, bool prefill, int num_groups, int max_group_tokens, int* err,
                           cudaStream_t s);
-
-// KV rows per chunk of the head_dim-512 pair kernel (the work-list unit for it).
-constexpr int kWideChunkRows = 64;
 
 // Query tokens one pair handles at head count H (one M=128 tile of rows, at
 // most 31 tokens: a row's token mask keeps bit 31 for its "loaded" flag).

@@ -40,7 +40,7 @@ namespace tcw {
 constexpr int kHalf = 256;          // head dims per CTA of the pair
 constexpr int kRowBytes = 576;      // 448 e4m3 + 64 bf16
 constexpr int kScaleBytes = 8;      // 7 UE8M0 bytes + pad
-constexpr int kCh = kWideChunkRows;  // KV rows per chunk
+constexpr int kCh = 64;             // KV rows per chunk
 constexpr int kStages = 3;          // raw ring: two chunks in flight
 constexpr int kKBufs = 2;           // bf16 K-tile ring
 constexpr int kSoftmaxWarps = 4;
@@ -125,10 +125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
   } else if (P.sched) {
     // balanced work list over groups of at most one tile of tokens
     const int4 it = reinterpret_cast<const int4*>(P.sched)[work];
-    // a work list built for another kernel's chunk size is refused
-    const int unit = P.sched[4 * P.sched_items + 2 * P.sched_groups];
-    if (unit != kCh && half == 0 && threadIdx.x == 0 && err) atomicOr(err, 64);
-    if (it.x < 0 || unit != kCh) return;
+    if (it.x < 0) return;
     int t0, t1;
     group_tokens(P, it.x, t0, t1);
     if (t1 - t0 > P.group_tokens || (t1 - t0) * H > P.max_rows) return;

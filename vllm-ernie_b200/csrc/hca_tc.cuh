@@ -102,51 +102,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   return true;
 }
 
-// The same waits and arrivals on an mbarrier given by its 32-bit shared
-// address (one register, where a generic pointer takes two).
-__device__ __forceinline__ bool mbar_try_wait_a(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_a(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
-  if (limit_ns == 0) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-  }
-  if (mbar_try_wait_a(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait_a(bar, parity))
-    if (global_ns() - t0 > limit_ns) return false;
-  return true;
-}
-
-__device__ __forceinline__ void mbar_arrive_a(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
-}
-
-// 16-byte shared-memory load from a 32-bit shared address.
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
-               : "memory");
-  return v;
-}
-
 // ------------------------------------------------------- 2-CTA clusters
 // Rank of this CTA in its cluster.
 __device__ __forceinline__ uint32_t cluster_ctarank() {

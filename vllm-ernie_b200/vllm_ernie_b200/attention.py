@@ -344,8 +344,7 @@ class Ernie5_5HCAAttention(nn.Module):
                 sms = _sm_count(qp.device)
                 c128.decode_items = max(sms if d == 128 else sms // 2, groups)
                 c128.decode_schedule = ops.decode_schedule(swa.decode_group_starts, ndt, swa.decode_swa_lens,
-                                                           c128.c128a_decode_topk_lens, c128.decode_items,
-                                                           head_dim=d)
+                                                           c128.c128a_decode_topk_lens, c128.decode_items)
             ops.sparse_decode(qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,
                               self.kv_cache, self.comp_page, c128.c128a_global_decode_topk_indices,
                               c128.c128a_decode_topk_lens, self.scale, sink, out=o[:ndt],

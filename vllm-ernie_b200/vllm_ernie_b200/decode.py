@@ -107,7 +107,7 @@ def build_decode_metadata(batch: DecodeBatch, max_compressed: int, num_splits: i
                               cidx, clens, gs, max_g, num_splits)
     # one wave: a CTA per SM, or a CTA pair per two SMs at head_dim 512
     items = max(max_items or (sm_count if d.head_dim == 128 else sm_count // 2), ngroups)
-    sched = ops.decode_schedule(gs, T, swa_lens, clens, items, out=buf.get("schedule"), head_dim=d.head_dim)
+    sched = ops.decode_schedule(gs, T, swa_lens, clens, items, out=buf.get("schedule"))
     buf["schedule"] = sched
     return DecodeMetadata(T, t2r, swa_slot, state_slot, comp_slot, is_valid, swa_idx, swa_lens,
                           cidx, clens, gs, max_g, 1, sched, items)

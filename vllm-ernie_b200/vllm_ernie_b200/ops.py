@@ -268,13 +268,11 @@ class DecodeWorkspace:
 _WS = DecodeWorkspace()
 
 
-def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_items: int, out=None,
-                    head_dim: int = 128):
+def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_items: int, out=None):
     """Per-step decode work list (the role of FlashMLA's ``get_mla_metadata``
     tile-scheduler metadata): ``int32[hca_decode_schedule_ints]``, valid for
     every layer of the step.  ``max_items`` = one wave of CTAs (the SM count,
-    at least the number of groups); ``head_dim`` selects the attention kernel
-    whose chunk size the list counts in (a list is refused by the other)."""
+    at least the number of groups)."""
     _check_cuda(swa_lens)
     num_groups = num_tokens if group_starts is None else group_starts.numel() - 1
     n = lib().hca_decode_schedule_ints(num_groups, max_items)
@@ -283,7 +281,7 @@ def decode_schedule(group_starts, num_tokens: int, swa_lens, comp_lens, max_item
     if out is None or out.numel() != n:
         out = torch.empty(n, dtype=torch.int32, device=swa_lens.device)
     call("hca_decode_schedule", _p(out), max_items, _p(group_starts), num_groups, num_tokens, _p(swa_lens),
-         _p(comp_lens), head_dim, _s())
+         _p(comp_lens), _s())
     return out
 
 
