@@ -321,8 +321,11 @@ int hca_sparse_decode_vha_fp8_quant(
  * loading this library holds until exit, and a call whose
  * hca_sparse_decode_workspace_bytes exceeds it returns HCA_E_TOO_LARGE.  No
  * memory is allocated.  The first call on a device looks up the array's
- * device address with that device current; make that first call before any
- * stream capture.  All calls on a GPU share the array: calls whose kernels
+ * device address with that device current and keeps it for the life of the
+ * process; make that first call before any stream capture, and do not call
+ * this entry point again after cudaDeviceReset.  Argument and shape errors
+ * (num_splits outside 1..16, head_dim other than 128 / 512) are reported as
+ * HCA_E_INVALID / HCA_E_UNSUPPORTED before the size check.  All calls on a GPU share the array: calls whose kernels
  * overlap on the GPU race, so order them on one stream.  Nothing in the array
  * needs clearing between calls (each call writes every partial it merges). */
 int hca_sparse_decode_noalloc(void* out, int64_t out_stride_tok, int64_t out_stride_head, float* lse,

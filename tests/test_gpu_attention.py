@@ -402,3 +402,50 @@ def test_bounded_wait_gives_up_and_next_launch_is_clean():
     assert err & 8, err
     assert ops.device_error() == 0
     _decode_case([300, 5000, 40000], 3, 64, None, seed=41)
+
+
+def test_decode_workspace_per_device_and_stable_under_capture():
+    """The split-K workspace keeps one buffer per device, reuses it for
+    smaller requests, and refuses to grow while a CUDA graph is being
+    captured (a regrown buffer would free the address the graph holds)."""
+    from vllm_ernie_b200.ops import DecodeWorkspace
+
+    ws = DecodeWorkspace()
+    a = ws.get(1 << 20, "cuda:0")
+    assert ws.get(1 << 10, "cuda:0").data_ptr() == a.data_ptr()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        assert ws.get(1 << 20, "cuda:0").data_ptr() == a.data_ptr()
+        with pytest.raises(RuntimeError):
+            ws.get(1 << 21, "cuda:0")
+    del g
+    if torch.cuda.device_count() > 1:
+        b = ws.get(1 << 20, "cuda:1")
+        assert b.device.index == 1 and ws.get(1 << 20, "cuda:0").data_ptr() == a.data_ptr()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in one process")
+def test_decode_on_two_devices_in_one_process():
+    """One process drives split-K decode on cuda:0 then cuda:1: each launch
+    gets its own device's workspace and both give the same output."""
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200.decode import build_decode_metadata
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
+
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        with torch.cuda.device(dev):
+            dims = HCADims(heads=64)
+            b = make_decode_batch([300, 5000, 40000], 3, dims, dev, seed=7, max_model_len=1024 * 128)
+            caches = alloc_layer_caches(b, seed=8)
+            md = build_decode_metadata(b, 1024, num_splits=3)
+            g = torch.Generator(device=dev).manual_seed(9)
+            q = torch.randn((b.num_tokens, 64, 128), generator=g, device=dev).to(torch.bfloat16)
+            sink = torch.randn(64, generator=g, device=dev)
+            o = ops.sparse_decode(q, caches.swa, 64, md.swa_indices, md.swa_lens, caches.comp, 2, md.comp_indices,
+                                  md.comp_lens, 128 ** -0.5, sink, group_starts=md.group_starts,
+                                  max_group_tokens=md.max_group_tokens, num_splits=3)
+            torch.cuda.synchronize()
+            outs.append(o.cpu())
+    assert torch.equal(outs[0], outs[1])

@@ -35,7 +35,10 @@ std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
 
 // Device address of the scratch on the current device, looked up once per
-// device (with that device current) and cached.
+// device (with that device current) and cached for the life of the process:
+// after cudaDeviceReset (or any teardown of the device's primary context)
+// the cached address is stale, so this entry point must not be used again
+// in that process.
 int noalloc_workspace(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return HCA_E_CUDA;
@@ -67,6 +70,10 @@ extern "C" int hca_sparse_decode_noalloc(void* out, int64_t out_stride_tok, int6
   // the same grouping rule as hca_sparse_decode: no group table = one token per group
   const int32_t groups = group_starts ? num_groups : num_tokens;
   const int32_t group_tokens = group_starts ? max_group_tokens : 1;
+  // argument and shape errors are reported as such before the size check
+  if (num_splits < 1 || num_splits > 16 || num_tokens < 0 || groups < 0 || num_heads < 1 || group_tokens < 1)
+    return HCA_E_INVALID;
+  if ((head_dim != 128 && head_dim != 512) || rope_dim != 64) return HCA_E_UNSUPPORTED;
   void* ws = nullptr;
   int64_t need = 0;
   if (num_splits > 1 && groups > 0 && num_tokens > 0) {

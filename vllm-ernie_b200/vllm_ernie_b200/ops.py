@@ -252,17 +252,34 @@ def device_error(clear: bool = True) -> int:
 
 
 class DecodeWorkspace:
-    """Persistent zero-initialised split-K workspace (graph-stable address)."""
+    """Persistent zero-initialised split-K workspace, one buffer per device.
+
+    A buffer's address is stable once a CUDA graph may hold it: it only
+    grows while no stream on its device is capturing (a grown buffer would
+    free the one a captured graph still points at); a request for more than
+    it holds during capture raises instead.  Size it before capture by one
+    eager call with the largest shapes (or ``reserve``)."""
 
     def __init__(self):
-        self.buf: torch.Tensor | None = None
+        self.bufs: dict[int, torch.Tensor] = {}
+
+    def reserve(self, nbytes: int, device) -> None:
+        self.get(nbytes, device)
 
     def get(self, nbytes: int, device) -> torch.Tensor | None:
         if nbytes == 0:
             return None
-        if self.buf is None or self.buf.numel() < nbytes:
-            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
-        return self.buf
+        device = torch.device(device)
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        buf = self.bufs.get(idx)
+        if buf is None or buf.numel() < nbytes:
+            if torch.cuda.is_current_stream_capturing():
+                have = 0 if buf is None else buf.numel()
+                raise RuntimeError(f"decode workspace on cuda:{idx} holds {have} bytes, {nbytes} needed while a "
+                                   "CUDA graph is being captured; size it with an eager call (or reserve) first")
+            buf = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+            self.bufs[idx] = buf
+        return buf
 
 
 _WS = DecodeWorkspace()
