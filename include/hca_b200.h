@@ -400,6 +400,28 @@ int hca_sigmoid_mul_quant_fp8(uint8_t* out, int32_t* scale, const void* x, int64
                               const void* gate, int64_t gate_stride, int32_t rows,
                               int32_t hidden, void* stream);
 
+/* Replaces the block-scaled FP8 GEMMs of the output path: the grouped wo_a
+ * einsum (DeepGEMM fp8_einsum "bhr,hdr->bhd", V/models/deepseek_v4/
+ * attention.py:317-347) and the gated wo_b linear (GatedDeepGemmLinear,
+ * E/nvidia/attention.py:364-395, apply_block_scaled_mm).
+ *   out[t, g, n] = sum_k x[t, g, k] * sx[t, g, k / 128] * w[g, n, k] * sw[g, n / 128, k / 128]
+ * x e4m3 rows of K bytes at x + g * x_stride_group + t * x_stride_tok (16-byte
+ * aligned); sx UE8M0 bytes, byte (b % xs_per_int) of the int32 at
+ * x_scale[t * xs_stride_tok + g * xs_stride_group + (b / xs_per_int) *
+ * xs_stride_pack] for K block b (xs_per_int 1 or 4: the layouts written by
+ * hca_vha_inv_rope_fp8_quant, hca_sparse_decode_vha_fp8_quant and
+ * hca_sigmoid_mul_quant_fp8); w e4m3 [G, N, K] contiguous with fp32 block
+ * scales w_scale [G, ceil(N / 128), K / 128]; out bf16 with element strides
+ * (out_stride_tok, out_stride_group), 16-byte aligned rows.  N a multiple of
+ * 64, K of 128; otherwise HCA_E_UNSUPPORTED.  fp32 accumulation: each
+ * 128-wide K block's partial product is scaled once and summed in fp32. */
+int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t out_stride_group,
+                         const uint8_t* x, int64_t x_stride_tok, int64_t x_stride_group,
+                         const int32_t* x_scale, int64_t xs_stride_tok, int64_t xs_stride_group,
+                         int64_t xs_stride_pack, int32_t xs_per_int, const uint8_t* w,
+                         const float* w_scale, int32_t num_tokens, int32_t num_groups, int32_t n,
+                         int32_t k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

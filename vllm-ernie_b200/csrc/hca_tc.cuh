@@ -171,6 +171,17 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
       : "memory");
 }
 
+// Tiled TMA load of one box of a rank-3 tensor map at (x, y, z) into shared
+// memory, completing its bytes on `bar` (no multicast).  x times the element
+// size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 16-byte global -> shared copy through L2 (LSU path, no TMA).
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src_gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst_smem)), "l"(src_gmem) : "memory");

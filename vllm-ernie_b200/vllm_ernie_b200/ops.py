@@ -460,3 +460,56 @@ def sigmoid_mul_quant_fp8(x, gate):
     return out, scale
 
 
+
+
+def fp8_grouped_gemm(x, x_scale, w, w_scale, out=None):
+    """Block-scaled FP8 GEMM of the output path: the grouped ``wo_a`` einsum
+    ``"bhr,hdr->bhd"`` (``V/models/deepseek_v4/attention.py:317-347``) for a
+    3-D ``x [T, G, K]`` and ``w [G, N, K]``, or the gated ``wo_b`` linear
+    (``E/nvidia/attention.py:364-395``) for a 2-D ``x [T, K]`` and ``w [N, K]``.
+    ``x`` e4m3 with the int32 UE8M0 scales the quant kernels write
+    (``[T, G, packs]`` or ``[T, packs]``, one or four 128-blocks per int32);
+    ``w`` e4m3 with fp32 128 x 128 block scales ``[G, ceil(N/128), K/128]`` (or
+    ``[ceil(N/128), K/128]``).  Returns bf16 ``[T, G, N]`` (or ``[T, N]``)."""
+    _check_cuda(x, x_scale, w, w_scale)
+    flat = x.dim() == 2
+    if flat:
+        x, x_scale, w, w_scale = x.unsqueeze(1), x_scale.unsqueeze(1), w.unsqueeze(0), w_scale.unsqueeze(0)
+    t, g, k = x.shape
+    n = w.shape[1]
+    assert x.dtype == FP8 and w.dtype == FP8 and x.stride(2) == 1
+    assert w.shape == (g, n, k) and w.is_contiguous()
+    assert w_scale.dtype == torch.float32 and w_scale.is_contiguous() and w_scale.shape == (g, (n + 127) // 128, k // 128)
+    assert x_scale.dtype == torch.int32 and x_scale.shape[:2] == (t, g) and k % 128 == 0
+    per_int = (k // 128) // x_scale.shape[2]
+    assert per_int in (1, 4) and per_int * x_scale.shape[2] == k // 128
+    if out is None:
+        out = torch.empty((t, g, n), dtype=torch.bfloat16, device=x.device)
+    elif flat:
+        out = out.unsqueeze(1)
+    assert out.shape == (t, g, n) and out.dtype == torch.bfloat16 and out.stride(2) == 1
+    if t:
+        call("hca_fp8_grouped_gemm", _p(out), out.stride(0), out.stride(1) if g > 1 else 0, _p(x), x.stride(0),
+             x.stride(1) if g > 1 else 0, _p(x_scale), x_scale.stride(0), x_scale.stride(1) if g > 1 else 0,
+             x_scale.stride(2), per_int, _p(w), _p(w_scale), t, g, n, k, _s())
+    return out.squeeze(1) if flat else out
+
+
+def quantize_weight_block_fp8(w: torch.Tensor, block: int = 128):
+    """Load-time 128 x 128 block FP8 quant of a bf16 weight ``[..., N, K]``:
+    power-of-two (UE8M0-valued) fp32 block scales, the format the Blackwell
+    DeepGEMM path runs block-FP8 checkpoints in (``E/nvidia/quant_config.py``;
+    ``dequantize_block_fp8`` there is its inverse).  Returns ``(w_fp8,
+    scale [..., ceil(N/128), K/128])``.  A one-off weight transform, not a
+    step of the forward pass."""
+    *lead, n, k = w.shape
+    assert k % block == 0
+    nb = (n + block - 1) // block
+    wf = torch.zeros((*lead, nb * block, k), dtype=torch.float32, device=w.device)
+    wf[..., :n, :] = w.float()
+    blocks = wf.view(*lead, nb, block, k // block, block)
+    amax = blocks.abs().amax(dim=(-3, -1)).clamp_min(1e-10)
+    e = torch.ceil(torch.log2(amax / 448.0))
+    scale = torch.exp2(e)
+    q = (blocks / scale[..., :, None, :, None]).clamp(-448.0, 448.0).to(FP8)
+    return q.view(*lead, nb * block, k)[..., :n, :].contiguous(), scale.contiguous()
