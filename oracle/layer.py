@@ -8,6 +8,14 @@ attention (``V/models/deepseek_v4/nvidia/flashmla.py:130-424``), with the
 unfused bf16 ``wo_a`` output path (the checkpoint is not 128x128 block FP8:
 ``E/nvidia/attention.py:417-428``, ``V/v1/attention/ops/rocm_aiter_mla_sparse.py:894-927``).
 
+``fp8_output=True`` follows the reference's FP8 output path instead
+(128 x 128 block-FP8 ``wo_a``/``wo_b``: ``E/nvidia/attention.py:417-428,
+439-469``, ``V/models/deepseek_v4/attention.py:317-347``): the fused VHA +
+inverse RoPE + 1x128 UE8M0 quant, the grouped ``wo_a`` on the dequantised
+operands with one bf16 rounding, ``sigmoid_mul_quant_fp8`` and ``wo_b`` on
+its dequantised output; ``wo_a.weight``/``wo_b.weight`` are then the
+dequantised block-FP8 weights.
+
 Two evaluations: ``emulate_quant=True`` runs the FP8/UE8M0 cache and the
 bf16 roundings exactly as the reference kernels do (the comparison target
 of the CUDA path); ``emulate_quant=False`` keeps everything fp32 (the
@@ -23,8 +31,8 @@ import numpy as np
 from . import cache as C
 from . import metadata as M
 from .attention import sparse_attention_token
-from .fp8 import bf16_round
-from .output import kv_rope, q_prep, rms_norm, vha_fold
+from .fp8 import bf16_round, e4m3_to_f32
+from .output import kv_rope, q_prep, rms_norm, sigmoid_mul_quant_fp8, vha_fold, vha_inv_rope_fp8_quant
 
 
 @dataclass
@@ -79,10 +87,12 @@ class HCALayerOracle:
     STATE_PAGE = 8
 
     def __init__(self, shape: HCAShape, weights: dict[str, np.ndarray], max_len: int,
-                 num_reqs: int, emulate_quant: bool = True):
+                 num_reqs: int, emulate_quant: bool = True, fp8_output: bool = False):
         self.s = shape
         self.w = weights
         self.emulate = emulate_quant
+        self.fp8_output = fp8_output
+        assert emulate_quant or not fp8_output
         s = shape
         self.cos_sin = C.rope_cos_sin_cache(max_len + 1, s.rope_dim, s.rope_theta)
         sw_pages = (max_len + self.SWA_PAGE - 1) // self.SWA_PAGE
@@ -162,6 +172,8 @@ class HCALayerOracle:
             o[t] = sparse_attention_token(q[t], k, s.head_dim ** -0.5, w["attn_sink"])
         o = self._r(o)
 
+        if self.fp8_output:
+            return self.output_fp8(o, self._r(qr @ w["o_gate.weight"].T), positions)
         # Gate, VHA, inverse RoPE, grouped wo_a, gated wo_b.
         gate = self._r(1.0 / (1.0 + np.exp(-self._r(qr @ w["o_gate.weight"].T))))
         m = vha_fold(w["vha.U"], w["vha.V"])
@@ -173,6 +185,23 @@ class HCALayerOracle:
         z = self._r(np.einsum("tgd,grd->tgr", o, wa)).reshape(len(positions), -1)
         zg = self._r(z * gate)
         return (zg @ w["wo_b.weight"].T).astype(np.float32)
+
+    def output_fp8(self, o, gate_logits, positions):
+        """The FP8 output path on the bf16 attention output ``o [T, H, D]``
+        and the bf16 gate logits ``[T, G * o_lora]``."""
+        s, w = self.s, self.w
+        t = len(positions)
+        m = bf16_round(vha_fold(w["vha.U"], w["vha.V"]))
+        q8, exp = vha_inv_rope_fp8_quant(o, m, positions, self.cos_sin, s.o_groups, s.rope_dim)
+        scale = np.ldexp(np.float32(1.0), np.repeat(exp, 128, axis=-1))        # [T, H, D]
+        x = e4m3_to_f32(q8.transpose(1, 0, 2)).reshape(t, s.heads, s.head_dim) * scale
+        x = x.reshape(t, s.o_groups, -1)
+        wa = w["wo_a.weight"].reshape(s.o_groups, s.o_lora, -1)
+        z = bf16_round(np.einsum("tgd,grd->tgr", x.astype(np.float64), wa.astype(np.float64))).reshape(t, -1)
+        zq, packed = sigmoid_mul_quant_fp8(z, gate_logits)
+        ez = np.stack([(packed.view(np.uint32) >> (8 * c)) & 0xFF for c in range(4)], -1).reshape(t, -1)
+        zf = e4m3_to_f32(zq) * np.ldexp(np.float32(1.0), np.repeat(ez.astype(np.int64) - 127, 128, axis=-1))
+        return bf16_round(zf.astype(np.float64) @ w["wo_b.weight"].T.astype(np.float64)).astype(np.float32)
 
     def _compress_exact(self, t2r, positions, st_slots):
         """fp32 compressed rows (no quantisation) for the exact evaluation."""

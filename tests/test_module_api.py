@@ -191,8 +191,9 @@ def test_attention_custom_op_schema_and_fake():
 
     op = torch.ops.hca_b200.hca_attention
     schema = str(op.default._schema)
-    out_arg = next(a for a in op.default._schema.arguments if a.name == "out")
-    assert out_arg.alias_info is not None and out_arg.alias_info.is_write, schema
+    for name in ("out", "out_scale"):
+        arg = next(a for a in op.default._schema.arguments if a.name == name)
+        assert arg.alias_info is not None and arg.alias_info.is_write, schema
     assert schema.endswith("-> ()"), schema
     with FakeTensorMode():
         q = torch.empty(3, 16, 128, dtype=torch.bfloat16)
@@ -200,7 +201,10 @@ def test_attention_custom_op_schema_and_fake():
         ks = torch.empty(3, 256)
         pos = torch.empty(3, dtype=torch.int64)
         out = torch.empty(3, 16, 128, dtype=torch.bfloat16)
-        assert op(q, kv, ks, pos, out, "model.layers.0.self_attn.x") is None
+        assert op(q, kv, ks, pos, out, torch.empty(0, dtype=torch.int32), "model.layers.0.self_attn.x") is None
+        out8 = torch.empty(4, 3, 512, dtype=torch.float8_e4m3fn)
+        sc = torch.empty(4, 4, 4, dtype=torch.int32)
+        assert op(q, kv, ks, pos, out8, sc, "model.layers.0.self_attn.x") is None
     cfg = A.Ernie5_5HCAConfig(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, head_dim=128,
                               q_lora_rank=512, qk_rope_head_dim=64, o_groups=4, o_lora_rank=64,
                               hybrid_mla_num_attention_heads=16, num_nextn_predict_layers=0)
@@ -209,3 +213,60 @@ def test_attention_custom_op_schema_and_fake():
     layer = A.Ernie5_5HCAAttention(vcfg, prefix="model.layers.0.self_attn")
     assert vcfg.compilation_config.static_forward_context[layer.layer_name] is layer
     assert A._find_layer(layer.layer_name) is layer
+
+
+# --------------------------------------------------------------------------- block-FP8 output path
+
+
+def _fp8_cfg(**kw):
+    base = dict(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, head_dim=128, q_lora_rank=512,
+                qk_rope_head_dim=64, o_groups=4, o_lora_rank=128, hybrid_mla_num_attention_heads=16,
+                num_nextn_predict_layers=0)
+    base.update(kw)
+    return A.Ernie5_5HCAConfig(**base)
+
+
+def test_fp8_output_selection_follows_the_quant_config():
+    """``wo_a``/``wo_b`` are block FP8 exactly when the reference keeps
+    ``wo_a`` FP8 (a 128 x 128 block-FP8 config that does not ignore it) and the
+    blocks tile the groups."""
+    assert not A.keeps_fp8_output(None)
+    assert not A.keeps_fp8_output(SimpleNamespace(weight_block_size=[32, 32], ignored_layers=[]))
+    assert not A.keeps_fp8_output(A.block_fp8_quant_config(["model.layers.0.self_attn.attn.wo_a"]))
+    assert A.keeps_fp8_output(A.block_fp8_quant_config())
+    layer = A.Ernie5_5HCAAttention(A.make_vllm_config(_fp8_cfg(), max_model_len=1152,
+                                                      quant_config=A.block_fp8_quant_config()),
+                                   prefix="model.layers.0.self_attn")
+    assert layer.fp8_output
+    assert layer.wo_a.weight.dtype == torch.float8_e4m3fn and layer.wo_a.weight_scale_inv.shape == (4, 4)
+    assert layer.wo_b.weight.shape == (2048, 512) and layer.wo_b.weight_scale_inv.shape == (16, 4)
+    # rank-64 groups do not tile 128-row blocks: the bf16 path
+    layer64 = A.Ernie5_5HCAAttention(A.make_vllm_config(_fp8_cfg(o_lora_rank=64), max_model_len=1152,
+                                                        quant_config=A.block_fp8_quant_config()),
+                                     prefix="model.layers.0.self_attn")
+    assert not layer64.fp8_output and layer64.wo_a.weight.dtype == torch.bfloat16
+
+
+def test_fp8_weights_load_from_block_fp8_or_quantise_on_load():
+    """A block-FP8 checkpoint (e4m3 + ``weight_scale_inv``) loads as is; a
+    bf16 weight is quantised to the same bytes and scales on load."""
+    from vllm_ernie_b200.ops import quantize_weight_block_fp8
+
+    vc = A.make_vllm_config(_fp8_cfg(), max_model_len=1152, quant_config=A.block_fp8_quant_config())
+    g = torch.Generator().manual_seed(0)
+    wa = torch.randn(512, 512, generator=g) * 0.02
+    wb = torch.randn(2048, 512, generator=g) * 0.02
+    qa, sa = quantize_weight_block_fp8(wa)
+    qb, sb = quantize_weight_block_fp8(wb)
+    assert torch.equal(sa, torch.exp2(torch.log2(sa))) and sa.shape == (4, 4)
+    deq = qa.float() * sa.repeat_interleave(128, 0).repeat_interleave(128, 1)
+    assert ((deq - wa).abs() <= wa.abs() * 2 ** -4 + sa.repeat_interleave(128, 0).repeat_interleave(128, 1) * 2 ** -9).all()
+    a = A.Ernie5_5HCAAttention(vc, prefix="model.layers.0.self_attn")
+    got = a.load_weights([("wo_a.weight", qa), ("wo_a.weight_scale_inv", sa), ("wo_b.weight", qb),
+                          ("wo_b.weight_scale_inv", sb)])
+    assert got == {"wo_a.weight", "wo_a.weight_scale_inv", "wo_b.weight", "wo_b.weight_scale_inv"}
+    b = A.Ernie5_5HCAAttention(vc, prefix="model.layers.0.self_attn")
+    b.load_weights([("wo_a.weight", wa), ("wo_b.weight", wb)])
+    for x, y in ((a.wo_a, b.wo_a), (a.wo_b, b.wo_b)):
+        assert torch.equal(x.weight.view(torch.uint8), y.weight.view(torch.uint8))
+        assert torch.equal(x.weight_scale_inv, y.weight_scale_inv)

@@ -13,10 +13,16 @@ Mirrors the plugin's module API (``E/nvidia/attention.py``):
 * ``VHAPostMix`` / ``fold_vha`` (``:121-163``) including the TP branch
   (``o + V all_reduce(U^T o)`` in fp32 over this rank's heads).
 
-The attention-side work is the library's CUDA kernels; the projections
-(``fused_wqa_wkv``, ``wq_b``, compressor ``kv_score``, ``o_gate``, grouped
-``wo_a``, gated ``wo_b``) are plain torch/cuBLAS GEMMs, bf16 ``wo_a``
-(block-FP8 checkpoints are dequantised at load).
+The attention-side work is the library's CUDA kernels.  With a 128 x 128
+block-FP8 quant config (``keeps_fp8_output``, the condition of
+``keeps_fp8_wo_a`` in ``E/nvidia/quant_config.py``) the output path is the
+reference's FP8 one: VHA + inverse RoPE + 1x128 UE8M0 quant (fused into the
+decode attention launch on decode-only steps), the grouped ``wo_a`` einsum
+and the gated ``wo_b`` on the library's tcgen05 FP8 GEMM, the gate's sigmoid
+fused into ``wo_b``'s input quant.  Without it ``wo_a``/``wo_b`` stay bf16
+(torch/cuBLAS), as the reference's non-FP8 path.  The input projections
+(``fused_wqa_wkv``, ``wq_b``, compressor ``kv_score``, ``o_gate``) are
+torch/cuBLAS GEMMs.
 """
 
 from __future__ import annotations
@@ -70,14 +76,30 @@ class Ernie5_5HCAConfig:
 
 
 def make_vllm_config(hf_config: Any, max_model_len: int = 131072, max_num_batched_tokens: int = 8192,
-                     kv_cache_dtype: str = "fp8", num_speculative_tokens: int = 0) -> SimpleNamespace:
+                     kv_cache_dtype: str = "fp8", num_speculative_tokens: int = 0,
+                     quant_config: Any = None) -> SimpleNamespace:
     """A duck-typed stand-in for the ``VllmConfig`` fields the module reads."""
     spec = SimpleNamespace(num_speculative_tokens=num_speculative_tokens) if num_speculative_tokens else None
     return SimpleNamespace(
         model_config=SimpleNamespace(hf_config=hf_config, max_model_len=max_model_len),
         cache_config=SimpleNamespace(cache_dtype=kv_cache_dtype, block_size=256),
         scheduler_config=SimpleNamespace(max_num_batched_tokens=max_num_batched_tokens),
-        speculative_config=spec, quant_config=None)
+        speculative_config=spec, quant_config=quant_config)
+
+
+def block_fp8_quant_config(ignored_layers: list[str] | None = None) -> SimpleNamespace:
+    """The ``Fp8Config`` fields of a 128 x 128 block-FP8 checkpoint."""
+    return SimpleNamespace(weight_block_size=[128, 128], ignored_layers=list(ignored_layers or []))
+
+
+def keeps_fp8_output(quant_config: Any) -> bool:
+    """Whether ``wo_a``/``wo_b`` run block FP8: a 128 x 128 block-FP8 config
+    that does not ignore ``wo_a`` (``keeps_fp8_wo_a``,
+    ``E/nvidia/quant_config.py``)."""
+    if quant_config is None or list(getattr(quant_config, "weight_block_size", None) or []) != [128, 128]:
+        return False
+    ignored = getattr(quant_config, "ignored_layers", None) or []
+    return not any(n.endswith(("linear_o_group_proj", ".attn.wo_a")) for n in ignored)
 
 
 def _tp(group) -> tuple[int, int]:
@@ -114,6 +136,8 @@ class VHAPostMix(nn.Module):
         self.V.weight_loader = self.load_local_heads
         if self.tp_size == 1:
             self.register_buffer("m", torch.eye(num_heads), persistent=False)
+            # the bf16 copy the fused VHA kernels read
+            self.register_buffer("m_bf16", torch.eye(num_heads, dtype=torch.bfloat16), persistent=False)
 
     def load_local_heads(self, param: nn.Parameter, loaded: torch.Tensor) -> None:
         rows = param.shape[0]
@@ -125,6 +149,7 @@ class VHAPostMix(nn.Module):
             return
         eye = torch.eye(self.U.shape[0], dtype=self.U.dtype, device=self.U.device)
         self.m.copy_(torch.addmm(eye, self.V, self.U.t()))
+        self.m_bf16.copy_(self.m)
 
     def forward(self, o: torch.Tensor) -> torch.Tensor:
         if self.tp_size == 1:
@@ -150,6 +175,18 @@ class _Linear(nn.Module):
 
     def forward(self, x):
         return x @ self.weight.t()
+
+
+class _FP8Linear(nn.Module):
+    """Block-FP8 weight: ``weight`` e4m3 ``[N, K]`` and ``weight_scale_inv``
+    fp32 ``[ceil(N / 128), K / 128]`` (the checkpoint names and layout of
+    vLLM's block-FP8 linears)."""
+
+    def __init__(self, in_features: int, out_features: int):
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(out_features, in_features, dtype=ops.FP8), requires_grad=False)
+        self.weight_scale_inv = nn.Parameter(
+            torch.empty((out_features + 127) // 128, in_features // 128, dtype=torch.float32), requires_grad=False)
 
 
 class _RMSNorm(nn.Module):
@@ -205,18 +242,21 @@ def _find_layer(name: str) -> nn.Module:
     return layer
 
 
-@torch.library.custom_op("hca_b200::hca_attention", mutates_args=("out",))
+@torch.library.custom_op("hca_b200::hca_attention", mutates_args=("out", "out_scale"))
 def hca_attention(q: torch.Tensor, kv: torch.Tensor, kv_score: torch.Tensor, positions: torch.Tensor,
-                  out: torch.Tensor, layer_name: str) -> None:
-    """The layer's attention (KV insert, compressor, sparse decode / prefill)
-    into ``out`` ``[T, H_local, D]``, reading this step's metadata from the
-    forward context."""
+                  out: torch.Tensor, out_scale: torch.Tensor, layer_name: str) -> None:
+    """The layer's attention (KV insert, compressor, sparse decode / prefill),
+    reading this step's metadata from the forward context, into either
+    ``out`` bf16 ``[T, H_local, D]`` (``out_scale`` empty), or, on the FP8
+    output path, ``wo_a``'s quantised input: ``out`` e4m3 ``[G, T, HPG * D]``
+    of VHA + inverse RoPE and ``out_scale`` int32 ``[G, HPG, round_up(T, 4)]``
+    UE8M0 exponents."""
     layer = _find_layer(layer_name)
-    layer._attention(q, kv, kv_score, positions, out, get_forward_context().attn_metadata)
+    layer._attention(q, kv, kv_score, positions, out, out_scale, get_forward_context().attn_metadata)
 
 
 @hca_attention.register_fake
-def _hca_attention_fake(q, kv, kv_score, positions, out, layer_name):
+def _hca_attention_fake(q, kv, kv_score, positions, out, out_scale, layer_name):
     return None
 
 
@@ -260,8 +300,19 @@ class Ernie5_5HCAAttention(nn.Module):
         self.q_norm = _RMSNorm(self.q_lora_rank, dtype)
         self.wq_b = _Linear(self.q_lora_rank, self.n_local_heads * self.head_dim, dtype)
         self.kv_norm = _RMSNorm(self.head_dim, dtype)
-        self.wo_a = _Linear(self.n_heads * self.head_dim // self.n_groups, self.n_local_groups * self.o_lora_rank, dtype)
-        self.wo_b = _Linear(self.n_local_groups * self.o_lora_rank, self.hidden_size, dtype)
+        wo_a_in = self.n_heads * self.head_dim // self.n_groups
+        # block-FP8 wo_a/wo_b where the reference keeps them FP8 and the
+        # blocks tile the groups (o_lora_rank and the group width multiples
+        # of 128; wo_b's input quant packs four 128-blocks per int32)
+        self.fp8_output = (keeps_fp8_output(getattr(vllm_config, "quant_config", None))
+                           and self.o_lora_rank % 128 == 0 and wo_a_in % (128 if tp_size == 1 else 512) == 0
+                           and (self.n_local_groups * self.o_lora_rank) % 512 == 0)
+        if self.fp8_output:
+            self.wo_a = _FP8Linear(wo_a_in, self.n_local_groups * self.o_lora_rank)
+            self.wo_b = _FP8Linear(self.n_local_groups * self.o_lora_rank, self.hidden_size)
+        else:
+            self.wo_a = _Linear(wo_a_in, self.n_local_groups * self.o_lora_rank, dtype)
+            self.wo_b = _Linear(self.n_local_groups * self.o_lora_rank, self.hidden_size, dtype)
         self.o_gate = _Linear(self.q_lora_rank, self.n_local_groups * self.o_lora_rank, dtype)
         self.vha = VHAPostMix(self.n_heads, tp_group=tp_group)
         self.attn_sink = nn.Parameter(torch.full((max(self.n_local_heads, 64),), -float("inf")),
@@ -301,19 +352,33 @@ class Ernie5_5HCAAttention(nn.Module):
         qr, kv = qr_kv.split([self.q_lora_rank, d], dim=-1)
         qr, kv = ops.fused_q_kv_rmsnorm(qr, kv, self.q_norm.weight, self.kv_norm.weight, self.eps)
         q = self.wq_b(qr).view(T, self.n_local_heads, d)
-        gate = torch.sigmoid(self.o_gate(qr))
+        # the FP8 path's wo_b input quant applies the sigmoid itself
+        gate = self.o_gate(qr) if self.fp8_output else torch.sigmoid(self.o_gate(qr))
         attn_metadata = get_forward_context().attn_metadata
-        o = torch.empty((T, self.n_local_heads, d), dtype=hidden_states.dtype, device=hidden_states.device)
+        dev = hidden_states.device
+        if self.fp8_output and self.vha.tp_size == 1:
+            # VHA + inverse RoPE + FP8 quant inside the attention op
+            hpg = self.n_local_heads // self.n_local_groups
+            o = torch.empty((self.n_local_groups, T, hpg * d), dtype=ops.FP8, device=dev)
+            o_scale = torch.empty((self.n_local_groups, hpg, ops._aligned(T)), dtype=torch.int32, device=dev)
+        else:
+            o = torch.empty((T, self.n_local_heads, d), dtype=hidden_states.dtype, device=dev)
+            o_scale = torch.empty(0, dtype=torch.int32, device=dev)
         if not isinstance(attn_metadata, dict):  # profile / dummy run
-            o.zero_()
+            o.view(torch.uint8).zero_() if o.dtype == ops.FP8 else o.zero_()
+            o_scale.fill_(127)
         else:
             # the attention part is one opaque op that writes `o` in place (an
             # eager break under graph compilation, as the reference's)
-            torch.ops.hca_b200.hca_attention(q, kv, kv_score, positions, o, self.layer_name)
+            torch.ops.hca_b200.hca_attention(q, kv, kv_score, positions, o, o_scale, self.layer_name)
+        if o.dtype == ops.FP8:
+            return self._output_fp8(o.transpose(0, 1), o_scale.permute(2, 0, 1)[:T], gate)
         return self._output(o, positions, gate)
 
-    def _attention(self, q, kv, kv_score, positions, o, md: dict) -> None:
+    def _attention(self, q, kv, kv_score, positions, o, o_scale, md: dict) -> None:
         d, r = self.head_dim, self.rope_head_dim
+        quant = o.dtype == ops.FP8  # o: wo_a's FP8 input [G, T, HPG*D], o_scale its exponents
+        T = o.shape[1] if quant else o.shape[0]
         swa = md[f"{self.prefix}.swa_cache"]
         c128 = md[self.prefix]
         comp = md[self.compressor.state_cache_prefix]
@@ -345,19 +410,42 @@ class Ernie5_5HCAAttention(nn.Module):
                 c128.decode_items = max(sms if d == 128 else sms // 2, groups)
                 c128.decode_schedule = ops.decode_schedule(swa.decode_group_starts, ndt, swa.decode_swa_lens,
                                                            c128.c128a_decode_topk_lens, c128.decode_items)
+            if quant and ndt == T and d == 128 and self.n_local_heads % 16 == 0 and self.n_local_heads <= 64:
+                # decode-only step: attention, split merge, VHA, inverse RoPE
+                # and FP8 quant in two launches (no bf16 O round trip)
+                ops.sparse_decode_vha_fp8_quant(
+                    qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,
+                    self.kv_cache, self.comp_page, c128.c128a_global_decode_topk_indices, c128.c128a_decode_topk_lens,
+                    self.scale, sink, swa.decode_group_starts, swa.decode_max_group_tokens, c128.decode_schedule,
+                    c128.decode_items, self.vha.m_bf16, positions, self.cos_sin_cache, self.n_local_groups, r,
+                    out=o, scale_out=o_scale)
+                return
+        ob = torch.empty((T, self.n_local_heads, d), dtype=q.dtype, device=q.device) if quant else o
+        if ndt:
             ops.sparse_decode(qp[:ndt], self.swa_cache, SWA_BLOCK_SIZE, swa.decode_swa_indices, swa.decode_swa_lens,
                               self.kv_cache, self.comp_page, c128.c128a_global_decode_topk_indices,
-                              c128.c128a_decode_topk_lens, self.scale, sink, out=o[:ndt],
+                              c128.c128a_decode_topk_lens, self.scale, sink, out=ob[:ndt],
                               group_starts=swa.decode_group_starts, max_group_tokens=swa.decode_max_group_tokens,
                               rope_dim=r, schedule=c128.decode_schedule, max_items=c128.decode_items)
         if swa.num_prefills:
             qsl = swa.query_start_loc[nd:] - ndt
             ops.sparse_prefill(qp[ndt:n], qsl, swa.seq_lens[nd:], self.swa_cache, SWA_BLOCK_SIZE,
                                swa.block_table[nd:], self.kv_cache, self.comp_page, c128.block_table[nd:],
-                               self.window_size, self.compress_ratio, self.scale, sink, out=o[ndt:n], rope_dim=r)
+                               self.window_size, self.compress_ratio, self.scale, sink, out=ob[ndt:n], rope_dim=r)
+        if quant:
+            if n < T:
+                ob[n:].zero_()  # padding rows: finite values for the quant
+            ops.vha_inv_rope_fp8_quant(ob, self.vha.m_bf16, positions, self.cos_sin_cache, self.n_local_groups,
+                                       self.nope_head_dim, r, out=o, scale_out=o_scale)
 
     def _output(self, o, positions, gate):
         T = o.shape[0]
+        if self.fp8_output:
+            # head-sharded TP: VHA with its all-reduce, then inverse RoPE + quant
+            x, xs = ops.fused_inv_rope_fp8_quant(self.vha(o), positions, self.cos_sin_cache, self.n_local_groups,
+                                                 self.n_local_heads // self.n_local_groups, self.nope_head_dim,
+                                                 self.rope_head_dim)
+            return self._output_fp8(x, xs, gate)
         if self.vha.tp_size == 1:
             o = ops.vha_inv_rope(o, self.vha.m.to(o.dtype), positions, self.cos_sin_cache, self.rope_head_dim)
         else:
@@ -366,6 +454,23 @@ class Ernie5_5HCAAttention(nn.Module):
         wa = self.wo_a.weight.view(self.n_local_groups, self.o_lora_rank, -1)  # [G, o_lora, HPG*D]
         z = torch.bmm(og, wa.transpose(1, 2)).transpose(0, 1).reshape(T, -1)  # [T, G*o_lora]
         y = self.wo_b(z * gate)
+        if self.tp_group is not None and self.vha.tp_size > 1:
+            dist.all_reduce(y, group=self.tp_group)
+        return y
+
+    def _output_fp8(self, x, xs, gate_logits):
+        """The reference's FP8 output path (``V/models/deepseek_v4/attention.py:317-347``
+        and the gated ``wo_b`` of ``E/nvidia/attention.py:364-395,466-469``):
+        grouped ``wo_a`` on ``x`` (e4m3 ``[T, G, HPG*D]``, UE8M0 exponents
+        ``xs`` ``[T, G, packs]``) -> ``z`` bf16 ``[T, G * o_lora]`` ->
+        ``z * sigmoid(gate)`` quantised 1x128 -> ``wo_b`` (all-reduced over
+        the TP group)."""
+        G, L = self.n_local_groups, self.o_lora_rank
+        T, K = x.shape[0], x.shape[2]
+        z = ops.fp8_grouped_gemm(x, xs, self.wo_a.weight.view(G, L, K),
+                                 self.wo_a.weight_scale_inv.view(G, L // 128, K // 128))
+        zq, zs = ops.sigmoid_mul_quant_fp8(z.view(T, G * L), gate_logits)
+        y = ops.fp8_grouped_gemm(zq, zs, self.wo_b.weight, self.wo_b.weight_scale_inv)
         if self.tp_group is not None and self.vha.tp_size > 1:
             dist.all_reduce(y, group=self.tp_group)
         return y
@@ -389,6 +494,9 @@ class Ernie5_5HCAAttention(nn.Module):
                          "compressor.fused_wkv_wgate.weight": [self.head_dim, self.head_dim]}[name]
                 off = sum(sizes[:shard])
                 p.data[off:off + sizes[shard]].copy_(w)
+            elif self.fp8_output and name in ("wo_a.weight", "wo_a.weight_scale_inv", "wo_b.weight",
+                                              "wo_b.weight_scale_inv"):
+                self._load_fp8(name, p, w)
             elif name in ("wq_b.weight", "wo_a.weight", "o_gate.weight"):
                 rows = p.shape[0]
                 p.data.copy_(w[self.tp_rank * rows:(self.tp_rank + 1) * rows])
@@ -399,6 +507,31 @@ class Ernie5_5HCAAttention(nn.Module):
                 p.data.copy_(w)
             loaded.add(name)
         return loaded
+
+    def _load_fp8(self, name: str, p: nn.Parameter, w: torch.Tensor) -> None:
+        """This rank's slice of a block-FP8 ``wo_a`` (rows) or ``wo_b``
+        (columns) weight or its block scales.  A weight that arrives in
+        bf16/fp32 is quantised to 128 x 128 block FP8 here (power-of-two
+        scales), filling ``weight_scale_inv`` too."""
+        lin = self.wo_a if name.startswith("wo_a") else self.wo_b
+        by_rows = name.startswith("wo_a")
+        rows, cols = lin.weight.shape
+
+        def local(t, block):
+            if by_rows:
+                n = rows // block
+                return t[self.tp_rank * n:(self.tp_rank + 1) * n]
+            n = cols // block
+            return t[:, self.tp_rank * n:(self.tp_rank + 1) * n]
+
+        if name.endswith("weight_scale_inv"):
+            p.data.copy_(local(w, 128).float())
+        elif w.dtype == ops.FP8:
+            p.data.copy_(local(w, 1))
+        else:
+            q, sc = ops.quantize_weight_block_fp8(local(w, 1).to(torch.float32))
+            lin.weight.data.copy_(q)
+            lin.weight_scale_inv.data.copy_(sc)
 
 
 def _layer_index(prefix: str) -> int:

@@ -369,16 +369,29 @@ def _aligned(n: int) -> int:
     return (n + 3) // 4 * 4
 
 
+def _quant_out(out, scale, n_groups: int, t: int, hpg: int, d: int, device):
+    """The ``(data [G, T, HPG*D] e4m3, scale [G, HPG, round_up(T, 4)] int32)``
+    buffers of the VHA quant: the caller's or new ones."""
+    if out is None:
+        out = torch.empty((n_groups, t, hpg * d), dtype=FP8, device=device)
+    if scale is None:
+        scale = torch.empty((n_groups, hpg, _aligned(t)), dtype=torch.int32, device=device)
+    assert out.shape == (n_groups, t, hpg * d) and out.dtype == FP8 and out.is_contiguous()
+    assert scale.shape == (n_groups, hpg, _aligned(t)) and scale.dtype == torch.int32 and scale.is_contiguous()
+    return out, scale
+
+
 def vha_inv_rope_fp8_quant(o, mix, positions, cos_sin_cache, n_groups: int, nope_dim: int,
-                           rope_dim: int):
+                           rope_dim: int, out=None, scale_out=None):
     """``E/nvidia/attention.py:232-285``: returns ``(data [T, G, HPG*D] e4m3,
-    scale [T, G, HPG] int32)`` views with the plugin's strides."""
+    scale [T, G, HPG] int32)`` views with the plugin's strides (of ``out``
+    ``[G, T, HPG*D]`` and ``scale_out`` ``[G, HPG, round_up(T, 4)]`` when
+    given)."""
     _check_cuda(o, mix, positions, cos_sin_cache)
     t, h, d = o.shape
     assert d == nope_dim + rope_dim and o.stride(-1) == 1
     hpg = h // n_groups
-    out = torch.empty((n_groups, t, hpg * d), dtype=FP8, device=o.device)
-    scale = torch.empty((n_groups, hpg, _aligned(t)), dtype=torch.int32, device=o.device)
+    out, scale = _quant_out(out, scale_out, n_groups, t, hpg, d, o.device)
     if t:
         call("hca_vha_inv_rope_fp8_quant", _p(out), _p(scale), _p(o), o.stride(0), o.stride(1),
              _p(mix), _p(positions), _p(cos_sin_cache), cos_sin_cache.stride(0), t, h, n_groups, d,
@@ -390,7 +403,7 @@ def sparse_decode_vha_fp8_quant(q, swa_cache, swa_block_size: int, swa_indices, 
                                 comp_block_size: int, comp_indices, comp_lens, softmax_scale: float,
                                 attn_sink, group_starts, max_group_tokens: int, schedule, max_items: int,
                                 mix, positions, cos_sin_cache, n_groups: int, rope_dim: int = 64,
-                                workspace: DecodeWorkspace | None = None):
+                                workspace: DecodeWorkspace | None = None, out=None, scale_out=None):
     """Decode attention (scheduled) fused with the VHA mix, inverse RoPE and
     FP8 quant: ``sparse_decode`` followed by ``vha_inv_rope_fp8_quant`` in two
     launches, without the bf16 O round trip.  Returns the same
@@ -398,8 +411,7 @@ def sparse_decode_vha_fp8_quant(q, swa_cache, swa_block_size: int, swa_indices, 
     _check_cuda(q, swa_cache, swa_indices, swa_lens, mix, positions, cos_sin_cache, schedule)
     t, h, d = q.shape
     hpg = h // n_groups
-    out = torch.empty((n_groups, t, hpg * d), dtype=FP8, device=q.device)
-    scale = torch.empty((n_groups, hpg, _aligned(t)), dtype=torch.int32, device=q.device)
+    out, scale = _quant_out(out, scale_out, n_groups, t, hpg, d, q.device)
     if t == 0:
         return out.transpose(0, 1), scale.permute(2, 0, 1)[:t]
     si = swa_indices.reshape(swa_indices.shape[0], -1)
