@@ -40,6 +40,11 @@ extern "C" {
 #define HCA_NOALLOC_WORKSPACE_BYTES (16ll * 1024 * 1024)
 
 const char* hca_status_string(int status);
+
+/* The CUDA error string behind this thread's last HCA_E_CUDA status (a
+ * library diagnostic with no counterpart in the reference). */
+const char* hca_last_cuda_error(void);
+
 /* Library ABI version (major * 100 + minor). */
 int hca_version(void);
 /* Device error word of the current device (synchronous read): non-zero if a

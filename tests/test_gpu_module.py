@@ -76,14 +76,17 @@ def _block_fp8(weights: dict, names=("wo_a.weight", "wo_b.weight")):
     return ckpt, deq
 
 
-@pytest.mark.parametrize("head_dim,fp8", [(128, False), (512, False), (128, True), (512, True)])
-def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim, fp8):
+@pytest.mark.parametrize("head_dim,fp8,aux", [(128, False, False), (512, False, False), (128, True, False),
+                                              (512, True, False), (128, True, True)])
+def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim, fp8, aux):
     """head_dim 128 is config 1; 512 is the model's own head size (the CTA-pair
     attention kernel, head_dim-512 cache rows, compressor and output path).
     ``fp8``: a 128 x 128 block-FP8 checkpoint (rank-128 groups), so the module
     runs the reference's FP8 output path (fused VHA + quant on the decode
     step, the tcgen05 FP8 GEMMs for wo_a and gated wo_b), against the
-    oracle's FP8 output path on the same block-FP8 weights."""
+    oracle's FP8 output path on the same block-FP8 weights.  ``aux``: the
+    model's two aux streams (kv_score beside fused_wqa_wkv, the gate beside
+    attention); the output must equal the serial run's bit for bit."""
     from vllm_ernie_b200 import attention as A
     from vllm_ernie_b200.cache_layout import page_bytes
     from vllm_ernie_b200.forward_context import set_forward_context
@@ -102,8 +105,10 @@ def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim, fp8):
                               hybrid_mla_num_attention_heads=16, num_nextn_predict_layers=0,
                               compress_rope_theta=shape.rope_theta)
     quant = A.block_fp8_quant_config() if fp8 else None
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()] if aux else None
     layer = A.Ernie5_5HCAAttention(A.make_vllm_config(cfg, max_model_len=max_len, num_speculative_tokens=2,
-                                                      quant_config=quant), prefix=PREFIX).to(DEV)
+                                                      quant_config=quant), prefix=PREFIX,
+                                   aux_stream_list=streams).to(DEV)
     assert layer.fp8_output == fp8
     loaded = layer.load_weights(list(ckpt.items()))
     assert loaded == set(ckpt)
@@ -136,6 +141,13 @@ def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim, fp8):
         md, pos_d = _metadata(layer, oracle.swa_bt, oracle.comp_bt, oracle.state_bt, qsl, seq_lens, positions, spec)
         with set_forward_context(md):
             y = layer(pos_d, hidden_bf16.to(DEV))
+            if aux:
+                # the same step serially (the cache writes repeat the same bytes)
+                layer.aux_stream_list = None
+                y_serial = layer(pos_d, hidden_bf16.to(DEV))
+                layer.aux_stream_list = streams
+                torch.cuda.synchronize()
+                assert torch.equal(y, y_serial)
         torch.cuda.synchronize()
         got = y.float().cpu().numpy()
         assert np.isfinite(got).all()

@@ -13,4 +13,13 @@ extern "C" const char* hca_status_string(int status) {
   }
 }
 
+namespace hca {
+const char*& last_cuda_error() {
+  thread_local const char* msg = "no CUDA error recorded";
+  return msg;
+}
+}  // namespace hca
+
+extern "C" const char* hca_last_cuda_error(void) { return hca::last_cuda_error(); }
+
 extern "C" int hca_version(void) { return 100; }

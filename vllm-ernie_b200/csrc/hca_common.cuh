@@ -14,7 +14,7 @@
     if (!(cond)) return HCA_E_INVALID; \
   } while (0)
 
-#define HCA_LAUNCH_STATUS() (cudaGetLastError() == cudaSuccess ? HCA_OK : HCA_E_CUDA)
+#define HCA_LAUNCH_STATUS() (::hca::cuda_status(cudaGetLastError()))
 
 namespace hca {
 
@@ -71,6 +71,17 @@ __device__ __forceinline__ void pdl_wait_and_release() {
   pdl_release();
 }
 
+// The CUDA error behind the last HCA_E_CUDA status of this thread
+// (hca_last_cuda_error).
+const char*& last_cuda_error();
+
+// HCA_OK, or HCA_E_CUDA with the error recorded for hca_last_cuda_error.
+inline int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return HCA_OK;
+  last_cuda_error() = cudaGetErrorString(e);
+  return HCA_E_CUDA;
+}
+
 template <typename... KArgs, typename... Args>
 inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchAttribute attr[1];
@@ -83,7 +94,7 @@ inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? HCA_OK : HCA_E_CUDA;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 
 inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }

@@ -6,21 +6,28 @@
 //   gated wo_b     y = W_b . q(z * g), the same GEMM with G = 1 on the output of
 //                  the fused sigmoid gate quant (E/nvidia/attention.py:364-395).
 //
-// One CTA per (128-token tile, N tile, group); 6 warps:
+// Swap-AB: the weight is the MMA's M = 128 operand and the token tile (TT <=
+// 192 tokens) its N, so at decode sizes (a few hundred tokens) one CTA reads
+// each weight byte once for all tokens.  CTA (split rank r, 128-row weight
+// tile, group x token tile), a cluster of `split` CTAs along K.  10 warps:
 //   warp 0     TMA producer (lane 0): per 128-wide K block, the 128 x 128-byte
-//              x box and the N_TILE x 128-byte weight box, 128B-swizzled, into
-//              a kStages-deep ring (rows past the token count read as zero)
+//              weight box and the TT x 128-byte token box, 128B-swizzled,
+//              into a kStages-deep ring (tokens past T read as zero)
 //   warp 1     TMEM owner and MMA issuer (lane 0): tcgen05.mma.kind::f8f6f4,
-//              M128 x N_TILE x K32, e4m3 x e4m3 -> fp32; K block kb
-//              accumulates into TMEM buffer kb % kAccBufs, so the block scales
-//              (per token and per weight block) are applied once per block
-//   warps 2-5  epilogue: one token row per lane (TMEM lane quadrant =
-//              warp % 4); per K block, acc_kb * sx[t, kb] * sw[kb] added to
-//              fp32 registers (the promotion of DeepGEMM's block-scaled GEMM),
-//              the buffer handed back to the MMA warp, the sum rounded to bf16
+//              M128 x N=TT x K32, e4m3 x e4m3 -> fp32; K block i of this CTA
+//              accumulates into TMEM buffer i % 2, so the block scales (one
+//              per weight block, one per token) are applied once per block
+//   warps 2-9  epilogue: weight row = TMEM lane (quadrant warp % 4), half of
+//              the token columns each; per K block, acc * sw[kb] * sx[t, kb]
+//              added to fp32 registers (the promotion step of DeepGEMM's
+//              block-scaled GEMM), the buffer handed back to the MMA warp
+// The CTA's partial [TT x 128] fp32 tile goes to its shared memory; after a
+// cluster barrier CTA r sums rank-r's token slice over the cluster's partial
+// tiles (distributed shared memory), rounds to bf16 and stores coalesced rows.
 // Every mbarrier wait is bounded; a timeout sets the device error word, and
 // the producer and MMA threads wait (bounded) for their copies and MMAs in
-// flight before the CTA frees its TMEM and exits.
+// flight before the CTA frees its TMEM; the cluster barriers are taken by
+// every thread on every path.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -34,20 +41,29 @@ namespace hca {
 namespace {
 
 constexpr int kStages = 4;
-constexpr int kAccBufs = 4;
-constexpr int kThreads = 192;
-constexpr int kBoxBytes = 128 * 128;  // one 128 x 128-byte swizzled box
+constexpr int kAccBufs = 2;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kWBox = 128 * 128;  // one 128-row x 128-byte weight box
+constexpr int kPStride = 128 + 4;  // floats per token row of the partial tile (bank spread)
+constexpr int kMaxSplit = 8;
+constexpr int kMaxKBlocks = 64;  // K blocks of one CTA (its scale table)
 
-template <int N_TILE>
+template <int TT>
 struct GemmSmem {
-  static constexpr int kA = 0;
-  static constexpr int kB = kStages * kBoxBytes;
-  static constexpr int kBBytes = N_TILE * 128;
-  // full[kStages] empty[kStages] acc_full[kAccBufs] acc_empty[kAccBufs] drain
-  static constexpr int kBar = kB + kStages * kBBytes;
+  static constexpr int kXBox = TT * 128;
+  static constexpr int kStage = kWBox + kXBox;
+  static constexpr int kPipe = kStages * kStage;
+  static constexpr int kPart = TT * kPStride * 4;  // reuses the ring after the K loop
+  static constexpr int kBody = kPipe > kPart ? kPipe : kPart;
+  static constexpr int kScale = kBody;  // [kMaxKBlocks][TT] floats: sx * sw of each K block and token
+  static constexpr int kBar = kScale + kMaxKBlocks * TT * 4 + kMaxKBlocks * 4;
+  // full[kStages] empty[kStages] acc_full[2] acc_empty[2] drain
   static constexpr int kMisc = kBar + (2 * kStages + 2 * kAccBufs + 1) * 8;
   static constexpr int kBytes = kMisc + 64 + 1024;  // + 1024 alignment slack
-  static constexpr int kTmemCols = N_TILE * kAccBufs;
+  static constexpr int kTmemCols = TT * kAccBufs <= 256 ? 256 : 512;
+  static_assert(kBytes <= 227 * 1024, "shared memory");
+  static_assert(TT % 64 == 0 && TT <= 192, "token tile");
 };
 
 struct GemmArgs {
@@ -59,6 +75,7 @@ struct GemmArgs {
   const float* ws;         // weight scales [G][ceil(N / 128)][K / 128]
   int T, G, N, K;
   int n_blocks;            // ceil(N / 128)
+  int split;               // CTAs per cluster along K
   uint64_t wait_ns;
 };
 
@@ -86,12 +103,15 @@ __device__ __forceinline__ uint32_t pack_bf16_rn(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <int N_TILE>
+// 10 warps: at most 168 registers a thread (three warps share one SM
+// sub-partition's 16K registers); the epilogue holds up to 96 fp32 partial
+// sums per lane
+template <int TT>
 __global__ void __launch_bounds__(kThreads, 1)
     hca_fp8_gemm_kernel(const GemmArgs A, int* err, const __grid_constant__ CUtensorMap xmap,
                         const __grid_constant__ CUtensorMap wmap) {
   using namespace tc;
-  using L = GemmSmem<N_TILE>;
+  using L = GemmSmem<TT>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   // TMEM is allocated after the wait (the kernel before may hold columns on
@@ -99,8 +119,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // columns before its own wait cannot starve this CTA)
   pdl_wait();  // x and its scales were written by the kernel before this one
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * N_TILE, g = blockIdx.z;
+  const int split = A.split;
+  const int rank = static_cast<int>(blockIdx.x);  // rank in the cluster (cluster = the grid's x extent)
+  const int n0 = blockIdx.y * 128;
+  const int g = static_cast<int>(blockIdx.z) % A.G;
+  const int t0 = (static_cast<int>(blockIdx.z) / A.G) * TT;
   const int nkb = A.K / 128;
+  const int kb0 = rank * nkb / split, nk = (rank + 1) * nkb / split - kb0;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
@@ -119,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, 4);  // lane 0 of each epilogue warp
+      mbar_init(acc_empty + b, kEpiWarps);  // lane 0 of each epilogue warp
     }
     mbar_init(drain, 1);
     mbar_fence_init();
@@ -128,102 +153,205 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   pdl_release();
   const uint32_t tmem = misc[0];
-  if (warp == 0 && lane == 0) {
+  float o[TT / 2];  // epilogue: this lane's weight row over this warp's token half
+  bool ok = true;
+  if (warp == 0) {
     // ---------------------------------------------------------------- TMA
-    bool ok = true;
-    int issued = 0;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kStages;
-      if (kb >= kStages && !mbar_wait(empty + s, ((kb / kStages) - 1) & 1, A.wait_ns)) {
-        ok = false;
-        break;
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, A.wait_ns)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * L::kStage;
+        mbar_arrive_expect_tx(full + s, L::kStage);
+        tma_load_3d(st, &wmap, (kb0 + i) * 128, n0, g, full + s);
+        tma_load_3d(st + kWBox, &xmap, (kb0 + i) * 128, t0, g, full + s);
+        issued = i + 1;
       }
-      mbar_arrive_expect_tx(full + s, kBoxBytes + L::kBBytes);
-      tma_load_3d(smem + L::kA + s * kBoxBytes, &xmap, kb * 128, m0, g, full + s);
-      tma_load_3d(smem + L::kB + s * L::kBBytes, &wmap, kb * 128, n0, g, full + s);
-      issued = kb + 1;
+      // the copies still in flight land before the ring is reused
+      for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+        ok &= mbar_wait(full + i % kStages, (i / kStages) & 1, A.wait_ns);
+      if (!ok && err) atomicOr(err, 1 << 7);
     }
-    // the copies still in flight land before the CTA exits
-    for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
-      ok &= mbar_wait(full + kb % kStages, (kb / kStages) & 1, A.wait_ns);
-    if (!ok && err) atomicOr(err, 1 << 7);
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
-    bool ok = true;
-    const uint32_t idesc = umma_idesc_e4m3(128, N_TILE);
-    const uint64_t da = umma_desc_sw128(smem_u32(smem + L::kA), 16, 1024);
-    const uint64_t dw = umma_desc_sw128(smem_u32(smem + L::kB), 16, 1024);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % kStages, b = kb % kAccBufs;
-      if (!mbar_wait(full + s, (kb / kStages) & 1, A.wait_ns) ||
-          (kb >= kAccBufs && !mbar_wait(acc_empty + b, ((kb / kAccBufs) - 1) & 1, A.wait_ns))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_e4m3(128, TT);
+      const uint64_t d0 = umma_desc_sw128(smem_u32(smem), 16, 1024);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % kStages, b = i % kAccBufs;
+        if (!mbar_wait(full + s, (i / kStages) & 1, A.wait_ns) ||
+            (i >= kAccBufs && !mbar_wait(acc_empty + b, ((i / kAccBufs) - 1) & 1, A.wait_ns))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t so = static_cast<uint32_t>(s * L::kStage);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)  // 32 e4m3 (32 bytes) of K per MMA
-        umma_f8(tmem + b * N_TILE, da + ((s * kBoxBytes + kk * 32) >> 4), dw + ((s * L::kBBytes + kk * 32) >> 4),
-                idesc, kk > 0 ? 1u : 0u);
-      umma_commit(empty + s);
-      umma_commit(acc_full + b);
+        for (int kk = 0; kk < 4; ++kk)  // 32 e4m3 (32 bytes) of K per MMA
+          umma_f8(tmem + b * TT, d0 + ((so + kk * 32) >> 4), d0 + ((so + kWBox + kk * 32) >> 4), idesc,
+                  kk > 0 ? 1u : 0u);
+        umma_commit(empty + s);
+        umma_commit(acc_full + b);
+      }
+      // every MMA issued completes before the ring and the TMEM are reused
+      umma_commit(drain);
+      ok &= mbar_wait(drain, 0, A.wait_ns);
+      if (!ok && err) atomicOr(err, 1 << 7);
     }
-    // every MMA issued completes before the TMEM is freed
-    umma_commit(drain);
-    ok &= mbar_wait(drain, 0, A.wait_ns);
-    if (!ok && err) atomicOr(err, 1 << 7);
-  } else if (warp >= 2) {
+  } else {
     // ----------------------------------------------------------- epilogue
-    const int quad = warp & 3;
-    const int t = m0 + quad * 32 + lane;
-    const int64_t wbase = (static_cast<int64_t>(g) * A.n_blocks + n0 / 128) * nkb;
-    auto block_scale = [&](int kb) -> float {
-      float sx = 0.0f;
-      if (t < A.T) {
-        const int32_t v = A.xs[t * A.xs_t + g * A.xs_g + (kb / A.per_int) * A.xs_k];
-        sx = exp2i(static_cast<int>((static_cast<uint32_t>(v) >> (8 * (kb % A.per_int))) & 0xffu) - 127);
-      }
-      return sx * A.ws[wbase + kb];
-    };
+    constexpr int kCols = TT / 2;     // token columns of this warp
+    constexpr int kHalf = kCols / 2;  // columns per TMEM round trip
+    const int e = warp - 2;
+    const int quad = warp & 3, c0 = (e >> 2) * kCols;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    float o[N_TILE];
+    // the scale of every (K block, token) of this CTA, weight scale folded
+    // in, loaded once while the ring fills (tokens past T: 0)
+    float* tab = reinterpret_cast<float*>(smem + L::kScale);
+    {
+      // each packed scale int of the CTA's (K block, token) range loaded once
+      // (up to kU per thread, all in flight together), with this CTA's weight
+      // block scales staged in shared memory first
+      constexpr int kU = 8, kStep = 32 * kEpiWarps;
+      float* wtab = tab + kMaxKBlocks * TT;  // [kMaxKBlocks]
+      const int tid = threadIdx.x - 64;
+      const int p0 = kb0 / A.per_int, npk = (kb0 + nk - 1) / A.per_int - p0 + 1;
+      const int total = npk * TT;
+      const float wv = tid < nk ? A.ws[(static_cast<int64_t>(g) * A.n_blocks + n0 / 128) * nkb + kb0 + tid] : 0.0f;
+      int32_t xv[kU];
+      auto load = [&](int base) {
 #pragma unroll
-    for (int e = 0; e < N_TILE; ++e) o[e] = 0.0f;
-    bool ok = true;
-    float sc_next = block_scale(0);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const float sc = sc_next;
-      if (kb + 1 < nkb) sc_next = block_scale(kb + 1);  // in flight during the wait
-      const int b = kb % kAccBufs;
-      if (!mbar_wait(acc_full + b, (kb / kAccBufs) & 1, A.wait_ns)) {
+        for (int u = 0; u < kU; ++u) {
+          const int idx = base + u * kStep;
+          const int pk = idx / TT, t = t0 + idx - pk * TT;
+          xv[u] = 0;
+          if (idx < total && t < A.T) xv[u] = A.xs[t * A.xs_t + g * A.xs_g + (p0 + pk) * A.xs_k];
+        }
+      };
+      auto expand = [&](int base) {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int idx = base + u * kStep;
+          if (idx < total) {
+            const int pk = idx / TT, tl = idx - pk * TT;
+            const bool live = t0 + tl < A.T;
+            for (int c = 0; c < A.per_int; ++c) {
+              const int kq = (p0 + pk) * A.per_int + c - kb0;
+              if (kq >= 0 && kq < nk) {
+                const int ex = static_cast<int>((static_cast<uint32_t>(xv[u]) >> (8 * c)) & 0xffu);
+                tab[kq * TT + tl] = live ? exp2i(ex - 127) * wtab[kq] : 0.0f;
+              }
+            }
+          }
+        }
+      };
+      load(tid);  // every epilogue thread, in-range or not, reaches the barrier below
+      if (tid < nk) wtab[tid] = wv;
+      asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kEpiWarps) : "memory");
+      expand(tid);
+      for (int base = tid + kU * kStep; base < total; base += kU * kStep) {
+        load(base);
+        expand(base);
+      }
+      asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kEpiWarps) : "memory");  // the epilogue warps
+    }
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) o[j] = 0.0f;
+    for (int i = 0; i < nk; ++i) {
+      const int b = i % kAccBufs;
+      if (!mbar_wait(acc_full + b, (i / kAccBufs) & 1, A.wait_ns)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const float* sc = tab + i * TT + c0;
 #pragma unroll
-      for (int c = 0; c < N_TILE / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_addr + b * N_TILE + c * 32, v);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v[kHalf];
+#pragma unroll
+        for (int c = 0; c < kHalf / 16; ++c) tmem_ld16(tmem + lane_addr + b * TT + c0 + h * kHalf + c * 16, v + c * 16);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[c * 32 + e] = fmaf(__uint_as_float(v[e]), sc, o[c * 32 + e]);
+        for (int q = 0; q < kHalf / 4; ++q) {
+          const float4 s4 = *reinterpret_cast<const float4*>(sc + h * kHalf + q * 4);
+          float* oo = o + h * kHalf + q * 4;
+          oo[0] = fmaf(__uint_as_float(v[q * 4 + 0]), s4.x, oo[0]);
+          oo[1] = fmaf(__uint_as_float(v[q * 4 + 1]), s4.y, oo[1]);
+          oo[2] = fmaf(__uint_as_float(v[q * 4 + 2]), s4.z, oo[2]);
+          oo[3] = fmaf(__uint_as_float(v[q * 4 + 3]), s4.w, oo[3]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + b);
     }
     if (!ok && lane == 0 && err) atomicOr(err, 1 << 7);
-    if (ok && t < A.T) {
-      uint4* dst = reinterpret_cast<uint4*>(A.out + static_cast<int64_t>(t) * A.out_st +
-                                            static_cast<int64_t>(g) * A.out_sg + n0);
+  }
+  // Split-K: CTA r owns tokens [r S, (r + 1) S) of the tile (S = TT /
+  // split).  Once every ring of the cluster is idle (copies landed, MMAs
+  // done), each CTA stores its partial sums of CTA r's tokens into CTA r's
+  // ring, rows [q S, (q + 1) S) for source rank q (posted stores into the
+  // owner's shared memory, no round trips); after a second cluster barrier
+  // each CTA sums its split rows and stores bf16.
+  __syncthreads();
+  if (split > 1) cluster_sync();
+  float* recv = reinterpret_cast<float*>(smem);  // [split][S][kPStride]
+  const int slice = TT / split;
+  if (warp >= 2) {
+    constexpr int kCols = TT / 2;
+    const int row = (warp & 3) * 32 + lane, c0 = ((warp - 2) >> 2) * kCols;
+    const uint32_t rbase = smem_u32(recv);
+    int owner = c0 / slice, tl = c0 - owner * slice;
+    uint32_t obase = split > 1 ? mapa_shared(rbase, static_cast<uint32_t>(owner)) : rbase;
 #pragma unroll
-      for (int q = 0; q < N_TILE / 8; ++q) {
+    for (int j = 0; j < kCols; ++j) {
+      if (tl == slice) {
+        ++owner;
+        tl = 0;
+        obase = mapa_shared(rbase, static_cast<uint32_t>(owner));
+      }
+      const uint32_t a = obase + static_cast<uint32_t>(((rank * slice + tl) * kPStride + row) * 4);
+      asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(a), "f"(o[j]) : "memory");
+      ++tl;
+    }
+  }
+  if (split > 1) {
+    cluster_sync();
+  } else {
+    __syncthreads();
+  }
+  {
+    const int items = slice * 16;  // 8 weight rows (16 output bytes) per item
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int tl = it / 16, r8 = (it % 16) * 8;
+      const int t = t0 + rank * slice + tl, n = n0 + r8;
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
+      for (int q = 0; q < split; ++q) {
+        const float4* src = reinterpret_cast<const float4*>(recv + (q * slice + tl) * kPStride + r8);
+        const float4 x0 = src[0], x1 = src[1];
+        acc[0] += x0.x;
+        acc[1] += x0.y;
+        acc[2] += x0.z;
+        acc[3] += x0.w;
+        acc[4] += x1.x;
+        acc[5] += x1.y;
+        acc[6] += x1.z;
+        acc[7] += x1.w;
+      }
+      if (ok && t < A.T && n < A.N) {
         uint4 w;
-        w.x = pack_bf16_rn(o[8 * q + 0], o[8 * q + 1]);
-        w.y = pack_bf16_rn(o[8 * q + 2], o[8 * q + 3]);
-        w.z = pack_bf16_rn(o[8 * q + 4], o[8 * q + 5]);
-        w.w = pack_bf16_rn(o[8 * q + 6], o[8 * q + 7]);
-        dst[q] = w;
+        w.x = pack_bf16_rn(acc[0], acc[1]);
+        w.y = pack_bf16_rn(acc[2], acc[3]);
+        w.z = pack_bf16_rn(acc[4], acc[5]);
+        w.w = pack_bf16_rn(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(A.out + static_cast<int64_t>(t) * A.out_st + static_cast<int64_t>(g) * A.out_sg +
+                                  n) = w;
       }
     }
   }
@@ -263,14 +391,29 @@ bool encode_u8_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, ui
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int N_TILE>
-int launch_gemm(const GemmArgs& A, int* err, const CUtensorMap& xm, const CUtensorMap& wm, cudaStream_t s) {
+template <int TT>
+int launch_gemm(const GemmArgs& A, int t_tiles, int* err, const CUtensorMap& xm, const CUtensorMap& wm,
+                cudaStream_t s) {
   static bool attr_set[kMaxDevices] = {};
-  if (set_func_attr_once(hca_fp8_gemm_kernel<N_TILE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         GemmSmem<N_TILE>::kBytes, attr_set) != HCA_OK)
+  if (set_func_attr_once(hca_fp8_gemm_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem<TT>::kBytes,
+                         attr_set) != HCA_OK)
     return HCA_E_CUDA;
-  dim3 grid((A.T + 127) / 128, A.N / N_TILE, A.G);
-  return launch_pdl(hca_fp8_gemm_kernel<N_TILE>, grid, dim3(kThreads), GemmSmem<N_TILE>::kBytes, s, A, err, xm, wm);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(A.split);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(A.split), static_cast<unsigned>(A.n_blocks),
+                     static_cast<unsigned>(A.G * t_tiles));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = GemmSmem<TT>::kBytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, hca_fp8_gemm_kernel<TT>, A, err, xm, wm));
 }
 
 }  // namespace
@@ -293,14 +436,25 @@ extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t o
   HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
                 x_stride_tok % 16 == 0 && x_stride_group % 16 == 0 && x_stride_tok >= k);
   HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(out) % 16 == 0 && out_stride_tok % 8 == 0 && out_stride_group % 8 == 0);
-  // 128-column N tiles while they fill the SMs, else 64
-  const int64_t m_tiles = (num_tokens + 127) / 128;
+  // token tile: all tokens up to 192 (a multiple of 64), else 192-token tiles
+  const int tt = num_tokens >= 192 ? 192 : ((num_tokens + 63) / 64) * 64;
+  const int64_t t_tiles = (num_tokens + tt - 1) / tt;
+  const int n_blocks = (n + 127) / 128;
+  HCA_CHECK_ARG(t_tiles * num_groups <= 65535);
   int sms = 148;
   {
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  const int n_tile = (n % 128 == 0 && m_tiles * (n / 128) * num_groups >= sms) ? 128 : 64;
+  // split K over a cluster while the CTAs fit one wave and each keeps at
+  // least two K blocks
+  const int64_t base = static_cast<int64_t>(n_blocks) * num_groups * t_tiles;
+  const int nkb = k / 128;
+  int split = 1;
+  while (split < kMaxSplit && base * split * 2 <= sms && nkb >= split * 4) split *= 2;
+  // at most kMaxKBlocks K blocks per CTA (its scale table)
+  while (split < kMaxSplit && nkb > split * kMaxKBlocks) split *= 2;
+  if (nkb > split * kMaxKBlocks) return HCA_E_UNSUPPORTED;
   GemmArgs A{};
   A.out = static_cast<__nv_bfloat16*>(out);
   A.out_st = out_stride_tok;
@@ -315,17 +469,23 @@ extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t o
   A.G = num_groups;
   A.N = n;
   A.K = k;
-  A.n_blocks = (n + 127) / 128;
+  A.n_blocks = n_blocks;
+  A.split = split;
   A.wait_ns = tc::kWaitLimitNs;
   CUtensorMap xm, wm;
   // x [G][T][K] bytes (token stride x_stride_tok, group stride
   // x_stride_group); w [G][N][K] contiguous
   const uint64_t gstride = num_groups > 1 ? static_cast<uint64_t>(x_stride_group)
                                           : static_cast<uint64_t>(x_stride_tok) * num_tokens;
-  if (!encode_u8_3d(&xm, x, k, num_tokens, num_groups, x_stride_tok, gstride, 128) ||
-      !encode_u8_3d(&wm, w, k, n, num_groups, k, static_cast<uint64_t>(n) * k, n_tile))
+  if (!encode_u8_3d(&xm, x, k, num_tokens, num_groups, x_stride_tok, gstride, static_cast<uint32_t>(tt)) ||
+      !encode_u8_3d(&wm, w, k, n, num_groups, k, static_cast<uint64_t>(n) * k, 128))
     return HCA_E_UNSUPPORTED;
   int* err = device_error_word();
   cudaStream_t s = as_stream(stream);
-  return n_tile == 128 ? launch_gemm<128>(A, err, xm, wm, s) : launch_gemm<64>(A, err, xm, wm, s);
+  const int tl = static_cast<int>(t_tiles);
+  switch (tt) {
+    case 64: return launch_gemm<64>(A, tl, err, xm, wm, s);
+    case 128: return launch_gemm<128>(A, tl, err, xm, wm, s);
+    default: return launch_gemm<192>(A, tl, err, xm, wm, s);
+  }
 }

@@ -83,5 +83,7 @@ def call(name: str, *args) -> int:
     status = getattr(lib(), name)(*args)
     if status != 0:
         msg = lib().hca_status_string(status).decode()
+        if status == -3:  # HCA_E_CUDA: the CUDA error behind it
+            msg += ": " + lib().hca_last_cuda_error().decode()
         raise HcaError(name, status, msg)
     return status

@@ -347,13 +347,19 @@ class Ernie5_5HCAAttention(nn.Module):
                 llama_4_scaling: torch.Tensor | None = None) -> torch.Tensor:
         T = hidden_states.shape[0]
         d, r = self.head_dim, self.rope_head_dim
+        aux = self._aux_streams(hidden_states)
+        # input GEMMs: fused_wqa_wkv here, the compressor's kv_score on aux
+        # stream 0 (V/models/deepseek_v4/attention.py:355-405)
+        kv_score = self._on_aux(aux, 0, lambda: self._kv_score(hidden_states))
         qr_kv = self.fused_wqa_wkv(hidden_states)
-        kv_score = hidden_states.float() @ self.compressor.fused_wkv_wgate.weight.float().t()
         qr, kv = qr_kv.split([self.q_lora_rank, d], dim=-1)
         qr, kv = ops.fused_q_kv_rmsnorm(qr, kv, self.q_norm.weight, self.kv_norm.weight, self.eps)
+        # the gate GEMM on aux stream 1 during attention (HCA has no
+        # indexer: E/nvidia/attention.py:487-510); the FP8 path's wo_b input
+        # quant applies the sigmoid itself
+        gate = self._on_aux(aux, 1, lambda: self.o_gate(qr) if self.fp8_output else torch.sigmoid(self.o_gate(qr)))
         q = self.wq_b(qr).view(T, self.n_local_heads, d)
-        # the FP8 path's wo_b input quant applies the sigmoid itself
-        gate = self.o_gate(qr) if self.fp8_output else torch.sigmoid(self.o_gate(qr))
+        kv_score = self._join(aux, 0, kv_score)
         attn_metadata = get_forward_context().attn_metadata
         dev = hidden_states.device
         if self.fp8_output and self.vha.tp_size == 1:
@@ -371,9 +377,46 @@ class Ernie5_5HCAAttention(nn.Module):
             # the attention part is one opaque op that writes `o` in place (an
             # eager break under graph compilation, as the reference's)
             torch.ops.hca_b200.hca_attention(q, kv, kv_score, positions, o, o_scale, self.layer_name)
+        gate = self._join(aux, 1, gate)
         if o.dtype == ops.FP8:
             return self._output_fp8(o.transpose(0, 1), o_scale.permute(2, 0, 1)[:T], gate)
         return self._output(o, positions, gate)
+
+    def _kv_score(self, x: torch.Tensor) -> torch.Tensor:
+        """fp32 ``x @ W^T`` of the bf16 compressor weight
+        (``torch.mm(..., out_dtype=torch.float32)`` as the reference; the fp32
+        matmul off the GPU)."""
+        w = self.compressor.fused_wkv_wgate.weight
+        if x.is_cuda:
+            return torch.mm(x, w.t(), out_dtype=torch.float32)
+        return x.float() @ w.float().t()
+
+    def _aux_streams(self, x: torch.Tensor):
+        """The first two aux streams when the caller passed them and the
+        step runs on a GPU, else None (serial)."""
+        if not x.is_cuda or not self.aux_stream_list or len(self.aux_stream_list) < 2:
+            return None
+        return self.aux_stream_list[:2]
+
+    def _on_aux(self, aux, i: int, fn):
+        """Run ``fn`` on aux stream ``i`` after the work queued so far on the
+        current stream; None streams run it inline."""
+        if aux is None:
+            return fn()
+        cur = torch.cuda.current_stream()
+        aux[i].wait_stream(cur)
+        with torch.cuda.stream(aux[i]):
+            out = fn()
+        return out
+
+    def _join(self, aux, i: int, t: torch.Tensor) -> torch.Tensor:
+        """Make the current stream wait for aux stream ``i``'s result ``t``."""
+        if aux is None:
+            return t
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(aux[i])
+        t.record_stream(cur)
+        return t
 
     def _attention(self, q, kv, kv_score, positions, o, o_scale, md: dict) -> None:
         d, r = self.head_dim, self.rope_head_dim
