@@ -324,6 +324,23 @@ def _cpu_sample(seconds_budget: float, worker: int = 0, n_workers: int = 1) -> t
     return done_tokens, t_total, reqs
 
 
+L2_NOTE = "inputs larger than L2: every layer has its own caches, cycled each step (run.l2 gives the bytes)"
+
+
+def decode_config(ws: int, layers: int, tokens: int, long_ctx: bool = False, head_dim: int = 128) -> dict:
+    """The workload keys of a decode line; both arms print the same dict."""
+    if long_ctx:
+        wl = (f"config 4 (16 req x 3 q at ~1M context: 8192 compressed + 128 window rows, H=64, D={head_dim}, "
+              f"fp8 KV) x {layers} HCA layers")
+    elif head_dim == 512:
+        wl = (f"config 2 requests at the model's head_dim (64 req x 3 q, ctx U[4K,128K], H=64, D=512, fp8 KV) "
+              f"x {layers} HCA layers")
+    else:
+        wl = f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers"
+    return {"workload": wl, "parallelism": f"dp{ws}", "layers": layers, "tokens_per_step_per_gpu": tokens,
+            "l2": L2_NOTE}
+
+
 def run_reference(args, ws, rank):
     if rank != 0:
         return
@@ -345,9 +362,8 @@ def run_reference(args, ws, rank):
             "warmup": args.warmup, "ms_per_step": Q_PER_SEQ * BATCH / v * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {LAYERS} HCA layers",
-                       "parallelism": f"dp{ws}", "layers": LAYERS, "tokens_per_step_per_gpu": BATCH * Q_PER_SEQ,
-                       "l2": "CPU run (the oracle port on the host cores)"},
+            "config": decode_config(ws, LAYERS, BATCH * Q_PER_SEQ),
+            "run": {"where": "the oracle port on the host cores"},
             "cpu_baseline": cb,
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -575,11 +591,12 @@ def module_forward_context(batch, layer, prefixes):
     return HCAStepMetadata(swa, c128, comp).as_forward_context(prefixes)
 
 
-def build_module_stack(batch, caches, layers: int, dev, seed: int = 0):
+def build_module_stack(batch, caches, layers: int, dev, seed: int = 0, tp_group=None):
     """``layers`` drop-in HCA modules of config 2's shape (hidden 4096, 64
     heads, q_lora 1024, 8 output groups of rank 1024) on the 128 x 128
     block-FP8 output path, random N(0, 0.02) weights (bf16 wo_a / wo_b
-    block-quantised on load), bound to the bench's caches."""
+    block-quantised on load), bound to the bench's caches.  With a TP group
+    every rank draws the same full weights and loads its head shard."""
     from vllm_ernie_b200 import attention as A
 
     d = batch.dims
@@ -593,21 +610,25 @@ def build_module_stack(batch, caches, layers: int, dev, seed: int = 0):
     g = torch.Generator(device=dev).manual_seed(seed)
     aux = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]  # the model's aux streams, shared by the layers
     mods = []
+    # full (unsharded) parameter shapes: those of a TP=1 layer
+    full = {n: (p.shape, p.dtype) for n, p in
+            A.Ernie5_5HCAAttention(vcfg, prefix="model.layers.shape_probe.self_attn").named_parameters()}
     for l in range(layers):
-        m = A.Ernie5_5HCAAttention(vcfg, prefix=f"model.layers.{l}.self_attn", aux_stream_list=aux).to(dev)
+        m = A.Ernie5_5HCAAttention(vcfg, prefix=f"model.layers.{l}.self_attn", aux_stream_list=aux,
+                                   tp_group=tp_group).to(dev)
         assert m.fp8_output
         ws = []
         for name, p in m.named_parameters():
             if name.endswith("weight_scale_inv"):
                 continue
-            shape = p.shape if name not in ("vha.U", "vha.V") else (d.heads, p.shape[1])
+            shape = full[name][0]
             if name.endswith("norm.weight"):
                 w = 1.0 + 0.02 * torch.randn(shape, generator=g, device=dev)
             elif name == "attn_sink":
                 w = torch.randn(shape, generator=g, device=dev)
             else:
                 w = 0.02 * torch.randn(shape, generator=g, device=dev)
-            ws.append((name, w.to(torch.float32 if p.dtype == torch.float32 else torch.bfloat16)))
+            ws.append((name, w.to(torch.float32 if full[name][1] == torch.float32 else torch.bfloat16)))
         m.load_weights(ws)
         m.process_weights_after_loading()
         m.bind_kv_cache(caches[l].swa, caches[l].comp, caches[l].state)
@@ -615,7 +636,7 @@ def build_module_stack(batch, caches, layers: int, dev, seed: int = 0):
     return mods
 
 
-def run_module(args, ws, batch, caches, layers, dev, attn_ms):
+def run_module(args, ws, batch, caches, layers, dev, attn_ms, tp_group=None):
     """Time the drop-in module: ``layers`` x ``Ernie5_5HCAAttention.forward``
     (input GEMMs, QK-norm, the attention op, the FP8 output GEMMs; a residual
     add feeds each layer's output to the next) captured in one CUDA graph,
@@ -625,7 +646,7 @@ def run_module(args, ws, batch, caches, layers, dev, attn_ms):
     copies inside the timed region."""
     from vllm_ernie_b200.forward_context import set_forward_context
 
-    mods = build_module_stack(batch, caches, layers, dev)
+    mods = build_module_stack(batch, caches, layers, dev, tp_group=tp_group)
     prefixes = [m.prefix for m in mods]
     T = batch.num_tokens
     ctx = module_forward_context(batch, mods[0], prefixes)
@@ -684,20 +705,74 @@ def run_module(args, ws, batch, caches, layers, dev, attn_ms):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(t0.elapsed_time(t1) / e2e_steps, ws)
     del graph
+    torch.cuda.synchronize()
     # per layer: q/kv RMSNorm, decode prep, attention, merge + VHA + inverse
-    # RoPE + FP8 quant, wo_a FP8 GEMM, gate quant, wo_b FP8 GEMM
+    # RoPE + FP8 quant (TP: inverse RoPE + FP8 quant after the VHA
+    # all-reduce), wo_a FP8 GEMM, gate quant, wo_b FP8 GEMM
     ours = 7 * layers
+    tok = T if tp_group is not None else ws * T  # TP: every rank serves the same tokens
     return {
         "call": f"{layers} x Ernie5_5HCAAttention.forward(positions, hidden_states), block-FP8 wo_a/wo_b, one CUDA graph",
-        "value": ws * T / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "per_layer_us": ms * 1e3 / layers,
-        "attention_share": attn_ms / ms,
+        "value": tok / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "per_layer_us": ms * 1e3 / layers,
+        "attention_share": attn_ms / ms if attn_ms else None,
         "gpu_launches_ours_per_step": ours,
     }, {
-        "value": ws * T / (e2e_ms * 1e-3), "unit": UNIT,
+        "value": tok / (e2e_ms * 1e-3), "unit": UNIT,
         "h2d_bytes_per_step": h_in.numel() * h_in.element_size() + h_pos.numel() * h_pos.element_size(),
         "d2h_bytes_per_step": h_out.numel() * h_out.element_size(),
         "call": "the module stack above, hidden_states/positions from pinned host memory, output back",
     }
+
+
+TP_METRIC = "HCA module decode tokens/s, head-sharded TP (config 2 requests on every rank)"
+
+
+def run_tp(args, ws, rank, local):
+    """Head-sharded TP (the config-5 variant): every rank serves the same 64
+    requests x 3 tokens with 64 / N of the heads and output groups; the VHA
+    low-rank term (fp32) and the wo_b output (bf16) are all-reduced over NCCL
+    in every layer.  Strong scaling.  The all-reduces are also timed alone
+    (the same sizes and count) for the collective's share of the step."""
+    from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch
+
+    dev = torch.device("cuda", local)
+    dims = HCADims(heads=64, head_dim=128, rope_dim=64, n_groups=8)
+    batch = make_decode_batch(contexts(0).tolist(), Q_PER_SEQ, dims, dev, seed=0, max_model_len=CTX_HI)
+    T = batch.num_tokens
+    layers = args.layers
+    caches = [alloc_layer_caches(batch, seed=l) for l in range(layers)]
+    group = torch.distributed.group.WORLD if ws > 1 else None
+    with ClockSampler(local) as clk:
+        module, e2e = run_module(args, ws, batch, caches, layers, dev, None, tp_group=group)
+    coll = None
+    if ws > 1:
+        z = torch.zeros((T, 16, dims.head_dim), dtype=torch.float32, device=dev)
+        y = torch.zeros((T, 4096), dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            torch.distributed.all_reduce(z)
+            torch.distributed.all_reduce(y)
+        torch.cuda.synchronize()
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(layers):
+            torch.distributed.all_reduce(z)
+            torch.distributed.all_reduce(y)
+        e1.record()
+        torch.cuda.synchronize()
+        ar_ms = max_over_ranks(e0.elapsed_time(e1), ws)
+        coll = {"what": f"{layers} x (all-reduce fp32 [{T}, 16, {dims.head_dim}] + all-reduce bf16 [{T}, 4096]), NCCL",
+                "ms_per_step_alone": ar_ms, "share_of_step": ar_ms / module["ms_per_step"]}
+    if rank == 0:
+        line = {"metric": TP_METRIC, "value": module["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": module["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": (f"config 2 requests (64 req x 3 q, ctx U[4K,128K], H=64 sharded over "
+                                        f"{ws}, D=128, fp8 KV) x {layers} HCA modules"),
+                           "parallelism": f"tp{ws}", "layers": layers, "tokens_per_step_per_gpu": T, "l2": L2_NOTE},
+                "module": module, "e2e": e2e, "collective": coll,
+                "gpu_launches": module["gpu_launches_ours_per_step"] * args.steps, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
 
 
 def main():
@@ -706,6 +781,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--parallel", default="dp", choices=["dp", "tp"],
+                    help="dp: requests shard over the GPUs (the headline); tp: the module stack with the heads "
+                         "sharded over the GPUs and NCCL all-reduces (a supplementary line)")
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "decode1m"],
@@ -729,6 +807,11 @@ def main():
         return
     if args.workload == "prefill":
         run_prefill(args, ws, rank, local)
+        return
+    if args.parallel == "tp":
+        run_tp(args, ws, rank, local)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
         return
 
     from vllm_ernie_b200 import ops
@@ -867,17 +950,10 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": (f"config 4 (16 req x 3 q at ~1M context: 8192 compressed + 128 window rows, "
-                                    f"H=64, D={dims.head_dim}, fp8 KV) x {layers} HCA layers" if long_ctx else
-                                    f"config 2 (64 req x 3 q, ctx U[4K,128K], H=64, D=128, fp8 KV) x {layers} HCA layers"
-                                    if not wide else
-                                    f"config 2 requests at the model's head_dim (64 req x 3 q, ctx U[4K,128K], "
-                                    f"H=64, D=512, fp8 KV) x {layers} HCA layers"),
-                       "parallelism": f"dp{ws}", "layers": layers, "tokens_per_step_per_gpu": T,
-                       "split_k": (f"balanced work list, {md.max_items} CTAs" if md.schedule is not None
-                                   else f"{md.num_splits} uniform splits per request"),
-                       "l2": l2_note,
-                       "per_layer_us": ms * 1e3 / layers},
+            "config": decode_config(ws, layers, T, long_ctx, dims.head_dim),
+            "run": {"split_k": (f"balanced work list, {md.max_items} CTAs" if md.schedule is not None
+                                else f"{md.num_splits} uniform splits per request"),
+                    "l2": l2_note, "per_layer_us": ms * 1e3 / layers},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": src,
                          "kernel": ("hca_wide_attention_kernel<decode> (CTA pairs)" if wide

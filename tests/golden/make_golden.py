@@ -231,6 +231,76 @@ def gen_compressor(g: torch.Generator) -> None:
          kv_cache=kv_cache.view(16, -1), cos_sin=cos_sin, norm_weight=w)
 
 
+def gen_compressor_blocks(g: torch.Generator, d: int = D) -> None:
+    """More compressed blocks at the model's head_dim (the reference's HCA
+    compressor kernel is the head_dim-512 one; other head sizes take its
+    indexer kernel and cache format): three requests whose spans cover 8
+    block boundaries -- a whole 512-token prefix, a span starting mid-block
+    on earlier-step states (its first block pools 108 states written before
+    the step), and a span from an odd offset -- through state pages of 8
+    tokens in shuffled order, so blocks straddle pages everywhere.  Stores the
+    compressed rows with their UE8M0 scale bytes."""
+    from vllm.models.deepseek_v4.common.ops.fused_compress_quant_cache import (
+        compress_norm_rope_store_triton,
+    )
+    from vllm.models.deepseek_v4.common.ops.save_partial_states import save_partial_states
+
+    ratio, sbs = 128, 8
+    nope = d - R
+    spans = [(0, 512), (1900, 2100), (4995, 5250)]
+    positions = torch.cat([torch.arange(a, b) for a, b in spans]).to(torch.int64)
+    t2r = torch.cat([torch.full((b - a,), i, dtype=torch.int32) for i, (a, b) in enumerate(spans)])
+    T = positions.shape[0]
+    width = 5250 // sbs + 1
+    state_bt = torch.zeros(len(spans), width, dtype=torch.int32)
+    need = [(a // ratio * ratio // sbs, (b + sbs - 1) // sbs) for a, b in spans]  # pages of the blocks touched
+    n_pages = sum(hi - lo for lo, hi in need)
+    perm = torch.randperm(n_pages, generator=g).to(torch.int32)
+    k = 0
+    for r, (lo, hi) in enumerate(need):
+        state_bt[r, lo:hi] = perm[k:k + hi - lo]
+        k += hi - lo
+    # earlier-step states only where a block starts before the step (bf16-
+    # representable values keep the fixture small); zeros elsewhere
+    state = torch.zeros(n_pages, sbs, 2 * d)
+    for r, (a, _) in enumerate(spans):
+        for p0 in range(a // ratio * ratio, a):
+            pg = int(state_bt[r, p0 // sbs])
+            state[pg, p0 % sbs] = torch.randn(2 * d, generator=g).bfloat16().float()
+    state_before = state.clone()
+    slot = (state_bt[t2r.long(), positions // sbs].long() * sbs + positions % sbs)
+    kv = torch.randn(T, d, generator=g).bfloat16().float()
+    score = (torch.randn(T, d, generator=g) * 2).bfloat16().float()
+    ape = (torch.randn(ratio, d, generator=g) * 0.5).bfloat16().float()
+    save_partial_states(kv, score, ape, positions, state, slot, sbs, d, ratio)
+    # compressed cache: 2 entries per page
+    n_cpages = 32
+    comp_bt = torch.stack([torch.randperm(n_cpages, generator=g)[:24] for _ in spans]).to(torch.int32)
+    cpos = positions // ratio
+    comp_slot = torch.where((positions + 1) % ratio == 0,
+                            comp_bt[t2r.long(), cpos // 2].long() * 2 + cpos % 2,
+                            torch.full_like(positions, -1))
+    entry = nope + 2 * R + nope // 64 + 1
+    kv_cache = torch.zeros(n_cpages, 2, entry, dtype=torch.uint8)
+    cos_sin = rope_cache(6144)
+    w = 1.0 + 0.1 * torch.randn(d, generator=g)
+
+    class Meta:
+        slot_mapping = comp_slot
+
+    compress_norm_rope_store_triton(
+        state_cache=state, num_actual=T, token_to_req_indices=t2r, positions=positions,
+        slot_mapping=slot, block_table=state_bt, block_size=sbs, state_width=d,
+        cos_sin_cache=cos_sin, kv_cache=kv_cache, k_cache_metadata=Meta, pdl_kwargs={},
+        head_dim=d, rope_head_dim=R, compress_ratio=ratio, overlap=False, use_fp4_cache=False,
+        rms_norm_weight=w, rms_norm_eps=1e-6, quant_block=64, token_stride=nope + 2 * R,
+        scale_dim=nope // 64 + 1)
+    assert int((comp_slot >= 0).sum()) == 8
+    save(f"compressor_blocks_d{d}", positions=positions, token_to_req=t2r, state_block_table=state_bt,
+         state_before=state_before, kv=kv, score=score, ape=ape, state_slot=slot, comp_block_table=comp_bt,
+         comp_slot=comp_slot, kv_cache=kv_cache.view(n_cpages, -1), cos_sin=cos_sin, norm_weight=w)
+
+
 def gen_metadata(g: torch.Generator) -> None:
     from vllm.models.deepseek_v4.common.ops.cache_utils import combine_topk_swa_indices
     from vllm.v1.attention.backends.mla.compressor_utils import get_compressed_slot_mapping
@@ -528,6 +598,8 @@ def main() -> None:
         gen_insert_and_gather(g)
     if "compressor" in which:
         gen_compressor(g)
+    if "compressor_blocks" in which:
+        gen_compressor_blocks(torch.Generator().manual_seed(11))
     if "metadata" in which:
         gen_metadata(g)
     if "output" in which:

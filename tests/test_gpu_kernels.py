@@ -204,6 +204,51 @@ def test_compressor_matches_reference_d512(ops):
     ref = C.read_rows(g["kv_cache"], slots, 2, 512, 64)
     assert np.linalg.norm(ours - ref) / np.linalg.norm(ref) < 2e-3
     np.testing.assert_allclose(ours, ref, rtol=2 ** -3, atol=1e-6)
+    _, _, sc = _compressed_bytes(cache.cpu().numpy(), slots)
+    _, _, rsc = _compressed_bytes(g["kv_cache"], slots)
+    assert np.array_equal(sc, rsc)  # UE8M0 scale bytes
+
+
+def _compressed_bytes(cache, slots, d=512, r=64):
+    """(e4m3 NoPE codes, bf16 RoPE bytes, UE8M0 scale bytes) of each row at ``slots``."""
+    nope = d - r
+    row, srow = nope + 2 * r, nope // 64 + 1
+    codes, rope, scales = [], [], []
+    for sl in slots:
+        page, off = divmod(int(sl), 2)
+        codes.append(cache[page, off * row:off * row + nope])
+        rope.append(cache[page, off * row + nope:(off + 1) * row])
+        scales.append(cache[page, 2 * row + off * srow:2 * row + (off + 1) * srow])
+    return np.array(codes), np.array(rope), np.array(scales)
+
+
+def test_compressor_many_blocks_matches_reference(ops):
+    """Eight blocks of the reference's head_dim-512 compressor (whole
+    prefix, earlier-step states, odd offsets, shuffled state pages): the
+    UE8M0 scale bytes equal, >= 99% of the e4m3 codes equal and the rest one
+    step apart, RoPE within one bf16 ulp."""
+    g = load("compressor_blocks_d512")
+    state = T(g["state_before"])
+    ops.save_partial_states(T(g["kv"]), T(g["score"]), T(g["ape"]), T(g["positions"]), state,
+                            T(g["state_slot"]), 8, 512, 128)
+    cache = torch.zeros(g["kv_cache"].shape, dtype=torch.uint8, device=DEV)
+    n = g["positions"].shape[0]
+    ops.compress_norm_rope_store(state, n, T(g["token_to_req"]), T(g["positions"]), T(g["state_slot"]),
+                                 T(g["state_block_table"]), 8, 512, T(g["cos_sin"]), cache,
+                                 T(g["comp_slot"]), 2, 512, 64, 128, T(g["norm_weight"]), 1e-6)
+    torch.cuda.synchronize()
+    slots = g["comp_slot"][g["comp_slot"] >= 0]
+    assert len(slots) == 8
+    got = cache.cpu().numpy()
+    oc, _, osc = _compressed_bytes(got, slots)
+    rc, _, rsc = _compressed_bytes(g["kv_cache"], slots)
+    assert np.array_equal(osc, rsc)
+    assert (oc == rc).mean() >= 0.99
+    ours = C.read_rows(got, slots, 2, 512, 64)
+    ref = C.read_rows(g["kv_cache"], slots, 2, 512, 64)
+    np.testing.assert_allclose(ours, ref, rtol=2 ** -3, atol=1e-6)
+    assert np.linalg.norm(ours - ref) / np.linalg.norm(ref) < 2e-3
+    assert ops.device_error() == 0
 
 
 def test_compressor_matches_oracle_d128(ops):

@@ -7,8 +7,10 @@ the block-FP8 variant's group width and ``wo_b`` input tile its 128 x 128
 blocks and 512-wide scale packs on every rank).  bf16 and block-FP8
 ``wo_a``/``wo_b``.  The layer output of every rank after the all-reduce must
 match the whole-layer CPU oracle within the tolerance of the single-GPU
-module test (relative L2 3e-2, max |err| <= 3e-2 x max |ref|), for a prefill
-step and an ECHO/MTP decode step, and all ranks must hold the same output.
+module test (relative L2 3e-2, max |err| <= 3e-2 x max |ref|; 6e-2 on the
+block-FP8 path, whose two e4m3 quant points turn small upstream differences
+into whole e4m3 steps), for a prefill step and an ECHO/MTP decode step, and
+all ranks must hold the same output.
 Skipped when the box has fewer GPUs than ranks.
 """
 
@@ -123,8 +125,9 @@ def test_module_tp_nccl_matches_layer_oracle(world, fp8):
         assert np.isfinite(y).all()
         err = np.abs(y - ref)
         rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
-        assert rel <= 3e-2, (rank, step, rel, err.max())
-        assert err.max() <= 3e-2 * np.abs(ref).max(), (rank, step, rel, err.max())
+        tol = 6e-2 if fp8 else 3e-2
+        assert rel <= tol, (rank, step, rel, err.max())
+        assert err.max() <= tol * np.abs(ref).max(), (rank, step, rel, err.max())
     # every rank holds the same all-reduced output
     for step in range(len(STEPS)):
         for rank in range(1, world):

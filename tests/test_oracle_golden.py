@@ -69,6 +69,44 @@ def test_compressor_matches_reference():
         assert np.array_equal(cache[page, sb:sb + 8], g["kv_cache"][page, sb:sb + 8])
 
 
+def _compressed_bytes(cache, slots, d=D, r=R):
+    """(e4m3 NoPE codes, bf16 RoPE bytes, UE8M0 scale bytes) of each row at ``slots``."""
+    nope = d - r
+    row, srow = nope + 2 * r, nope // 64 + 1
+    codes, rope, scales = [], [], []
+    for s in slots:
+        page, off = divmod(int(s), 2)
+        base = off * row
+        codes.append(cache[page, base:base + nope])
+        rope.append(cache[page, base + nope:base + row])
+        sb = 2 * row + off * srow
+        scales.append(cache[page, sb:sb + srow])
+    return np.array(codes), np.array(rope), np.array(scales)
+
+
+def test_compressor_many_blocks_matches_reference():
+    """Eight blocks (whole prefix, earlier-step states, odd offsets, shuffled
+    state pages): UE8M0 scale bytes equal; e4m3 codes within one step with
+    >= 99% equal; RoPE within one bf16 ulp."""
+    g = load("compressor_blocks_d512")
+    state = g["state_before"].copy()
+    C.save_partial_states(state, g["kv"], g["score"], g["ape"], g["positions"], g["state_slot"], 8, 128)
+    cache = np.zeros_like(g["kv_cache"])
+    C.compress_norm_rope_store(state, g["token_to_req"], g["positions"], g["state_slot"],
+                               g["state_block_table"], 8, g["norm_weight"], 1e-6, g["cos_sin"],
+                               cache, g["comp_slot"], 2, D, R, 128)
+    slots = g["comp_slot"][g["comp_slot"] >= 0]
+    assert len(slots) == 8
+    oc, orope, osc = _compressed_bytes(cache, slots)
+    rc, rrope, rsc = _compressed_bytes(g["kv_cache"], slots)
+    assert np.array_equal(osc, rsc)
+    assert (oc == rc).mean() >= 0.99
+    ours = C.read_rows(cache, slots, 2, D, R)
+    ref = C.read_rows(g["kv_cache"], slots, 2, D, R)
+    np.testing.assert_allclose(ours, ref, rtol=2 ** -3, atol=1e-6)
+    assert np.linalg.norm(ours - ref) / np.linalg.norm(ref) < 2e-3
+
+
 def test_metadata_builders_bit_exact():
     g = load("metadata")
     qsl, seq_lens = g["query_start_loc"], g["seq_lens"]
