@@ -270,3 +270,13 @@ def test_fp8_weights_load_from_block_fp8_or_quantise_on_load():
     for x, y in ((a.wo_a, b.wo_a), (a.wo_b, b.wo_b)):
         assert torch.equal(x.weight.view(torch.uint8), y.weight.view(torch.uint8))
         assert torch.equal(x.weight_scale_inv, y.weight_scale_inv)
+
+
+def test_max_model_len_beyond_rope_table_is_refused():
+    """The RoPE kernels index the cos/sin table by position, so a context
+    the table does not cover is refused at construction."""
+    cfg = _fp8_cfg(max_position_embeddings=4096)
+    with pytest.raises(ValueError, match="max_position_embeddings"):
+        A.Ernie5_5HCAAttention(A.make_vllm_config(cfg, max_model_len=8192), prefix="model.layers.0.self_attn")
+    layer = A.Ernie5_5HCAAttention(A.make_vllm_config(cfg, max_model_len=4096), prefix="model.layers.0.self_attn")
+    assert layer.cos_sin_cache.shape[0] == 4096

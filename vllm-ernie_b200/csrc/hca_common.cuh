@@ -111,10 +111,10 @@ constexpr int kMaxDevices = 64;
 template <typename K>
 inline int set_func_attr_once(K kernel, cudaFuncAttribute attr, int value, bool (&done)[kMaxDevices]) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return HCA_E_CUDA;
+  if (cuda_status(cudaGetDevice(&dev)) != HCA_OK) return HCA_E_CUDA;
   const bool tracked = dev >= 0 && dev < kMaxDevices;
   if (tracked && done[dev]) return HCA_OK;
-  if (cudaFuncSetAttribute(kernel, attr, value) != cudaSuccess) return HCA_E_CUDA;
+  if (cuda_status(cudaFuncSetAttribute(kernel, attr, value)) != HCA_OK) return HCA_E_CUDA;
   if (tracked) done[dev] = true;
   return HCA_OK;
 }

@@ -441,11 +441,7 @@ extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t o
   const int64_t t_tiles = (num_tokens + tt - 1) / tt;
   const int n_blocks = (n + 127) / 128;
   HCA_CHECK_ARG(t_tiles * num_groups <= 65535);
-  int sms = 148;
-  {
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
+  const int sms = device_sm_count();
   // split K over a cluster while the CTAs fit one wave and each keeps at
   // least two K blocks
   const int64_t base = static_cast<int64_t>(n_blocks) * num_groups * t_tiles;

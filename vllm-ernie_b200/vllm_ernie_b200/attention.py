@@ -321,6 +321,11 @@ class Ernie5_5HCAAttention(nn.Module):
                                       f"{prefix}.compressor")
         theta = cfg.compress_rope_theta
         inv = 1.0 / (theta ** (torch.arange(0, self.rope_head_dim, 2, dtype=torch.float) / self.rope_head_dim))
+        # the RoPE kernels index this table by position: every position the
+        # model can reach must have a row (vLLM refuses such configs too)
+        if self.max_model_len > cfg.max_position_embeddings:
+            raise ValueError(f"max_model_len {self.max_model_len} exceeds max_position_embeddings "
+                             f"{cfg.max_position_embeddings}")
         t = torch.arange(min(cfg.max_position_embeddings, self.max_model_len + 1), dtype=torch.float)
         f = torch.outer(t, inv)
         self.register_buffer("cos_sin_cache", torch.cat([f.cos(), f.sin()], -1), persistent=False)
