@@ -280,3 +280,53 @@ def test_max_model_len_beyond_rope_table_is_refused():
         A.Ernie5_5HCAAttention(A.make_vllm_config(cfg, max_model_len=8192), prefix="model.layers.0.self_attn")
     layer = A.Ernie5_5HCAAttention(A.make_vllm_config(cfg, max_model_len=4096), prefix="model.layers.0.self_attn")
     assert layer.cos_sin_cache.shape[0] == 4096
+
+
+def _fp8_shard_worker(rank, world_size, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    try:
+        from vllm_ernie_b200.ops import quantize_weight_block_fp8
+
+        cfg = _fp8_cfg(num_attention_heads=32, hybrid_mla_num_attention_heads=32, o_groups=8, o_lora_rank=512)
+        vc = A.make_vllm_config(cfg, max_model_len=1152, quant_config=A.block_fp8_quant_config())
+        g = torch.Generator().manual_seed(4)
+        wa = torch.randn(8 * 512, 512, generator=g) * 0.02   # [G * o_lora, H * D / G]
+        wb = torch.randn(2048, 8 * 512, generator=g) * 0.02  # [hidden, G * o_lora]
+        qa, sa = quantize_weight_block_fp8(wa)
+        qb, sb = quantize_weight_block_fp8(wb)
+        for form, items in (("fp8", [("wo_a.weight", qa), ("wo_a.weight_scale_inv", sa), ("wo_b.weight", qb),
+                                     ("wo_b.weight_scale_inv", sb)]),
+                            ("bf16", [("wo_a.weight", wa), ("wo_b.weight", wb)])):
+            layer = A.Ernie5_5HCAAttention(vc, prefix="model.layers.0.self_attn", tp_group=dist.group.WORLD)
+            assert layer.fp8_output and layer.n_local_groups == 8 // world_size
+            layer.load_weights(items)
+            out[(rank, form)] = (layer.wo_a.weight.view(torch.uint8).clone(), layer.wo_a.weight_scale_inv.clone(),
+                                 layer.wo_b.weight.view(torch.uint8).clone(), layer.wo_b.weight_scale_inv.clone())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fp8_weights_shard_by_rank_gloo():
+    """Head-sharded TP of the block-FP8 output weights: wo_a by rows (output
+    groups), wo_b by columns, the 128 x 128 scale blocks with them; loading
+    the checkpoint's e4m3 + scales and quantising a bf16 weight on load give
+    each rank the same bytes, the matching slice of the unsharded layer's."""
+    from vllm_ernie_b200.ops import quantize_weight_block_fp8
+
+    world_size = 2
+    with mp.get_context("spawn").Manager() as manager:
+        out = manager.dict()
+        mp.spawn(_fp8_shard_worker, args=(world_size, _free_port(), out), nprocs=world_size)
+        got = dict(out.items())
+    g = torch.Generator().manual_seed(4)
+    qa, sa = quantize_weight_block_fp8(torch.randn(8 * 512, 512, generator=g) * 0.02)
+    qb, sb = quantize_weight_block_fp8(torch.randn(2048, 8 * 512, generator=g) * 0.02)
+    ra, rb = qa.shape[0] // world_size, qb.shape[1] // world_size
+    for r in range(world_size):
+        want = (qa[r * ra:(r + 1) * ra].view(torch.uint8), sa[r * ra // 128:(r + 1) * ra // 128],
+                qb[:, r * rb:(r + 1) * rb].view(torch.uint8), sb[:, r * rb // 128:(r + 1) * rb // 128])
+        for form in ("fp8", "bf16"):
+            for a, b in zip(got[(r, form)], want):
+                assert torch.equal(a, b), (r, form)
