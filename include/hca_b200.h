@@ -419,13 +419,20 @@ int hca_sigmoid_mul_quant_fp8(uint8_t* out, int32_t* scale, const void* x, int64
  * scales w_scale [G, ceil(N / 128), K / 128]; out bf16 with element strides
  * (out_stride_tok, out_stride_group), 16-byte aligned rows.  N a multiple of
  * 64, K of 128; otherwise HCA_E_UNSUPPORTED.  fp32 accumulation: each
- * 128-wide K block's partial product is scaled once and summed in fp32. */
+ * 128-wide K block's partial product is scaled once and summed in fp32.
+ * Small token counts split K over a thread-block cluster of 2-8 CTAs whose
+ * fp32 partial tiles go through `workspace` (16-byte aligned, at least
+ * hca_fp8_grouped_gemm_workspace_bytes(...) bytes; NULL when that is 0;
+ * HCA_E_WORKSPACE if smaller).  Calls sharing a workspace must be ordered on
+ * one stream. */
+int64_t hca_fp8_grouped_gemm_workspace_bytes(int32_t num_tokens, int32_t num_groups, int32_t n,
+                                             int32_t k);
 int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t out_stride_group,
                          const uint8_t* x, int64_t x_stride_tok, int64_t x_stride_group,
                          const int32_t* x_scale, int64_t xs_stride_tok, int64_t xs_stride_group,
                          int64_t xs_stride_pack, int32_t xs_per_int, const uint8_t* w,
                          const float* w_scale, int32_t num_tokens, int32_t num_groups, int32_t n,
-                         int32_t k, void* stream);
+                         int32_t k, void* workspace, int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

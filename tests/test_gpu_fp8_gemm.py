@@ -136,3 +136,31 @@ def test_fp8_gemm_empty_and_unsupported_shapes():
         ops.fp8_grouped_gemm(x, xs, w, sw)
     torch.cuda.synchronize()
     assert ops.device_error() == 0
+
+
+def test_fp8_gemm_split_k_workspace_checked_before_launch():
+    """A split-K call needs its workspace: missing or too small, the library
+    refuses it before launching (HCA_E_INVALID / HCA_E_WORKSPACE)."""
+    from vllm_ernie_b200 import ops
+    from vllm_ernie_b200._lib import HcaError, call, lib
+
+    t, n, k = 48, 4096, 8192
+    need = lib().hca_fp8_grouped_gemm_workspace_bytes(t, 1, n, k)
+    assert need > 0  # 32 weight tiles: split K over a cluster
+    x = torch.zeros((t, k), dtype=FP8, device=DEV)
+    xs = torch.zeros((t, k // 512), dtype=torch.int32, device=DEV)
+    w = torch.zeros((n, k), dtype=FP8, device=DEV)
+    sw = torch.ones((n // 128, k // 128), device=DEV)
+    out = torch.empty((t, n), dtype=torch.bfloat16, device=DEV)
+    small = torch.empty(need // 4 - 4, dtype=torch.float32, device=DEV)
+    s = torch.cuda.current_stream().cuda_stream
+    args = (out.data_ptr(), n, 0, x.data_ptr(), k, 0, xs.data_ptr(), 1, 0, t, 4, w.data_ptr(), sw.data_ptr(),
+            t, 1, n, k)
+    with pytest.raises(HcaError) as e:
+        call("hca_fp8_grouped_gemm", *args, small.data_ptr(), small.numel() * 4, s)
+    assert e.value.status == -4
+    with pytest.raises(HcaError) as e:
+        call("hca_fp8_grouped_gemm", *args, None, 0, s)
+    assert e.value.status == -1
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0

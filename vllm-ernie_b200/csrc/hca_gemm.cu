@@ -21,9 +21,9 @@
 //              the token columns each; per K block, acc * sw[kb] * sx[t, kb]
 //              added to fp32 registers (the promotion step of DeepGEMM's
 //              block-scaled GEMM), the buffer handed back to the MMA warp
-// The CTA's partial [TT x 128] fp32 tile goes to its shared memory; after a
-// cluster barrier CTA r sums rank-r's token slice over the cluster's partial
-// tiles (distributed shared memory), rounds to bf16 and stores coalesced rows.
+// The CTA's partial [TT x 128] fp32 tile goes to the caller's workspace (L2);
+// after one cluster barrier CTA r sums rank r's token slice over the
+// cluster's partial tiles, rounds to bf16 and stores coalesced rows.
 // Every mbarrier wait is bounded; a timeout sets the device error word, and
 // the producer and MMA threads wait (bounded) for their copies and MMAs in
 // flight before the CTA frees its TMEM; the cluster barriers are taken by
@@ -76,6 +76,7 @@ struct GemmArgs {
   int T, G, N, K;
   int n_blocks;            // ceil(N / 128)
   int split;               // CTAs per cluster along K
+  float* ws_part;          // split > 1: [tiles][split][TT][128] fp32 partial tiles
   uint64_t wait_ns;
 };
 
@@ -292,31 +293,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0 && err) atomicOr(err, 1 << 7);
   }
   // Split-K: CTA r owns tokens [r S, (r + 1) S) of the tile (S = TT /
-  // split).  Once every ring of the cluster is idle (copies landed, MMAs
-  // done), each CTA stores its partial sums of CTA r's tokens into CTA r's
-  // ring, rows [q S, (q + 1) S) for source rank q (posted stores into the
-  // owner's shared memory, no round trips); after a second cluster barrier
-  // each CTA sums its split rows and stores bf16.
+  // split).  Every CTA writes its partial tile [TT tokens][128 rows] fp32 to
+  // its slot of the workspace (coalesced, L2-resident), one cluster barrier
+  // (release / acquire at cluster scope) makes the cluster's slots visible,
+  // and each CTA sums the split rows of its tokens from L2 and stores bf16.
+  // Without a split the partial tile goes through the CTA's own (idle) ring.
   __syncthreads();
-  if (split > 1) cluster_sync();
-  float* recv = reinterpret_cast<float*>(smem);  // [split][S][kPStride]
   const int slice = TT / split;
+  constexpr int kCols = TT / 2;
+  float* part;
+  int64_t pstride;  // floats per token row
+  if (split > 1) {
+    part = A.ws_part + (static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * split * TT * 128;
+    pstride = 128;
+  } else {
+    part = reinterpret_cast<float*>(smem);
+    pstride = kPStride;
+  }
   if (warp >= 2) {
-    constexpr int kCols = TT / 2;
     const int row = (warp & 3) * 32 + lane, c0 = ((warp - 2) >> 2) * kCols;
-    const uint32_t rbase = smem_u32(recv);
-    int owner = c0 / slice, tl = c0 - owner * slice;
-    uint32_t obase = split > 1 ? mapa_shared(rbase, static_cast<uint32_t>(owner)) : rbase;
+    float* dst = part + static_cast<int64_t>(rank * TT + c0) * pstride + row;
+    if (split > 1) {
 #pragma unroll
-    for (int j = 0; j < kCols; ++j) {
-      if (tl == slice) {
-        ++owner;
-        tl = 0;
-        obase = mapa_shared(rbase, static_cast<uint32_t>(owner));
-      }
-      const uint32_t a = obase + static_cast<uint32_t>(((rank * slice + tl) * kPStride + row) * 4);
-      asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(a), "f"(o[j]) : "memory");
-      ++tl;
+      for (int j = 0; j < kCols; ++j) __stcg(dst + j * pstride, o[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kCols; ++j) dst[j * pstride] = o[j];
     }
   }
   if (split > 1) {
@@ -327,22 +329,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   {
     const int items = slice * 16;  // 8 weight rows (16 output bytes) per item
     for (int it = threadIdx.x; it < items; it += kThreads) {
-      const int tl = it / 16, r8 = (it % 16) * 8;
-      const int t = t0 + rank * slice + tl, n = n0 + r8;
+      const int tl = rank * slice + it / 16, r8 = (it % 16) * 8;
+      const int t = t0 + tl, n = n0 + r8;
+      // every split's 8 values requested before any is summed
+      float4 xq[2 * kMaxSplit];
+#pragma unroll
+      for (int q = 0; q < kMaxSplit; ++q) {
+        if (q < split) {
+          const float4* src = reinterpret_cast<const float4*>(part + static_cast<int64_t>(q * TT + tl) * pstride + r8);
+          xq[2 * q] = split > 1 ? __ldcg(src) : src[0];
+          xq[2 * q + 1] = split > 1 ? __ldcg(src + 1) : src[1];
+        }
+      }
       float acc[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] = 0.0f;
-      for (int q = 0; q < split; ++q) {
-        const float4* src = reinterpret_cast<const float4*>(recv + (q * slice + tl) * kPStride + r8);
-        const float4 x0 = src[0], x1 = src[1];
-        acc[0] += x0.x;
-        acc[1] += x0.y;
-        acc[2] += x0.z;
-        acc[3] += x0.w;
-        acc[4] += x1.x;
-        acc[5] += x1.y;
-        acc[6] += x1.z;
-        acc[7] += x1.w;
+#pragma unroll
+      for (int q = 0; q < kMaxSplit; ++q) {
+        if (q < split) {
+          acc[0] += xq[2 * q].x;
+          acc[1] += xq[2 * q].y;
+          acc[2] += xq[2 * q].z;
+          acc[3] += xq[2 * q].w;
+          acc[4] += xq[2 * q + 1].x;
+          acc[5] += xq[2 * q + 1].y;
+          acc[6] += xq[2 * q + 1].z;
+          acc[7] += xq[2 * q + 1].w;
+        }
       }
       if (ok && t < A.T && n < A.N) {
         uint4 w;
@@ -421,11 +434,48 @@ int launch_gemm(const GemmArgs& A, int t_tiles, int* err, const CUtensorMap& xm,
 
 using namespace hca;
 
+namespace hca {
+namespace {
+
+// Token tile, token tiles and split-K factor of one call.
+struct GemmPlan {
+  int tt, t_tiles, n_blocks, split;
+  int64_t ws_bytes;  // split-K workspace (0 without a split)
+};
+
+GemmPlan plan_gemm(int num_tokens, int num_groups, int n, int k) {
+  GemmPlan P{};
+  // token tile: all tokens up to 192 (a multiple of 64), else 192-token tiles
+  P.tt = num_tokens >= 192 ? 192 : ((num_tokens + 63) / 64) * 64;
+  P.t_tiles = (num_tokens + P.tt - 1) / P.tt;
+  P.n_blocks = (n + 127) / 128;
+  const int sms = device_sm_count();
+  // split K over a cluster while the CTAs fit one wave and each keeps at
+  // least two K blocks; at most kMaxKBlocks K blocks per CTA (its scale table)
+  const int64_t base = static_cast<int64_t>(P.n_blocks) * num_groups * P.t_tiles;
+  const int nkb = k / 128;
+  P.split = 1;
+  while (P.split < kMaxSplit && base * P.split * 2 <= sms && nkb >= P.split * 4) P.split *= 2;
+  while (P.split < kMaxSplit && nkb > P.split * kMaxKBlocks) P.split *= 2;
+  P.ws_bytes = P.split > 1 ? base * P.split * P.tt * 128 * static_cast<int64_t>(sizeof(float)) : 0;
+  return P;
+}
+
+}  // namespace
+}  // namespace hca
+
+extern "C" int64_t hca_fp8_grouped_gemm_workspace_bytes(int32_t num_tokens, int32_t num_groups, int32_t n,
+                                                        int32_t k) {
+  if (num_tokens <= 0 || num_groups < 1 || n < 64 || k < 128 || k % 128 || n % 64) return 0;
+  return hca::plan_gemm(num_tokens, num_groups, n, k).ws_bytes;
+}
+
 extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t out_stride_group, const uint8_t* x,
                                     int64_t x_stride_tok, int64_t x_stride_group, const int32_t* x_scale,
                                     int64_t xs_stride_tok, int64_t xs_stride_group, int64_t xs_stride_pack,
                                     int32_t xs_per_int, const uint8_t* w, const float* w_scale, int32_t num_tokens,
-                                    int32_t num_groups, int32_t n, int32_t k, void* stream) {
+                                    int32_t num_groups, int32_t n, int32_t k, void* workspace,
+                                    int64_t workspace_bytes, void* stream) {
   HCA_CHECK_ARG(num_tokens >= 0 && num_groups >= 1 && n >= 1 && k >= 128);
   HCA_CHECK_ARG(xs_per_int == 1 || xs_per_int == 4);
   // N a multiple of 64 and K of 128 (the 128 x 128 weight blocks; N = 64
@@ -436,21 +486,13 @@ extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t o
   HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 &&
                 x_stride_tok % 16 == 0 && x_stride_group % 16 == 0 && x_stride_tok >= k);
   HCA_CHECK_ARG(reinterpret_cast<uintptr_t>(out) % 16 == 0 && out_stride_tok % 8 == 0 && out_stride_group % 8 == 0);
-  // token tile: all tokens up to 192 (a multiple of 64), else 192-token tiles
-  const int tt = num_tokens >= 192 ? 192 : ((num_tokens + 63) / 64) * 64;
-  const int64_t t_tiles = (num_tokens + tt - 1) / tt;
-  const int n_blocks = (n + 127) / 128;
-  HCA_CHECK_ARG(t_tiles * num_groups <= 65535);
-  const int sms = device_sm_count();
-  // split K over a cluster while the CTAs fit one wave and each keeps at
-  // least two K blocks
-  const int64_t base = static_cast<int64_t>(n_blocks) * num_groups * t_tiles;
-  const int nkb = k / 128;
-  int split = 1;
-  while (split < kMaxSplit && base * split * 2 <= sms && nkb >= split * 4) split *= 2;
-  // at most kMaxKBlocks K blocks per CTA (its scale table)
-  while (split < kMaxSplit && nkb > split * kMaxKBlocks) split *= 2;
-  if (nkb > split * kMaxKBlocks) return HCA_E_UNSUPPORTED;
+  const GemmPlan P = plan_gemm(num_tokens, num_groups, n, k);
+  HCA_CHECK_ARG(static_cast<int64_t>(P.t_tiles) * num_groups <= 65535);
+  if (k / 128 > P.split * kMaxKBlocks) return HCA_E_UNSUPPORTED;
+  if (P.ws_bytes > 0) {
+    if (!workspace || reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return HCA_E_INVALID;
+    if (workspace_bytes < P.ws_bytes) return HCA_E_WORKSPACE;
+  }
   GemmArgs A{};
   A.out = static_cast<__nv_bfloat16*>(out);
   A.out_st = out_stride_tok;
@@ -465,23 +507,23 @@ extern "C" int hca_fp8_grouped_gemm(void* out, int64_t out_stride_tok, int64_t o
   A.G = num_groups;
   A.N = n;
   A.K = k;
-  A.n_blocks = n_blocks;
-  A.split = split;
+  A.n_blocks = P.n_blocks;
+  A.split = P.split;
+  A.ws_part = static_cast<float*>(workspace);
   A.wait_ns = tc::kWaitLimitNs;
   CUtensorMap xm, wm;
   // x [G][T][K] bytes (token stride x_stride_tok, group stride
   // x_stride_group); w [G][N][K] contiguous
   const uint64_t gstride = num_groups > 1 ? static_cast<uint64_t>(x_stride_group)
                                           : static_cast<uint64_t>(x_stride_tok) * num_tokens;
-  if (!encode_u8_3d(&xm, x, k, num_tokens, num_groups, x_stride_tok, gstride, static_cast<uint32_t>(tt)) ||
+  if (!encode_u8_3d(&xm, x, k, num_tokens, num_groups, x_stride_tok, gstride, static_cast<uint32_t>(P.tt)) ||
       !encode_u8_3d(&wm, w, k, n, num_groups, k, static_cast<uint64_t>(n) * k, 128))
     return HCA_E_UNSUPPORTED;
   int* err = device_error_word();
   cudaStream_t s = as_stream(stream);
-  const int tl = static_cast<int>(t_tiles);
-  switch (tt) {
-    case 64: return launch_gemm<64>(A, tl, err, xm, wm, s);
-    case 128: return launch_gemm<128>(A, tl, err, xm, wm, s);
-    default: return launch_gemm<192>(A, tl, err, xm, wm, s);
+  switch (P.tt) {
+    case 64: return launch_gemm<64>(A, P.t_tiles, err, xm, wm, s);
+    case 128: return launch_gemm<128>(A, P.t_tiles, err, xm, wm, s);
+    default: return launch_gemm<192>(A, P.t_tiles, err, xm, wm, s);
   }
 }

@@ -474,7 +474,12 @@ def sigmoid_mul_quant_fp8(x, gate):
 
 
 
-def fp8_grouped_gemm(x, x_scale, w, w_scale, out=None):
+# split-K partial tiles of the FP8 GEMM (one buffer per device; calls are
+# ordered on the current stream)
+_GEMM_WS = DecodeWorkspace()
+
+
+def fp8_grouped_gemm(x, x_scale, w, w_scale, out=None, workspace: DecodeWorkspace | None = None):
     """Block-scaled FP8 GEMM of the output path: the grouped ``wo_a`` einsum
     ``"bhr,hdr->bhd"`` (``V/models/deepseek_v4/attention.py:317-347``) for a
     3-D ``x [T, G, K]`` and ``w [G, N, K]``, or the gated ``wo_b`` linear
@@ -501,9 +506,11 @@ def fp8_grouped_gemm(x, x_scale, w, w_scale, out=None):
         out = out.unsqueeze(1)
     assert out.shape == (t, g, n) and out.dtype == torch.bfloat16 and out.stride(2) == 1
     if t:
+        nbytes = lib().hca_fp8_grouped_gemm_workspace_bytes(t, g, n, k)
+        ws = (workspace or _GEMM_WS).get(nbytes, x.device) if nbytes > 0 else None
         call("hca_fp8_grouped_gemm", _p(out), out.stride(0), out.stride(1) if g > 1 else 0, _p(x), x.stride(0),
              x.stride(1) if g > 1 else 0, _p(x_scale), x_scale.stride(0), x_scale.stride(1) if g > 1 else 0,
-             x_scale.stride(2), per_int, _p(w), _p(w_scale), t, g, n, k, _s())
+             x_scale.stride(2), per_int, _p(w), _p(w_scale), t, g, n, k, _p(ws), nbytes, _s())
     return out.squeeze(1) if flat else out
 
 
