@@ -461,20 +461,23 @@ __device__ __forceinline__ void vha_merge_token(const AttnParams& P, int t, int 
   const int lane = threadIdx.x & 31;
   (void)lane;
   const int64_t row0 = static_cast<int64_t>(first) * P.max_rows + static_cast<int64_t>(t - t0) * H;
-  const int64_t o_step = static_cast<int64_t>(P.max_rows) * D / 4;  // float4s between splits
   const int nitems = H * 8;
-  // the first pair of splits of this thread's first item
-  float4 v[2][4];
-  {
-    const int it = threadIdx.x;
+  // the partials are bf16 (the fused path's attention launch writes them
+  // so): four splits' 16 dims (2 x 16 bytes each) in flight per round
+  const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(P.ws_o);
+  const int64_t b_step = static_cast<int64_t>(P.max_rows) * D / 8;  // uint4s between splits
+  uint4 vb[4][2];
+  auto load_round = [&](int it, int sp) {
     const int h = it >> 3, seg = it & 7;
-    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
+    const uint4* bp = reinterpret_cast<const uint4*>(ob + (row0 + h) * D + seg * 16);
 #pragma unroll
-    for (int k = 0; k < 2; ++k)
+    for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        v[k][q] = (it < nitems && k < S) ? __ldcg(op + k * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+      for (int q = 0; q < 2; ++q)
+        vb[k][q] = (it < nitems && sp + k < S) ? __ldcg(bp + (sp + k) * b_step + q) : make_uint4(0, 0, 0, 0);
+  };
+  // the first round of splits of this thread's first item
+  load_round(threadIdx.x, 0);
   // split weights: thread (head, split) pairs, two per thread in flight;
   // H * kMaxSplits is a multiple of 256, so validity is uniform per warp
   for (int base = 0; base < H * kMaxSplits; base += 2 * blockDim.x) {
@@ -512,27 +515,23 @@ __device__ __forceinline__ void vha_merge_token(const AttnParams& P, int t, int 
   __syncthreads();
   for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
     const int h = it >> 3, seg = it & 7;
-    const float4* op = reinterpret_cast<const float4*>(P.ws_o + (row0 + h) * D + seg * 16);
     float acc[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) acc[e] = 0.0f;
-    for (int sp = 0; sp < S; sp += 2) {
-      if (sp > 0 || it != threadIdx.x) {
+    for (int sp = 0; sp < S; sp += 4) {
+      if (sp > 0 || it != threadIdx.x) load_round(it, sp);
 #pragma unroll
-        for (int k = 0; k < 2; ++k)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            v[k][q] = sp + k < S ? __ldcg(op + (sp + k) * o_step + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
+      for (int k = 0; k < 4; ++k) {
         const float wt = sp + k < S ? sm.w[h][sp + k] : 0.0f;
+        if (wt == 0.0f) continue;  // an empty split's row was never written
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[4 * q] += wt != 0.0f ? wt * v[k][q].x : 0.0f;
-          acc[4 * q + 1] += wt != 0.0f ? wt * v[k][q].y : 0.0f;
-          acc[4 * q + 2] += wt != 0.0f ? wt * v[k][q].z : 0.0f;
-          acc[4 * q + 3] += wt != 0.0f ? wt * v[k][q].w : 0.0f;
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t w4[4] = {vb[k][q].x, vb[k][q].y, vb[k][q].z, vb[k][q].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[8 * q + 2 * e] += wt * __uint_as_float(w4[e] << 16);
+            acc[8 * q + 2 * e + 1] += wt * __uint_as_float(w4[e] & 0xffff0000u);
+          }
         }
       }
     }
@@ -1258,7 +1257,13 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
           const int aidx = (warp >> 2) == 0 ? (warp & 3) : act0 + (warp & 3);  // index among active warps
           for (int row = aidx; row < rows_q; row += nact) {
             const float4 v = *reinterpret_cast<const float4*>(stage + row * kD + ((lane ^ (row & 7)) << 2));
-            reinterpret_cast<float4*>(P.ws_o + (item * P.max_rows + row) * kD)[lane] = v;
+            if (P.bf16_partials) {
+              // bf16 rows, 256 bytes: lane's 4 dims as 8 bytes
+              reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.ws_o) + (item * P.max_rows + row) * kD)[lane] =
+                  make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+            } else {
+              reinterpret_cast<float4*>(P.ws_o + (item * P.max_rows + row) * kD)[lane] = v;
+            }
           }
         }
       }
@@ -1385,7 +1390,8 @@ __global__ void __launch_bounds__(kSchedThreads) hca_decode_schedule_kernel(
 // Fused split-K merge + VHA head mix + inverse RoPE + FP8 quant (decode).
 // One CTA (512 threads) per token, padded to a multiple of 4 tokens.
 //   merge: thread (head h = tid / 8, 16-dim segment tid % 8) sums the
-//          group's partials weighted by 2^(m_s - m), applies the sink and
+//          group's bf16 partials (all of up to four splits' loads in flight
+//          at once) weighted by 2^(m_s - m), applies the sink and
 //          rounds O to bf16 in shared memory (the combine kernel's math);
 //   mix:   warp w < 8: heads 16 (w % 4) .. +15, dims 64 (w / 4) .. +63 of
 //          y = mix @ O (mma.sync m16n8k16 bf16, fp32 accumulate);
@@ -1615,6 +1621,7 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   P.sched = schedule;
   P.sched_items = schedule ? max_items : 0;
   P.force_partials = fused;
+  P.bf16_partials = fused && !wide;  // read only by the fused merge + VHA kernel
   P.wait_ns = attention_wait_ns();
   // partial slots: groups x splits, or one per work-list item
   const int32_t slot_groups = schedule ? 1 : num_groups;

@@ -65,6 +65,9 @@ struct AttnParams {
   // every CTA writes its partial, even a group's only CTA (the merge happens
   // in the fused combine + VHA kernel)
   int force_partials;
+  // the partial O rows are bf16 (the fused merge + VHA path): half the bytes,
+  // every split of a token in flight at once in the merge
+  int bf16_partials;
   // limit of every mbarrier wait of the head_dim-128 kernel (0: probe once)
   uint64_t wait_ns;
 };
