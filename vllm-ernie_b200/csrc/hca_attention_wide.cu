@@ -17,11 +17,13 @@
 //   - O_h += P V_h runs on each CTA's own half (V = K, M128 N256).
 // Warp roles per CTA: warps 0-3 softmax (one thread per query row), warp 4
 // MMA issuer + TMEM owner, warps 5-8 gather + dequant producers, 16 rows of
-// every 64-row chunk each.  Exchanges are paced by mbarriers that the peer
-// arrives on remotely (x_full: its partial landed here; x_empty: it has read
-// the partial this CTA wrote there).  Every wait is bounded (device error
-// word); both CTAs meet at a cluster barrier before exit, so neither leaves
-// while the other may still write its shared memory.
+// every 64-row chunk each.  Exchanges are paced by two mbarriers per CTA:
+// x_full counts the bytes of the peer's partial landing here (the peer writes
+// it with st.async, complete_tx on this barrier; warp 0 arms each phase with
+// the expected byte count), x_empty takes one remote arrival per peer softmax
+// warp once it has read the partial this CTA wrote there.  Every wait is
+// bounded (device error word); both CTAs meet at a cluster barrier before
+// exit, so neither leaves while the other may still write its shared memory.
 //
 // Work: decode -- split s of tile k of group g, a tile being up to 128 / H
 // consecutive tokens of the group (their union of rows, per-token masks);
@@ -192,8 +194,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
       mbar_init(pv_done + b, 1);
     }
     mbar_init(q_full, kQWarps * 32 + kQWarps);
-    mbar_init(x_full, nact * 32);   // the peer's softmax threads with rows
-    mbar_init(x_empty, nact * 32);
+    mbar_init(x_full, 1);      // this CTA's arming arrival; the peer's bytes as tx
+    mbar_init(x_empty, nact);  // one arrival per peer softmax warp with rows
     misc[1] = 0;
     mbar_fence_init();
   }
@@ -462,14 +464,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
       tmem_ld32(s_addr + 32, sr + 32);
       tmem_wait_ld();
       // ---- exchange the partial S with the peer and add its partial ----
+      // Arm this chunk's phase of x_full with the bytes the peer's softmax
+      // threads will store.  Phase i - 1 completed before (this thread waited
+      // on it), and phase i cannot complete before every warp here has read
+      // chunk i - 1: the peer sends chunk i only after all of them arrived
+      // on its x_empty.
+      if (warp == 0 && lane == 0) mbar_arrive_expect_tx(x_full, static_cast<uint32_t>(nact * 32 * kCh * 4));
       if (i > 0 && !mbar_wait_cluster(x_empty, (i - 1) & 1)) {
         ok = false;
         break;
       }
 #pragma unroll
       for (int c4 = 0; c4 < kCh / 4; ++c4)
-        st_cluster_v4(x_remote + c4 * 128 * 16, sr[4 * c4], sr[4 * c4 + 1], sr[4 * c4 + 2], sr[4 * c4 + 3]);
-      mbar_arrive_cluster(x_full_remote);
+        st_async_v4(x_remote + c4 * 128 * 16, sr[4 * c4], sr[4 * c4 + 1], sr[4 * c4 + 2], sr[4 * c4 + 3],
+                    x_full_remote);
       if (!mbar_wait_cluster(x_full, i & 1)) {
         ok = false;
         break;
@@ -482,7 +490,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tcw::kThreads, 1)
         sr[4 * c4 + 2] = __float_as_uint(__uint_as_float(sr[4 * c4 + 2]) + v.z);
         sr[4 * c4 + 3] = __float_as_uint(__uint_as_float(sr[4 * c4 + 3]) + v.w);
       }
-      mbar_arrive_cluster(x_empty_remote);
+      // the warp's reads of the buffer are done: one release arrival frees it
+      // for the peer's next chunk
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(x_empty_remote);
       // ---- softmax (base 2, lazily raised max) ----
       if (!full) {
 #pragma unroll

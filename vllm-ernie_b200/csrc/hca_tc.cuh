@@ -123,6 +123,18 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_
                : "memory");
 }
 
+// Asynchronous 16-byte store into a cluster CTA's shared memory that counts
+// its bytes on an mbarrier of that CTA (complete_tx); both addresses from
+// mapa_shared.  The receiver sees the data once it observes the barrier's
+// phase complete (no release fence on this side).
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(
+                   addr),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
+               : "memory");
+}
+
 // Arrive on a cluster CTA's mbarrier (address from mapa_shared), releasing
 // this thread's earlier shared-memory accesses at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
