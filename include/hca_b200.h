@@ -219,8 +219,9 @@ int hca_decode_prep(void* q_out, int64_t q_out_stride_tok, int64_t q_out_stride_
 /* ---------------------------------------------------------------------- */
 
 /* Workspace bytes hca_sparse_decode needs for these sizes (0 if
- * num_splits == 1): fp32 split-K partials, written by the attention kernel
- * and merged by a second launch on the same stream.  Calls that share one
+ * num_splits == 1): split-K partials (bf16 rows at head_dim 128, fp32 at
+ * 512, each with an fp32 running max and sum), written by the attention
+ * kernel and merged by a second launch on the same stream.  Calls that share one
  * workspace must be ordered on one stream. */
 int64_t hca_sparse_decode_workspace_bytes(int32_t num_groups, int32_t max_group_tokens,
                                           int32_t num_heads, int32_t head_dim,

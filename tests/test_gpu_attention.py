@@ -290,11 +290,11 @@ def _dequant(data, scale):
 def test_decode_fused_vha_quant_matches_unfused():
     """Scheduled attention fused with the VHA mix + inverse RoPE + FP8 quant
     equals attention followed by hca_vha_inv_rope_fp8_quant up to roundings:
-    the fused path keeps the split partials in bf16 (one more bf16 rounding
-    of O), so >= 95% of the e4m3 bytes agree, each element is within one
-    e4m3 step or 2 units of its head's scale (near-zero elements where the
-    splits cancel), and the dequantised outputs are within relative L2
-    2e-2."""
+    both read the same bf16 split partials, but the fused merge adds them in
+    another order and mixes in another kernel, so >= 95% of the e4m3 bytes
+    agree, each element is within one e4m3 step or 2 units of its head's
+    scale (near-zero elements where the splits cancel), and the dequantised
+    outputs are within relative L2 2e-2."""
     from vllm_ernie_b200 import ops
     from vllm_ernie_b200.decode import build_decode_metadata, random_layer_weights
     from vllm_ernie_b200.synthetic import HCADims, alloc_layer_caches, make_decode_batch, rope_cos_sin_cache

@@ -394,9 +394,20 @@ __global__ void __launch_bounds__(256) hca_attention_combine_kernel(const AttnPa
 #pragma unroll 4
     for (int sp = 0; sp < S; ++sp) {
       const float w = w_s[rr][sp];
-      const float4* src = reinterpret_cast<const float4*>(
-          P.ws_o + (gbase + static_cast<int64_t>(sp) * P.max_rows + r) * D + seg * 8);
-      const float4 a = __ldcg(src), b = __ldcg(src + 1);
+      const int64_t e0 = (gbase + static_cast<int64_t>(sp) * P.max_rows + r) * D + seg * 8;
+      float4 a, b;
+      if (P.bf16_partials) {
+        // bf16 partial rows: the 8 dims in one 16-byte load
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(P.ws_o) + e0));
+        a = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                        __uint_as_float(u.y & 0xffff0000u));
+        b = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u), __uint_as_float(u.w << 16),
+                        __uint_as_float(u.w & 0xffff0000u));
+      } else {
+        const float4* src = reinterpret_cast<const float4*>(P.ws_o + e0);
+        a = __ldcg(src);
+        b = __ldcg(src + 1);
+      }
       if (w != 0.0f) {
         acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
         acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
@@ -1621,7 +1632,9 @@ static int sparse_decode_impl(void* out, int64_t out_stride_tok, int64_t out_str
   P.sched = schedule;
   P.sched_items = schedule ? max_items : 0;
   P.force_partials = fused;
-  P.bf16_partials = fused && !wide;  // read only by the fused merge + VHA kernel
+  // D=128 split partials are bf16 rows (half the bytes through L2 for the
+  // attention's epilogue and the merge); the D=512 pair kernel writes fp32
+  P.bf16_partials = !wide;
   P.wait_ns = attention_wait_ns();
   // partial slots: groups x splits, or one per work-list item
   const int32_t slot_groups = schedule ? 1 : num_groups;
