@@ -3,7 +3,8 @@ backend's metadata builders and the forward context, against the whole-layer
 CPU oracle (config 1: hidden 2048, 16 heads x 128, and the same with the
 model's head_dim 512; prefill of 1024 and 640 tokens from an empty cache, then
 an ECHO/MTP decode step of 3 tokens per request on the caches the prefill
-wrote).
+wrote, a verify step after partial acceptance that writes the rejected
+drafts' positions again, and a one-token step).
 
 Tolerance of the block-FP8 output path: relative L2 and max |err| / max
 |ref| <= 6e-2.  Its two 1x128 e4m3 quant points (wo_a's and wo_b's inputs)
@@ -130,6 +131,11 @@ def test_module_forward_prefill_then_decode_matches_layer_oracle(head_dim, fp8, 
     steps = [  # (query_start_loc, seq_lens, speculative tokens)
         (np.array([0, 1024, 1664]), np.array([1024, 640]), 0),   # prefill from an empty cache
         (np.array([0, 3, 6]), np.array([1027, 643]), 2),         # decode, 3 tokens per request
+        # ECHO/MTP verify after partial acceptance: request 0 kept 2 of its 3
+        # tokens, request 1 kept 1, so the rejected drafts' positions (1026;
+        # 641, 642) are written again with new values beside the next ones
+        (np.array([0, 3, 6]), np.array([1029, 644]), 2),
+        (np.array([0, 1, 2]), np.array([1030, 645]), 2),         # one token per request (a draft step)
     ]
     for qsl, seq_lens, spec in steps:
         n = int(qsl[-1])
