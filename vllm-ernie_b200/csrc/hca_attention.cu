@@ -669,7 +669,11 @@ constexpr int kD = 128;
 constexpr int kNope = 64;
 constexpr int kRowBytes = 192;  // kNope e4m3 + 64 bf16
 constexpr int kCh = 64;         // KV rows per step
-constexpr int kStages = 4;
+// raw gather ring: one chunk in flight while the previous one is dequantised.
+// Deeper rings start every CTA with a larger burst of gathers (all CTAs
+// reach their first chunk at once), which delays the first chunk more than
+// the extra prefetch helps: a chunk's MMAs and softmax outlast its gather.
+constexpr int kStages = 2;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kMmaWarp = 8;
 constexpr int kProdWarp0 = 9;
