@@ -972,9 +972,20 @@ __global__ void __launch_bounds__(tcd::kThreads, 1) hca_tc_attention_kernel(cons
     if (kStages - 1 < n) resolve(c_begin + kStages - 1, rn);
     for (int i = 0; i < n; ++i) {
       const int s = i % kStages, b = i % kKBufs;
-      issue(i + kStages - 1, rn);
-      if (i + kStages < n) resolve(c_begin + i + kStages, rn);
-      cp_async_wait_group<kStages - 1>();  // chunk i's group has landed
+      if (kPrefill && i == 0) {
+        // prefill: chunk 0 lands before the next gathers go out (a tile's
+        // CTA requests its Q tile and first rows at once, and the first S
+        // needs only those: 3.50 -> 3.44 ms a config-3 layer).  Decode keeps
+        // chunk 1 in flight: in the decode chain the delay cost more (33.7
+        // -> 34.1 us a layer) than the smaller start-up burst saved.
+        cp_async_wait_group<0>();
+        issue(kStages - 1, rn);
+        if (kStages < n) resolve(c_begin + kStages, rn);
+      } else {
+        issue(i + kStages - 1, rn);
+        if (i + kStages < n) resolve(c_begin + i + kStages, rn);
+        cp_async_wait_group<kStages - 1>();  // chunk i's group has landed
+      }
       __syncwarp();
       if (i >= kKBufs && !mbar_wait(k_empty + b, ((i / kKBufs) - 1) & 1, wait_ns)) {
         report(err, misc + 1, 2);
