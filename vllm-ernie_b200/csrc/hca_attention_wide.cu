@@ -43,7 +43,7 @@ constexpr int kHalf = 256;          // head dims per CTA of the pair
 constexpr int kRowBytes = 576;      // 448 e4m3 + 64 bf16
 constexpr int kScaleBytes = 8;      // 7 UE8M0 bytes + pad
 constexpr int kCh = 64;             // KV rows per chunk
-constexpr int kStages = 3;          // raw ring: two chunks in flight
+constexpr int kStages = 2;          // raw ring: one chunk in flight
 constexpr int kKBufs = 2;           // bf16 K-tile ring
 constexpr int kSoftmaxWarps = 4;
 constexpr int kMmaWarp = 4;
